@@ -1,0 +1,74 @@
+// Internal declarations shared by the libflashgmm_sm100 translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include <string>
+
+namespace fgmm {
+
+constexpr double kLog2Pi = 1.8378770664093453;  // log(2 pi)
+constexpr double kLog2E = 1.4426950408889634;   // 1 / ln 2
+
+enum Variant { kIso = 0, kDiag = 1, kFull = 2 };
+
+// Arguments of one E-step call, as received through the C ABI.
+struct EstepArgs {
+  const float* X;
+  int64_t sxn, sxd;
+  const float* mu;
+  int64_t smk, smd;
+  const float* cov;  // iso: log_sigma_sq (K); diag: log_sigma_sq (K,D);
+                     // full: prec_chol (K,D,D)
+  const float* lpi;
+  int64_t N;
+  int K, D;
+  float* logZ;
+  float* Nk;
+  float* mu_acc;
+  float* sig;
+  void* ws;
+  size_t ws_bytes;
+  unsigned flags;
+  cudaStream_t stream;
+};
+
+// Bump allocator over the caller's workspace; every block 256-byte aligned.
+struct WsCarve {
+  char* base;
+  size_t used = 0;
+  explicit WsCarve(void* p) : base(static_cast<char*>(p)) {}
+  template <typename T>
+  T* take(size_t count) {
+    size_t off = (used + 255) & ~size_t(255);
+    used = off + count * sizeof(T);
+    return base ? reinterpret_cast<T*>(base + off) : nullptr;
+  }
+};
+
+// General (CUDA-core) kernels: any strides, any K, D <= kGeneralMaxD.
+constexpr int kGeneralMaxD = 256;
+constexpr int kGeneralMaxDFull = 128;
+size_t general_workspace_bytes(int variant, int64_t N, int K, int D);
+cudaError_t general_estep(int variant, const EstepArgs& a);
+
+// Tensor-core (tcgen05) isotropic / diagonal path.
+bool tc_supported(int variant, const EstepArgs& a, std::string* why);
+size_t tc_workspace_bytes(int variant, int64_t N, int K, int D);
+cudaError_t tc_estep(int variant, const EstepArgs& a);
+
+// Row generator for the streaming configuration.
+cudaError_t generate_iso_rows(float* X, const int64_t* row_ids, int64_t row0,
+                              int64_t nrows, int D, const float* centres, int K,
+                              uint64_t seed, cudaStream_t stream);
+
+int num_sms();
+
+// Launch accounting and the optional profiling events around the dominant
+// kernel (see fgmm_launch_count / fgmm_set_profile_events).
+void count_launches(int n);
+void profile_mark(bool stop, cudaStream_t stream);
+
+}  // namespace fgmm

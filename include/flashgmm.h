@@ -1,0 +1,140 @@
+/*
+ * flashgmm.h -- C ABI of the B200 (sm_100a) Gaussian-mixture E-step library
+ * libflashgmm_sm100.so.
+ *
+ * One entry point per covariance family.  Each replaces, as one call, the
+ * host wrapper + two Triton launches of the reference:
+ *
+ *   fgmm_estep_iso   <- flash_gmm.py:173-217        (flash_gmm_estep, fp32)
+ *                       flash_gmm_h100.py:254-328   (flash_gmm_estep, H100)
+ *   fgmm_estep_diag  <- flash_gmm_diag_h100.py:305-384 (flash_gmm_estep_diag)
+ *   fgmm_estep_full  <- flash_gmm_full_h100.py:235-336 (flash_gmm_estep_full)
+ *
+ * Conventions (all entry points):
+ *  - Every array argument is a DEVICE pointer owned by the caller.  float32.
+ *  - X is (N, D) with element strides (x_stride_n, x_stride_d), as the
+ *    reference passes X.stride() through (flash_gmm.py:202).  mu is (K, D)
+ *    with strides (mu_stride_k, mu_stride_d).  All other inputs are
+ *    contiguous: log_sigma_sq (K) iso / (K, D) diag, prec_chol (K, D, D),
+ *    log_pi (K).
+ *  - Outputs are contiguous and fully written by the call (no pre-zeroing):
+ *      logZ (N)       natural-log per-sample normaliser
+ *      Nk (K)         sum_n r_nk
+ *      mu_acc (K, D)  sum_n r_nk x_n
+ *      sig            iso : (K)      sum_n r_nk ||x_n - mu_k||^2
+ *                     diag: (K, D)   sum_n r_nk (x_nd - mu_kd)^2
+ *                     full: (K,D,D)  sum_n r_nk x_n x_n^T (uncentred)
+ *    With FGMM_FLAG_ACCUMULATE the Nk/mu_acc/sig results are ADDED to the
+ *    values already in those buffers (logZ is still overwritten); this is the
+ *    chunk-summing step of the reference's streaming recipe (README.md:81-103).
+ *  - workspace: device scratch of at least fgmm_workspace_bytes(...) bytes,
+ *    256-byte aligned.  It holds per-CTA partial statistics, which a second
+ *    kernel reduces in a fixed order: results are bitwise reproducible
+ *    run-to-run (the reference's tl.atomic_add accumulation is not).
+ *  - stream: a cudaStream_t passed as void*; NULL = legacy default stream.
+ *    The call is asynchronous on that stream and never synchronises.
+ *  - Return value: FGMM_OK (0) or one of the FGMM_ERR_* codes; no C++
+ *    exception crosses the ABI.  fgmm_last_error() gives a message for the
+ *    last failing call on the calling thread.
+ */
+#ifndef FLASHGMM_H_
+#define FLASHGMM_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define FGMM_API __attribute__((visibility("default")))
+#else
+#define FGMM_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FGMM_OK 0
+#define FGMM_ERR_ARG 1          /* bad shape, stride or null pointer      */
+#define FGMM_ERR_WORKSPACE 2    /* workspace missing, small or unaligned   */
+#define FGMM_ERR_UNSUPPORTED 3  /* shape outside what any kernel handles   */
+#define FGMM_ERR_CUDA 4         /* CUDA launch / runtime error             */
+#define FGMM_ERR_DEVICE 5       /* device is not sm_100                    */
+
+#define FGMM_VARIANT_ISO 0
+#define FGMM_VARIANT_DIAG 1
+#define FGMM_VARIANT_FULL 2
+
+#define FGMM_FLAG_ACCUMULATE 1u /* add Nk/mu_acc/sig into the outputs      */
+#define FGMM_FLAG_FORCE_GENERAL 2u /* use the general (non-tensor-core)
+                                      kernels even when the fast path applies */
+
+/* Library version, major*10000 + minor*100 + patch. */
+FGMM_API int fgmm_version(void);
+
+/* Message describing the last failed call on this thread ("" if none). */
+FGMM_API const char* fgmm_last_error(void);
+
+/* Bytes of device workspace the entry point for `variant` needs at this
+ * shape (0 is a valid answer).  Replaces the reference's internal torch
+ * allocations of padded copies and accumulators (e.g. flash_gmm_h100.py:
+ * 277-298).  Pure host function: touches no device state. */
+FGMM_API size_t fgmm_workspace_bytes(int variant, int64_t N, int32_t K, int32_t D);
+
+/* Isotropic E-step.  Replaces flash_gmm.py:173-217 and
+ * flash_gmm_h100.py:254-328. */
+FGMM_API int fgmm_estep_iso(const float* X, int64_t x_stride_n, int64_t x_stride_d,
+                   const float* mu, int64_t mu_stride_k, int64_t mu_stride_d,
+                   const float* log_sigma_sq, const float* log_pi,
+                   int64_t N, int32_t K, int32_t D,
+                   float* logZ, float* Nk, float* mu_acc, float* sig_acc,
+                   void* workspace, size_t workspace_bytes,
+                   unsigned flags, void* stream);
+
+/* Diagonal-covariance E-step; log_sigma_sq is (K, D).  Replaces
+ * flash_gmm_diag_h100.py:305-384 (without its pass-2 slab overlap). */
+FGMM_API int fgmm_estep_diag(const float* X, int64_t x_stride_n, int64_t x_stride_d,
+                    const float* mu, int64_t mu_stride_k, int64_t mu_stride_d,
+                    const float* log_sigma_sq, const float* log_pi,
+                    int64_t N, int32_t K, int32_t D,
+                    float* logZ, float* Nk, float* mu_acc, float* sig_acc,
+                    void* workspace, size_t workspace_bytes,
+                    unsigned flags, void* stream);
+
+/* Full-covariance E-step; prec_chol is (K, D, D) with
+ * prec_chol[k] @ prec_chol[k]^T = Sigma_k^-1.  Replaces
+ * flash_gmm_full_h100.py:235-336. */
+FGMM_API int fgmm_estep_full(const float* X, int64_t x_stride_n, int64_t x_stride_d,
+                    const float* mu, int64_t mu_stride_k, int64_t mu_stride_d,
+                    const float* prec_chol, const float* log_pi,
+                    int64_t N, int32_t K, int32_t D,
+                    float* logZ, float* Nk, float* mu_acc, float* sig_outer,
+                    void* workspace, size_t workspace_bytes,
+                    unsigned flags, void* stream);
+
+/* Number of kernels this library has launched in this process (all devices,
+ * all threads).  Lets a caller count the launches inside a timed region. */
+FGMM_API uint64_t fgmm_launch_count(void);
+
+/* Register two cudaEvent_t (passed as void*) that subsequent E-step calls on
+ * this thread record on their stream immediately before and after the
+ * dominant (tensor-core or pass-2) kernel; NULL, NULL disables.  Used by the
+ * benchmark to time that kernel alone with CUDA events. */
+FGMM_API void fgmm_set_profile_events(void* start_event, void* stop_event);
+
+/* Fill rows of the isotropic mixture used by the streaming configuration:
+ * x_n = centres[c(n)] + z_n, z_n ~ N(0, I), with c(n) uniform over K and
+ * every value a pure function of (seed, n, d) -- the same global row n gets
+ * the same values whatever the sharding.  Output row i is global row
+ * row_ids[i] when row_ids (device, int64) is non-NULL, else row0 + i.
+ * X is (nrows, D) contiguous; centres is (K, D) contiguous.  This is the
+ * on-device stand-in for the reference's host->device chunk loop
+ * (README.md:81-103); it has no counterpart kernel in the reference. */
+FGMM_API int fgmm_generate_iso_rows(float* X, const int64_t* row_ids, int64_t row0,
+                           int64_t nrows, int32_t D, const float* centres,
+                           int32_t K, uint64_t seed, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FLASHGMM_H_ */

@@ -1,0 +1,214 @@
+"""CPU oracle for the Gaussian-mixture E-step -- TEST INFRASTRUCTURE ONLY.
+
+This module restates, in plain numpy (float64 by default), the arithmetic of
+the four reference Flash-GMM entry points.  It is the checker the parity tests,
+``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline leg compare the
+CUDA path against.  Nothing in the product package imports it; the product path
+fails loudly when its CUDA library is missing instead of falling back here.
+
+Pinning: the isotropic fp32 restatement is pinned against golden vectors that
+``tests/golden/make_golden.py`` produced by running the reference's own Triton
+kernels (flash_gmm.py:50-103, 110-166) under ``TRITON_INTERPRET=1``; the
+diagonal and full-covariance restatements are pinned against fp32-substituted
+runs of the reference kernels (flash_gmm_diag_h100.py:63-130, 159-282 and
+flash_gmm_full_h100.py:71-139, 146-228) made by the same script.  The
+reference ships no golden vectors or tests of its own.
+
+All functions return ``(logZ, Nk, mu_acc, sig)`` with the reference's shapes
+and natural-log ``logZ`` (flash_gmm_h100.py:326, diag:382, full:335).
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+
+LOG_2PI = math.log(2.0 * math.pi)   # flash_gmm.py:91 (1.8378770664093453)
+LOG2_E = 1.0 / math.log(2.0)        # flash_gmm_h100.py:251
+
+
+def _lse_rows(ll: np.ndarray) -> np.ndarray:
+    """Row-wise log-sum-exp with the max shift (flash_gmm.py:95-102)."""
+    m = np.max(ll, axis=1)
+    m_safe = np.where(np.isfinite(m), m, 0.0)
+    s = np.sum(np.exp(ll - m_safe[:, None]), axis=1)
+    with np.errstate(divide="ignore"):
+        return m_safe + np.log(s)
+
+
+def _responsibilities(ll: np.ndarray):
+    logZ = _lse_rows(ll)
+    r = np.exp(ll - logZ[:, None])           # flash_gmm.py:151
+    r = np.where(np.isfinite(ll), r, 0.0)   # flash_gmm.py:152 masks to 0
+    return logZ, r
+
+
+def loglik_iso(X, mu, log_sigma_sq, log_pi):
+    """ll[n,k] and sq[n,k] of the isotropic model (flash_gmm.py:84-93).
+
+    ll = log_pi_k - 0.5*||x_n - mu_k||^2 * exp(-lss_k) - 0.5*D*(log 2pi + lss_k).
+    ``sq`` is formed as x_sq - 2 x.mu + mu_sq exactly as the reference
+    expands it (flash_gmm.py:85-88); in float64 the expansion is exact enough.
+    """
+    X = np.asarray(X, dtype=np.float64)
+    mu = np.asarray(mu, dtype=np.float64)
+    lss = np.asarray(log_sigma_sq, dtype=np.float64)
+    lpi = np.asarray(log_pi, dtype=np.float64)
+    D = X.shape[1]
+    x_sq = np.sum(X * X, axis=1)
+    mu_sq = np.sum(mu * mu, axis=1)
+    sq = x_sq[:, None] - 2.0 * (X @ mu.T) + mu_sq[None, :]
+    ll = lpi[None, :] - 0.5 * sq * np.exp(-lss)[None, :] \
+        - 0.5 * D * (LOG_2PI + lss[None, :])
+    return ll, sq
+
+
+def estep_iso(X, mu, log_sigma_sq, log_pi, chunk: int = 65536):
+    """Isotropic E-step (flash_gmm.py:173-217; same maths as
+    flash_gmm_h100.py:254-328, whose log2-space folding at 286-291 and
+    137-138 is an algebraic rewrite of the same ll).
+
+    Returns logZ (N,), Nk (K,), mu_acc (K,D) = R^T X (flash_gmm.py:161),
+    sig_acc (K,) = sum_n r_nk ||x_n - mu_k||^2 (flash_gmm.py:156).
+    """
+    X = np.asarray(X, dtype=np.float64)
+    N, D = X.shape
+    K = np.asarray(mu).shape[0]
+    logZ = np.empty(N)
+    Nk = np.zeros(K)
+    mu_acc = np.zeros((K, D))
+    sig = np.zeros(K)
+    for s in range(0, N, chunk):
+        xs = X[s:s + chunk]
+        ll, sq = loglik_iso(xs, mu, log_sigma_sq, log_pi)
+        lz, r = _responsibilities(ll)
+        logZ[s:s + chunk] = lz
+        Nk += r.sum(axis=0)
+        mu_acc += r.T @ xs
+        sig += (r * sq).sum(axis=0)
+    return logZ, Nk, mu_acc, sig
+
+
+def loglik_diag(X, mu, log_sigma_sq, log_pi):
+    """ll[n,k] of the diagonal model, restating flash_gmm_diag_h100.py:332-339
+    (c0 with the log-det and mu^2/sigma^2 terms) and 116-119
+    (ll2 = c0 - x^2 . inv^T + 2 x . (mu*inv)^T), converted back to natural-log
+    units: ll = log_pi - 0.5*(D log 2pi + sum_d lss) - 0.5 sum_d (x-mu)^2 e^-lss.
+    """
+    X = np.asarray(X, dtype=np.float64)
+    mu = np.asarray(mu, dtype=np.float64)
+    lss = np.asarray(log_sigma_sq, dtype=np.float64)
+    lpi = np.asarray(log_pi, dtype=np.float64)
+    D = X.shape[1]
+    inv = np.exp(-lss)                                          # (K, D)
+    quad = (X * X) @ inv.T - 2.0 * X @ (mu * inv).T \
+        + np.sum(mu * mu * inv, axis=1)[None, :]
+    ll = (lpi - 0.5 * (D * LOG_2PI + lss.sum(axis=1)))[None, :] - 0.5 * quad
+    return ll
+
+
+def estep_diag(X, mu, log_sigma_sq, log_pi, chunk: int = 65536):
+    """Diagonal-covariance E-step (flash_gmm_diag_h100.py:305-384).
+
+    sig_acc (K,D) is the centred, unweighted per-dimension second moment
+    sum_n r_nk (x_nd - mu_kd)^2, which the reference rebuilds from raw moments
+    at diag:258-260.  The reference's pass-2 slab-overlap defect
+    (diag:220-236 over-counts rows when ceil(N/N_SPLIT) % BLOCK_N != 0) is NOT
+    reproduced: this is the intended maths.
+    """
+    X = np.asarray(X, dtype=np.float64)
+    mu = np.asarray(mu, dtype=np.float64)
+    N, D = X.shape
+    K = mu.shape[0]
+    logZ = np.empty(N)
+    Nk = np.zeros(K)
+    mu_acc = np.zeros((K, D))
+    rx2 = np.zeros((K, D))
+    for s in range(0, N, chunk):
+        xs = X[s:s + chunk]
+        ll = loglik_diag(xs, mu, log_sigma_sq, log_pi)
+        lz, r = _responsibilities(ll)
+        logZ[s:s + chunk] = lz
+        Nk += r.sum(axis=0)
+        mu_acc += r.T @ xs
+        rx2 += r.T @ (xs * xs)
+    sig = rx2 - 2.0 * mu * mu_acc + mu * mu * Nk[:, None]
+    return logZ, Nk, mu_acc, sig
+
+
+def loglik_full(X, mu, prec_chol, log_pi):
+    """ll[n,k] of the full-covariance model (flash_gmm_full_h100.py:288-296,
+    124-129): maha = ||L_k^T (x - mu_k)||^2 with prec_chol[k] = L_k,
+    ll = log_pi + sum_d log(|L_kdd| + 1e-30) - 0.5 D log 2pi - 0.5 maha.
+    """
+    X = np.asarray(X, dtype=np.float64)
+    mu = np.asarray(mu, dtype=np.float64)
+    L = np.asarray(prec_chol, dtype=np.float64)
+    lpi = np.asarray(log_pi, dtype=np.float64)
+    D = X.shape[1]
+    K = mu.shape[0]
+    log_diag = np.log(np.abs(np.diagonal(L, axis1=1, axis2=2)) + 1e-30).sum(axis=1)
+    c = lpi + log_diag - 0.5 * D * LOG_2PI
+    ll = np.empty((X.shape[0], K))
+    for k in range(K):
+        v = (X - mu[k][None, :]) @ L[k]       # rows of (L_k^T (x - mu_k))^T
+        ll[:, k] = c[k] - 0.5 * np.sum(v * v, axis=1)
+    return ll
+
+
+def estep_full(X, mu, prec_chol, log_pi, chunk: int = 16384):
+    """Full-covariance E-step (flash_gmm_full_h100.py:235-336).
+
+    sig_outer (K,D,D) = sum_n r_nk x_n x_n^T, the UNcentred second moment the
+    reference accumulates at full:213-228 (M-step recovery at full:257-260).
+    """
+    X = np.asarray(X, dtype=np.float64)
+    N, D = X.shape
+    K = np.asarray(mu).shape[0]
+    logZ = np.empty(N)
+    Nk = np.zeros(K)
+    mu_acc = np.zeros((K, D))
+    sig = np.zeros((K, D, D))
+    for s in range(0, N, chunk):
+        xs = X[s:s + chunk]
+        ll = loglik_full(xs, mu, prec_chol, log_pi)
+        lz, r = _responsibilities(ll)
+        logZ[s:s + chunk] = lz
+        Nk += r.sum(axis=0)
+        mu_acc += r.T @ xs
+        sig += np.einsum("nk,ni,nj->kij", r, xs, xs, optimize=True)
+    return logZ, Nk, mu_acc, sig
+
+
+# ---------------------------------------------------------------------------
+# Timed CPU baseline: the same isotropic formulas, dense fp32 on torch-CPU,
+# chunked over N (multithreaded over the host cores).  Used only by bench.py's
+# cpu_baseline / --impl reference legs.
+# ---------------------------------------------------------------------------
+
+def estep_iso_cpu_fp32(X, mu, log_sigma_sq, log_pi, chunk: int = 65536):
+    """fp32 torch-CPU restatement of flash_gmm.py:84-101 and 151-166."""
+    import torch
+    N, D = X.shape
+    K = mu.shape[0]
+    mu = mu.float()
+    inv_s = torch.exp(-log_sigma_sq.float())
+    const = log_pi.float() - 0.5 * D * (LOG_2PI + log_sigma_sq.float())
+    mu_sq = (mu * mu).sum(1)
+    logZ = torch.empty(N)
+    Nk = torch.zeros(K)
+    mu_acc = torch.zeros(K, D)
+    sig = torch.zeros(K)
+    for s in range(0, N, chunk):
+        xs = X[s:s + chunk].float()
+        x_sq = (xs * xs).sum(1)
+        sq = x_sq[:, None] - 2.0 * (xs @ mu.T) + mu_sq[None, :]
+        ll = const[None, :] - 0.5 * sq * inv_s[None, :]
+        lz = torch.logsumexp(ll, dim=1)
+        r = torch.exp(ll - lz[:, None])
+        logZ[s:s + chunk] = lz
+        Nk += r.sum(0)
+        mu_acc += r.T @ xs
+        sig += (r * sq).sum(0)
+    return logZ, Nk, mu_acc, sig
