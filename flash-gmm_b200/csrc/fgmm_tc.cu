@@ -1,13 +1,916 @@
-// Tensor-core (tcgen05) E-step kernels -- placeholder until the fast path lands.
+// Tensor-core (tcgen05 / TMEM) isotropic E-step for sm_100a.
+//
+// One fused kernel replaces the reference's two launches (online LSE pass,
+// flash_gmm.py:50-103, and the atomic statistics pass, flash_gmm.py:110-166):
+// the distance GEMM is evaluated ONCE per (row, component) pair and the
+// responsibilities never leave the chip.
+//
+// Orientation ("components on TMEM lanes"):
+//   * a CTA owns a slice of 128 components = the 128 TMEM lanes; a cluster of
+//     C = ceil(K/128) CTAs covers all components and processes the same
+//     128-row tiles of X in lock-step;
+//   * distance GEMM  S^T[k, n] = sum_d W[k, d] X[n, d],  W = 2*ish_k*mu_k
+//       A = W (fp16 hi/lo, resident in TMEM), B = X tile (fp16 hi/lo, SMEM,
+//       K-major 128B swizzle), three passes lo*hi + hi*lo + hi*hi: each
+//       operand carries 22 significant bits (fp32-level products).  fp16 is
+//       used for its 11-bit mantissa; ranges are kept in fp16 by exact
+//       power-of-two scaling: X' = X 2^-a (one a per call, from max|mu|) and
+//       W'_k = W_k 2^-s_k (per component), undone exactly in the epilogue;
+//   * ll2[k, n] = S^T + c0'_k - ish_k * |x_n|^2 (log2 units, the folding of
+//     flash_gmm_h100.py:286-291 and 137-138);
+//   * per-row log-sum-exp over components: warp max (redux.sync.max.f32),
+//     exp2, warp sum (fixed point redux.sync.add.u32), combine the 4 warps
+//     that share a row, then exchange one (max, sum) pair per row and CTA
+//     over distributed shared memory -- no second distance pass;
+//   * r = p * 2^(m - logZ2); statistics GEMM  T[k, d] += sum_n R^T[k, n] X[n, d]
+//       A = R^T (fp16 hi/lo written to TMEM by the epilogue warps),
+//       B = the same X' tile read MN-major, three passes again (T = T' 2^a);
+//     Nk_k = sum r and sig_k = sum r*||x - mu_k||^2 are per-thread sums
+//     (thread = component), with sig formed as (c0*Nk - sum r*ll2)/ish.
+//   * per-cluster partials go to the workspace; a second kernel reduces them
+//     in a fixed order (deterministic; the reference uses tl.atomic_add).
+//
+// X enters through a split pass (tc_split_kernel): one read of X writes the
+// fp16 hi/lo words already in the swizzled per-tile order the MMAs read, plus
+// |x|^2 per row, so each stage is filled by one contiguous cp.async.bulk.
+//
+// Warp roles (640 threads): warps 0-15 epilogue (warp w: lane quadrant w%4,
+// row block w/4), warp 16 loads X tiles, warp 17 issues the MMAs, warps 18-19
+// are idle.  Every wait is bounded: on timeout the kernel sets an error word (outputs become NaN) and
+// leaves its loops.
+#include <cuda_fp16.h>
+#include <math.h>
+
+#include <algorithm>
+
 #include "fgmm_internal.cuh"
 
 namespace fgmm {
+namespace {
 
-bool tc_supported(int, const EstepArgs&, std::string* why) {
-  if (why) *why = "tensor-core path not built";
-  return false;
+constexpr int kRows = 128;           // rows per tile (MMA N of the distance GEMM)
+constexpr int kComps = 128;          // components per CTA (TMEM lanes, MMA M)
+constexpr int kMaxD = 128;
+constexpr int kStages = 3;           // X tile buffers
+constexpr int kEpiWarps = 16;
+constexpr int kLoadWarp = kEpiWarps;                        // 16
+constexpr int kMmaWarp = kEpiWarps + 1;                     // 17
+constexpr int kThreads = (kEpiWarps + 4) * 32;              // 640: 5 warpgroups
+constexpr int kMaxCluster = 8;
+constexpr int kChunkBytes = kRows * 128;                    // one 64-feature chunk
+constexpr int kSms = 148;                                   // B200
+constexpr long long kTimeoutCycles = 4000000000LL;          // ~2 s at 2 GHz
+
+// TMEM column map (512 columns allocated).
+constexpr uint32_t kColT = 0;     // statistics accumulator, up to 128 cols
+constexpr uint32_t kColS = 128;   // distance accumulator, 128 cols
+constexpr uint32_t kColR = 256;   // R^T hi (64 cols) + lo (64 cols)
+constexpr uint32_t kColW = 384;   // W hi (Dp/2 cols) + lo (Dp/2 cols)
+
+struct TcParams {
+  const uint8_t* xsplit;     // [num_tiles][stage bytes] swizzled fp16 hi/lo
+  const float* xsq;          // [num_tiles * 128] |x|^2 (0 for padding rows)
+  int64_t N;
+  int K, D, Dp, nch, C;
+  int num_tiles;
+  const __half* Whi;         // [C*128][Dp]  W'_k = W_k 2^-s_k
+  const __half* Wlo;
+  const float4* consts;      // [C*128] {c0', ish, c0, s_k}
+  const int* xscale;         // [0] = a (X' = X 2^-a), set by the split pass
+  float* logZ;
+  float* part;               // [clusters][C*128][D+2]
+  int* err;
+};
+
+struct __align__(8) SmemCtl {
+  uint64_t xfull[kStages];
+  uint64_t xempty[kStages];
+  uint64_t s_full, s_empty, r_full, r_empty, t_done;
+  uint64_t xchg_full[2];
+  uint64_t e_bar[2];   // epilogue-internal sync points (one arrive per warp)
+  uint64_t e_end;
+  uint32_t tmem_base;
+  volatile int abort_flag;
+};
+
+// ----------------------------------------------------------------- PTX helpers
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
 }
-size_t tc_workspace_bytes(int, int64_t, int, int) { return 0; }
-cudaError_t tc_estep(int, const EstepArgs&) { return cudaErrorNotSupported; }
+__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint32_t addr, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(addr), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_try_cluster(uint32_t addr, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(addr), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait; returns false (and raises the abort flag) on timeout or when
+// another role of this CTA already aborted.
+template <bool kCluster = false>
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, SmemCtl* ctl, int* err,
+                                          int code) {
+  const uint32_t a = smem_u32(b);
+  if (kCluster ? mbar_try_cluster(a, parity) : mbar_try(a, parity)) return true;
+  const long long t0 = clock64();
+  while (true) {
+    if (kCluster ? mbar_try_cluster(a, parity) : mbar_try(a, parity)) return true;
+    if (ctl->abort_flag) return false;
+    if (clock64() - t0 > kTimeoutCycles) {
+      ctl->abort_flag = 1;
+      atomicOr(err, code);
+      return false;
+    }
+  }
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t map_to_cta(uint32_t local_addr, uint32_t cta) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_addr), "r"(cta));
+  return r;
+}
+// Asynchronous remote store that completes `bytes` on the destination mbarrier.
+__device__ __forceinline__ void st_async_f2(uint32_t addr, float a, float b, uint32_t bar) {
+  asm volatile(
+      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];" ::"r"(
+          addr),
+      "f"(a), "f"(b), "r"(bar)
+      : "memory");
+}
+// Bulk copy global -> this CTA's shared memory, completing `bytes` on `bar`.
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes,
+                                         uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          dst),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+__device__ __forceinline__ void fence_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_commit(uint64_t* b) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(b))
+               : "memory");
+}
+// D[tmem] (+)= A[tmem] * B[smem desc]; kind::f16 with fp16 inputs, fp32 accum.
+__device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                       uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+      "%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+        "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
+        "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]),
+        "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]),
+        "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(taddr)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&v)[8]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ float redux_max(float v) {
+  float r;
+  asm("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(v));
+  return r;
+}
+__device__ __forceinline__ uint32_t redux_add(uint32_t v) {
+  uint32_t r;
+  asm("redux.sync.add.u32 %0, %1, 0xffffffff;" : "=r"(r) : "r"(v));
+  return r;
+}
+__device__ __forceinline__ float ex2(float x) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+__device__ __forceinline__ float lg2(float x) {
+  float r;
+  asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+// Pack (lo_elem, hi_elem) as f16x2 with lo_elem in the low half.
+__device__ __forceinline__ uint32_t pack_f16(float lo_elem, float hi_elem) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi_elem), "f"(lo_elem));
+  return r;
+}
+__device__ __forceinline__ float f16lo_f(uint32_t p) {
+  return __half2float(__ushort_as_half((unsigned short)(p & 0xffffu)));
+}
+__device__ __forceinline__ float f16hi_f(uint32_t p) {
+  return __half2float(__ushort_as_half((unsigned short)(p >> 16)));
+}
+
+// Split (a, b) into an fp16 hi pair and an fp16 lo pair:
+// a = hi.x + lo.x + O(2^-22 |a|) for |a| in fp16's normal range.
+__device__ __forceinline__ void split2(float a, float b, uint32_t& hi, uint32_t& lo) {
+  hi = pack_f16(a, b);
+  lo = pack_f16(a - f16lo_f(hi), b - f16hi_f(hi));
+}
+
+// UMMA shared-memory descriptors (sm_100: version bits 46-47 = 1), 128B swizzle.
+__device__ __forceinline__ uint64_t desc_kmajor(uint32_t addr) {
+  return (uint64_t)((addr >> 4) & 0x3FFF) | (1ull << 16) | (64ull << 32) | (1ull << 46) |
+         (2ull << 61);
+}
+__device__ __forceinline__ uint64_t desc_mnmajor(uint32_t addr) {
+  return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)(kChunkBytes >> 4) << 16) |
+         (64ull << 32) | (1ull << 46) | (2ull << 61);
+}
+// Instruction descriptor, kind::f16: f16 x f16 -> f32 (c_format = 1,
+// a_format = b_format = 0), M = 128.
+__host__ __device__ constexpr uint32_t idesc_f16(int N, bool b_mn_major) {
+  return (1u << 4) | ((b_mn_major ? 1u : 0u) << 16) | ((uint32_t)(N >> 3) << 17) |
+         ((uint32_t)(128 >> 4) << 24);
+}
+
+// Byte offset of element (row, feature) inside one stage's hi (or lo) buffer:
+// chunk = feature/64 (16 KB each), 128 B per row, 16B-granule XOR swizzle.
+__device__ __forceinline__ uint32_t xoff(int row, int f) {
+  const int e = f & 63;
+  return (uint32_t)((f >> 6) * kChunkBytes + row * 128 + ((((e >> 3) ^ (row & 7))) << 4) +
+                    ((e & 7) << 1));
+}
+
+// ---------------------------------------------------------------------------
+// Power-of-two scale exponent that maps a positive maximum m into [16, 32);
+// 0 for m == 0.  Exact scaling keeps fp16 hi/lo splits in their normal range.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ int scale_exp(float m) {
+  if (!(m > 0.f) || !isfinite(m)) return 0;
+  int e;
+  frexpf(m, &e);  // m = f * 2^e, f in [0.5, 1)
+  return e - 5;
+}
+
+// ---------------------------------------------------------------------------
+// Prep, one block per component (Kpad blocks of 128 threads):
+//   ish = 1/2 e^{-lss} log2 e,  c0 = (log pi - D/2 (log 2pi + lss)) log2 e,
+//   c0' = c0 - ish |mu|^2            (flash_gmm_h100.py:286-291)
+//   W = 2 ish mu, W' = W 2^-s (s from max|W_k|), split into fp16 hi/lo
+//   amax = max_k max_d |mu_kd| (atomic, for the X scale of the split pass).
+// Components >= K get W = 0, ish = 0, c0' = c0 = -1e30 so they carry zero
+// responsibility; -inf log-weights are clamped to the same finite floor.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(128) tc_prep_kernel(
+    const float* __restrict__ mu, int64_t smk, int64_t smd, const float* __restrict__ lss,
+    const float* __restrict__ lpi, int K, int D, int Dp, __half* __restrict__ Whi,
+    __half* __restrict__ Wlo, float4* __restrict__ consts, int* __restrict__ amax) {
+  const int k = blockIdx.x;
+  const bool valid = k < K;
+  double ish = 0.0, c0 = -1e30;
+  if (valid) {
+    const double l = (double)lss[k];
+    ish = 0.5 * exp(-l) * kLog2E;
+    c0 = ((double)lpi[k] - 0.5 * D * (kLog2Pi + l)) * kLog2E;
+  }
+  const int d = threadIdx.x;  // Dp <= 128
+  double m = 0.0;
+  if (valid && d < D) m = (double)mu[(int64_t)k * smk + (int64_t)d * smd];
+  const float w = (float)(2.0 * ish * m);
+  __shared__ double s_sq[4];
+  __shared__ float s_wmax[4], s_mmax[4];
+  double sq = m * m;
+  float wmax = fabsf(w), mmax = (float)fabs(m);
+  for (int o = 16; o > 0; o >>= 1) {
+    sq += __shfl_xor_sync(0xffffffffu, sq, o);
+    wmax = fmaxf(wmax, __shfl_xor_sync(0xffffffffu, wmax, o));
+    mmax = fmaxf(mmax, __shfl_xor_sync(0xffffffffu, mmax, o));
+  }
+  if ((threadIdx.x & 31) == 0) {
+    s_sq[threadIdx.x >> 5] = sq;
+    s_wmax[threadIdx.x >> 5] = wmax;
+    s_mmax[threadIdx.x >> 5] = mmax;
+  }
+  __syncthreads();
+  const double musq = s_sq[0] + s_sq[1] + s_sq[2] + s_sq[3];
+  const float wm = fmaxf(fmaxf(s_wmax[0], s_wmax[1]), fmaxf(s_wmax[2], s_wmax[3]));
+  const int sk = scale_exp(wm);
+  if (d < Dp) {
+    const float ws = ldexpf(w, -sk);
+    const __half h = __float2half_rn(ws);
+    Whi[(size_t)k * Dp + d] = h;
+    Wlo[(size_t)k * Dp + d] = __float2half_rn(ws - __half2float(h));
+  }
+  if (threadIdx.x == 0) {
+    const float mm = fmaxf(fmaxf(s_mmax[0], s_mmax[1]), fmaxf(s_mmax[2], s_mmax[3]));
+    if (valid) atomicMax(amax, __float_as_int(mm));  // non-negative floats order as ints
+    double c0p = c0 - ish * musq;
+    if (!(c0 > -1e30)) { c0 = -1e30; c0p = -1e30; }
+    if (c0p < -1e30) c0p = -1e30;
+    consts[k] = make_float4((float)c0p, (float)ish, (float)c0, (float)sk);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// The fused kernel.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kThreads, 1) tc_iso_kernel(const TcParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  const int stage_bytes = 2 * p.nch * kChunkBytes;  // hi + lo
+  uint8_t* xs = smem;                                // [kStages][hi | lo]
+  float* xsq = reinterpret_cast<float*>(smem + kStages * stage_bytes);      // [kStages][128]
+  float* red_m = xsq + kStages * kRows;              // [16 warps][32]
+  float* red_l = red_m + kEpiWarps * 32;             // [16 warps][32]
+  float* scale_s = red_l + kEpiWarps * 32;           // [4 quadrants][128 rows]
+  float* fin = scale_s + 4 * kRows;                  // [4][128] end-of-kernel sums
+  float2* xchg = reinterpret_cast<float2*>(fin + 8 * kRows);  // [2][kMaxCluster][128]
+  SmemCtl* ctl = reinterpret_cast<SmemCtl*>(xchg + 2 * kMaxCluster * kRows);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const int cluster_id = blockIdx.x / p.C;
+  const int num_clusters = gridDim.x / p.C;
+  const int ntiles = (p.num_tiles - cluster_id + num_clusters - 1) / num_clusters;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&ctl->xfull[s], 1);   // loader's arrive.expect_tx + bulk-copy bytes
+      mbar_init(&ctl->xempty[s], 1);  // commit of the stats MMA that read the stage
+    }
+    mbar_init(&ctl->s_full, 1);
+    mbar_init(&ctl->s_empty, kEpiWarps);
+    mbar_init(&ctl->r_full, kEpiWarps);
+    mbar_init(&ctl->r_empty, 1);
+    mbar_init(&ctl->t_done, 1);
+    mbar_init(&ctl->xchg_full[0], 1);     // local arrive.expect_tx + st.async bytes
+    mbar_init(&ctl->xchg_full[1], 1);
+    mbar_init(&ctl->e_bar[0], kEpiWarps);
+    mbar_init(&ctl->e_bar[1], kEpiWarps);
+    mbar_init(&ctl->e_end, kEpiWarps);
+    ctl->abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) {  // allocate all 512 TMEM columns (one CTA per SM)
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(
+                     smem_u32(&ctl->tmem_base))
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  // Components of this thread (epilogue warps): lane quadrant q, row block cb.
+  const int q = warp & 3, cb = warp >> 2;
+  const int kl = q * 32 + lane;                 // local component (TMEM lane)
+  const int kg = (int)rank * kComps + kl;       // global component
+  float4 kc = make_float4(-1e30f, 0.f, -1e30f, 0.f);
+  if (warp < kEpiWarps) kc = p.consts[kg];
+  const int xa = scale_exp(__int_as_float(*p.xscale));   // X' = X 2^-xa
+
+  for (int i = threadIdx.x; i < kStages * stage_bytes / 16; i += kThreads)
+    reinterpret_cast<uint4*>(xs)[i] = make_uint4(0u, 0u, 0u, 0u);
+  fence_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = ctl->tmem_base;
+  const uint32_t wcols = (uint32_t)(p.Dp / 2);
+
+  // W rows into TMEM (A operand of the distance GEMM): lane = component.
+  if (warp < 4) {
+    const uint4* wh = reinterpret_cast<const uint4*>(p.Whi + (size_t)kg * p.Dp);
+    const uint4* wl = reinterpret_cast<const uint4*>(p.Wlo + (size_t)kg * p.Dp);
+    for (int s = 0; s < p.Dp / 16; ++s) {
+      uint32_t v[8];
+      uint4 a = wh[2 * s], b = wh[2 * s + 1];
+      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+      tmem_st8(tmem + ((uint32_t)(q * 32) << 16) + kColW + 8 * s, v);
+      a = wl[2 * s]; b = wl[2 * s + 1];
+      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+      tmem_st8(tmem + ((uint32_t)(q * 32) << 16) + kColW + wcols + 8 * s, v);
+    }
+    tmem_wait_st();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // peers' barriers are initialised before any remote arrive
+  tc_fence_after();
+
+  if (warp == kMmaWarp) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t id_dist = idesc_f16(kRows, false);
+      const uint32_t id_stat = idesc_f16(64 * p.nch, true);
+      const int ksd = p.Dp / 16;
+      bool first_stats = true;
+      auto issue_stats = [&](int jj) -> void {
+        const uint8_t* st = xs + (jj % kStages) * stage_bytes;
+        const uint32_t xhi = smem_u32(st), xlo = smem_u32(st + p.nch * kChunkBytes);
+        // terms lo*hi, hi*lo, then hi*hi (smallest magnitudes first)
+        for (int t = 0; t < 3; ++t) {
+          const uint32_t acol = kColR + (t == 0 ? 64u : 0u);
+          const uint32_t b = t == 1 ? xlo : xhi;
+          for (int s = 0; s < kRows / 16; ++s) {
+            mma_ts(tmem + kColT, tmem + acol + 8 * s, desc_mnmajor(b + s * 2048), id_stat,
+                   (first_stats && t == 0 && s == 0) ? 0u : 1u);
+          }
+        }
+        first_stats = false;
+        tc_commit(&ctl->r_empty);
+        tc_commit(&ctl->xempty[jj % kStages]);
+      };
+      for (int j = 0; j < ntiles; ++j) {
+        const int b = j % kStages;
+        if (!mbar_wait(&ctl->xfull[b], (j / kStages) & 1, ctl, p.err, 1)) break;
+        if (j >= 1 && !mbar_wait(&ctl->s_empty, (j - 1) & 1, ctl, p.err, 2)) break;
+        tc_fence_after();
+        const uint8_t* st = xs + b * stage_bytes;
+        const uint32_t xhi = smem_u32(st), xlo = smem_u32(st + p.nch * kChunkBytes);
+        for (int t = 0; t < 3; ++t) {
+          const uint32_t acol = kColW + (t == 0 ? wcols : 0u);
+          const uint32_t bb = t == 1 ? xlo : xhi;
+          for (int s = 0; s < ksd; ++s) {
+            const uint32_t baddr = bb + (s >> 2) * kChunkBytes + (s & 3) * 32;
+            mma_ts(tmem + kColS, tmem + acol + 8 * s, desc_kmajor(baddr), id_dist,
+                   (t == 0 && s == 0) ? 0u : 1u);
+          }
+        }
+        tc_commit(&ctl->s_full);
+        if (j >= 1) {
+          if (!mbar_wait(&ctl->r_full, (j - 1) & 1, ctl, p.err, 4)) break;
+          tc_fence_after();
+          issue_stats(j - 1);
+        }
+      }
+      if (ntiles >= 1 && !ctl->abort_flag) {
+        if (mbar_wait(&ctl->r_full, (ntiles - 1) & 1, ctl, p.err, 4)) {
+          tc_fence_after();
+          issue_stats(ntiles - 1);
+          tc_commit(&ctl->t_done);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == kLoadWarp) {
+    // ------------------------------------------------------------ X loader
+    if (lane == 0) {
+      for (int j = 0; j < ntiles; ++j) {
+        const int b = j % kStages;
+        const int64_t tile = cluster_id + (int64_t)j * num_clusters;
+        if (!mbar_wait(&ctl->xempty[b], ((j / kStages) & 1) ^ 1, ctl, p.err, 8)) break;
+        mbar_arrive_expect_tx(&ctl->xfull[b], (uint32_t)stage_bytes + kRows * 4u);
+        bulk_g2s(smem_u32(xs + b * stage_bytes), p.xsplit + tile * stage_bytes,
+                 (uint32_t)stage_bytes, &ctl->xfull[b]);
+        bulk_g2s(smem_u32(xsq + b * kRows), p.xsq + tile * kRows, kRows * 4u, &ctl->xfull[b]);
+      }
+    }
+    __syncwarp();
+  } else if (warp < kEpiWarps) {
+    // ------------------------------------------------------------- epilogue
+    // Per tile: A) S^T -> ll, warp max / exp2 / fixed-point warp sum per row;
+    // B) combine the 4 lane quadrants per row and send one (max, sum) pair to
+    // every CTA of the cluster; C) combine the cluster's pairs -> logZ2 and a
+    // per-(quadrant, row) scale; D) r = p * scale, per-component sums, R^T
+    // (fp16 hi/lo) into TMEM for the statistics GEMM.
+    const float c0p = kc.x, ish = kc.y, c0 = kc.z;
+    const float sck = ldexpf(1.0f, xa + (int)kc.w);  // S = S' 2^(a + s_k)
+    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    float nk_acc = 0.f, rll_acc = 0.f;
+    const int tid_e = threadIdx.x;                 // 0..511
+    const int g = lane >> 3;                       // lane group for row work
+    const int Rw = 32 * cb + 8 * q + (lane & 7);   // row owned in B / C
+    for (int t = 0; t < ntiles; ++t) {
+      const int b = t % kStages;
+      const int64_t row0 = (int64_t)(cluster_id + (int64_t)t * num_clusters) * kRows;
+      // ---- A
+      if (!mbar_wait(&ctl->s_full, t & 1, ctl, p.err, 16)) break;
+      if (!mbar_wait(&ctl->xfull[b], (t / kStages) & 1, ctl, p.err, 4096)) break;
+      tc_fence_after();
+      float ll[32], pv[32];
+      {
+        uint32_t sv[32];
+        tmem_ld32(tmem + lane_base + kColS + 32 * cb, sv);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ctl->s_empty);
+        const float* xq = xsq + b * kRows + 32 * cb;
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) {
+          const float4 s4 = *reinterpret_cast<const float4*>(xq + i);
+          ll[i + 0] = fmaf(__uint_as_float(sv[i + 0]), sck, fmaf(-ish, s4.x, c0p));
+          ll[i + 1] = fmaf(__uint_as_float(sv[i + 1]), sck, fmaf(-ish, s4.y, c0p));
+          ll[i + 2] = fmaf(__uint_as_float(sv[i + 2]), sck, fmaf(-ish, s4.z, c0p));
+          ll[i + 3] = fmaf(__uint_as_float(sv[i + 3]), sck, fmaf(-ish, s4.w, c0p));
+        }
+      }
+#pragma unroll
+      for (int gg = 0; gg < 32; gg += 8) {
+        float m8[8];
+        uint32_t u8[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) m8[i] = redux_max(ll[gg + i]);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          // Fixed-point warp sum of p = 2^(ll - m) at 2^-21 resolution:
+          // p*2^21 + 1.5*2^23 holds the rounded integer in the low mantissa
+          // bits; the raw words are summed exactly (mod 2^32) and the 32
+          // copies of the 0x4B400000 bias are removed when decoded.
+          pv[gg + i] = ex2(ll[gg + i] - m8[i]);
+          u8[i] = redux_add(__float_as_uint(fmaf(pv[gg + i], 2097152.0f, 12582912.0f)));
+        }
+        if (lane == 0) {
+          float4* dm = reinterpret_cast<float4*>(red_m + warp * 32 + gg);
+          uint4* dl = reinterpret_cast<uint4*>(red_l + warp * 32 + gg);
+          dm[0] = make_float4(m8[0], m8[1], m8[2], m8[3]);
+          dm[1] = make_float4(m8[4], m8[5], m8[6], m8[7]);
+          dl[0] = make_uint4(u8[0], u8[1], u8[2], u8[3]);
+          dl[1] = make_uint4(u8[4], u8[5], u8[6], u8[7]);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ctl->e_bar[0]);
+      if (!mbar_wait(&ctl->e_bar[0], t & 1, ctl, p.err, 256)) break;
+
+      // ---- B + C: warp (q, cb) owns rows Rw = 32cb + 8q + (lane & 7); lane
+      // group g handles lane quadrant g and cluster peers g and g + 4.
+      const int slot = t & 1;
+      {
+        const int ri = Rw & 31;
+        const float mg = red_m[(g + 4 * cb) * 32 + ri];
+        const uint32_t raw = __float_as_uint(red_l[(g + 4 * cb) * 32 + ri]) - 32u * 0x4B400000u;
+        const float ug = (float)raw * (1.0f / 2097152.0f);
+        float M = fmaxf(mg, __shfl_xor_sync(0xffffffffu, mg, 8));
+        M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, 16));
+        float L = ug * ex2(mg - M);
+        L += __shfl_xor_sync(0xffffffffu, L, 8);
+        L += __shfl_xor_sync(0xffffffffu, L, 16);
+        const uint32_t my_slot = smem_u32(&xchg[(slot * kMaxCluster + rank) * kRows + Rw]);
+        const uint32_t my_bar = smem_u32(&ctl->xchg_full[slot]);
+        if (tid_e == 0) mbar_arrive_expect_tx(&ctl->xchg_full[slot], (uint32_t)(p.C * kRows * 8));
+        if (g < p.C) st_async_f2(map_to_cta(my_slot, g), M, L, map_to_cta(my_bar, g));
+        if (g + 4 < p.C) st_async_f2(map_to_cta(my_slot, g + 4), M, L, map_to_cta(my_bar, g + 4));
+        const bool ok = mbar_wait<true>(&ctl->xchg_full[slot], (t >> 1) & 1, ctl, p.err, 32);
+        float2 e0 = make_float2(-3e38f, 0.f), e1 = make_float2(-3e38f, 0.f);
+        if (g < p.C) e0 = xchg[(slot * kMaxCluster + g) * kRows + Rw];
+        if (g + 4 < p.C) e1 = xchg[(slot * kMaxCluster + g + 4) * kRows + Rw];
+        float GM = fmaxf(e0.x, e1.x);
+        GM = fmaxf(GM, __shfl_xor_sync(0xffffffffu, GM, 8));
+        GM = fmaxf(GM, __shfl_xor_sync(0xffffffffu, GM, 16));
+        float GL = e0.y * ex2(e0.x - GM) + e1.y * ex2(e1.x - GM);
+        GL += __shfl_xor_sync(0xffffffffu, GL, 8);
+        GL += __shfl_xor_sync(0xffffffffu, GL, 16);
+        const float lz2 = GM + lg2(GL);
+        const bool valid = ok && (row0 + Rw < p.N);
+        if (valid && rank == 0 && g == 0) p.logZ[row0 + Rw] = lz2 * 0.6931471805599453f;
+        scale_s[g * kRows + Rw] = valid ? ex2(mg - lz2) : 0.f;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ctl->e_bar[1]);
+      if (!mbar_wait(&ctl->e_bar[1], t & 1, ctl, p.err, 512)) break;
+
+      // ---- D: r = p * scale, per-component sums, R^T into TMEM (16 rows at a time)
+      const float* sc = scale_s + q * kRows + 32 * cb;
+      float nk_t = 0.f, rll_t = 0.f;
+      if (t >= 1 && !mbar_wait(&ctl->r_empty, (t - 1) & 1, ctl, p.err, 64)) break;
+      tc_fence_after();
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        uint32_t rh[8], rl[8];
+#pragma unroll
+        for (int i = 0; i < 16; i += 4) {
+          const float4 s4 = *reinterpret_cast<const float4*>(sc + 16 * h + i);
+          const int o = 16 * h + i;
+          const float r0 = pv[o + 0] * s4.x, r1 = pv[o + 1] * s4.y;
+          const float r2 = pv[o + 2] * s4.z, r3 = pv[o + 3] * s4.w;
+          nk_t += (r0 + r1) + (r2 + r3);
+          rll_t = fmaf(r0, ll[o + 0], rll_t);
+          rll_t = fmaf(r1, ll[o + 1], rll_t);
+          rll_t = fmaf(r2, ll[o + 2], rll_t);
+          rll_t = fmaf(r3, ll[o + 3], rll_t);
+          split2(r0, r1, rh[i / 2], rl[i / 2]);
+          split2(r2, r3, rh[i / 2 + 1], rl[i / 2 + 1]);
+        }
+        tmem_st8(tmem + lane_base + kColR + 16 * cb + 8 * h, rh);
+        tmem_st8(tmem + lane_base + kColR + 64 + 16 * cb + 8 * h, rl);
+      }
+      nk_acc += nk_t;
+      rll_acc += rll_t;
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ctl->r_full);
+    }
+
+    // End: statistics accumulator -> per-cluster partials.
+    fin[cb * kRows + kl] = nk_acc;
+    fin[(4 + cb) * kRows + kl] = rll_acc;
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&ctl->e_end);
+    const bool ok = !ctl->abort_flag && ntiles >= 1 &&
+                    mbar_wait(&ctl->e_end, 0, ctl, p.err, 1024) &&
+                    mbar_wait(&ctl->t_done, 0, ctl, p.err, 128);
+    const int plen = p.D + 2;
+    float* out = p.part + ((size_t)cluster_id * p.C * kComps + kg) * plen;
+    if (ok) {
+      tc_fence_after();
+      if (32 * cb < 64 * p.nch) {
+        uint32_t tv[32];
+        tmem_ld32(tmem + lane_base + kColT + 32 * cb, tv);
+        tmem_wait_ld();
+        for (int i = 0; i < 32; ++i) {
+          const int d = 32 * cb + i;
+          if (d < p.D) out[2 + d] = ldexpf(__uint_as_float(tv[i]), xa);  // T = T' 2^a
+        }
+      }
+      if (cb == 0) {
+        const float nk = fin[kl] + fin[kRows + kl] + fin[2 * kRows + kl] + fin[3 * kRows + kl];
+        const float rl = fin[4 * kRows + kl] + fin[5 * kRows + kl] + fin[6 * kRows + kl] +
+                         fin[7 * kRows + kl];
+        out[0] = nk;
+        out[1] = ish > 0.f ? (c0 * nk - rl) / ish : 0.f;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
+  }
+  cluster_sync_all();
+}
+
+// ---------------------------------------------------------------------------
+// Split pass: X (any strides) -> fp16 hi/lo words in the swizzled per-tile
+// order of the fused kernel's stage buffers, and |x|^2 per row.  One warp per
+// row; lane l carries features 4l..4l+3.  Rows past N and features past D
+// are zero.  x = hi + lo + O(2^-17 |x|).
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) tc_split_kernel(const float* __restrict__ X, int64_t sxn,
+                                                       int64_t sxd, int vec_ok, int64_t N, int D,
+                                                       int Dp, int nch, int64_t rows_pad,
+                                                       const int* __restrict__ amax,
+                                                       uint8_t* __restrict__ xsplit,
+                                                       float* __restrict__ xsq,
+                                                       int* __restrict__ err) {
+  const int lane = threadIdx.x & 31;
+  const int a = scale_exp(__int_as_float(*amax));  // X' = X 2^-a
+  const int64_t stage_bytes = (int64_t)2 * nch * kChunkBytes;
+  const int nact = Dp / 4;
+  for (int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5); row < rows_pad;
+       row += (int64_t)gridDim.x * 8) {
+    const int f = 4 * lane;
+    float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (lane < nact && row < N) {
+      const float* src = X + row * sxn;
+      if (vec_ok && f + 3 < D) {
+        x = __ldg(reinterpret_cast<const float4*>(src + f));
+      } else {
+        if (f + 0 < D) x.x = __ldg(src + (int64_t)(f + 0) * sxd);
+        if (f + 1 < D) x.y = __ldg(src + (int64_t)(f + 1) * sxd);
+        if (f + 2 < D) x.z = __ldg(src + (int64_t)(f + 2) * sxd);
+        if (f + 3 < D) x.w = __ldg(src + (int64_t)(f + 3) * sxd);
+      }
+    }
+    float sq = x.x * x.x;
+    sq = fmaf(x.y, x.y, sq);
+    sq = fmaf(x.z, x.z, sq);
+    sq = fmaf(x.w, x.w, sq);
+    if (lane < nact) {
+      const float4 xs = make_float4(ldexpf(x.x, -a), ldexpf(x.y, -a), ldexpf(x.z, -a),
+                                    ldexpf(x.w, -a));
+      const float mx = fmaxf(fmaxf(fabsf(xs.x), fabsf(xs.y)), fmaxf(fabsf(xs.z), fabsf(xs.w)));
+      if (!(mx < 65504.f)) atomicOr(err, 0x10000);  // outside fp16 range (or NaN)
+      uint32_t h0, l0, h1, l1;
+      split2(xs.x, xs.y, h0, l0);
+      split2(xs.z, xs.w, h1, l1);
+      uint8_t* tile = xsplit + (row / kRows) * stage_bytes;
+      const uint32_t off = xoff((int)(row % kRows), f);
+      *reinterpret_cast<uint2*>(tile + off) = make_uint2(h0, h1);
+      *reinterpret_cast<uint2*>(tile + nch * kChunkBytes + off) = make_uint2(l0, l1);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+    if (lane == 0) xsq[row] = sq;
+  }
+}
+
+// Sum the per-cluster partials in cluster order; NaN on a device-side error.
+__global__ void tc_reduce_kernel(const float* __restrict__ part, int clusters, int Kpad, int K,
+                                 int D, const int* __restrict__ err, float* __restrict__ Nk,
+                                 float* __restrict__ mu_acc, float* __restrict__ sig,
+                                 int accumulate) {
+  const int plen = D + 2;
+  const bool bad = *err != 0;
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < (int64_t)K * plen;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int k = (int)(e / plen), j = (int)(e % plen);
+    float s = 0.f;
+    for (int c = 0; c < clusters; ++c) s += part[((size_t)c * Kpad + k) * plen + j];
+    if (bad) s = __int_as_float(0x7fc00000);
+    float* dst = j == 0 ? &Nk[k] : j == 1 ? &sig[k] : &mu_acc[(size_t)k * D + (j - 2)];
+    *dst = accumulate ? *dst + s : s;
+  }
+}
+
+struct TcPlan {
+  int C, Kpad, Dp, nch, num_tiles, clusters;
+  size_t smem;
+};
+
+size_t tc_smem_bytes(int nch) {
+  return 1024 + (size_t)kStages * 2 * nch * kChunkBytes + (size_t)kStages * kRows * 4 +
+         (size_t)2 * kEpiWarps * 32 * 4 + (size_t)4 * kRows * 4 + (size_t)8 * kRows * 4 +
+         (size_t)2 * kMaxCluster * kRows * 8 + sizeof(SmemCtl) + 64;
+}
+
+int g_max_clusters[kMaxCluster + 1] = {0};
+
+TcPlan plan_tc(int64_t N, int K, int D, bool query_device) {
+  TcPlan pl;
+  // cluster size: a power of two so every CTA converts 128/C whole rows
+  pl.C = 1;
+  while (pl.C * kComps < K) pl.C *= 2;
+  pl.Kpad = pl.C * kComps;
+  pl.Dp = (D + 15) / 16 * 16;
+  pl.nch = (pl.Dp + 63) / 64;
+  pl.num_tiles = (int)((N + kRows - 1) / kRows);
+  pl.smem = tc_smem_bytes(pl.nch);
+  int maxc = kSms / std::max(pl.C, 1);
+  if (query_device && pl.C <= kMaxCluster) {
+    if (g_max_clusters[pl.C] == 0) {
+      cudaFuncSetAttribute(tc_iso_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)tc_smem_bytes(2));
+      cudaLaunchConfig_t cfg = {};
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = pl.C;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.gridDim = dim3(pl.C * 64, 1, 1);
+      cfg.blockDim = dim3(kThreads, 1, 1);
+      cfg.dynamicSmemBytes = tc_smem_bytes(2);
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, tc_iso_kernel, &cfg) != cudaSuccess || n <= 0) {
+        cudaGetLastError();
+        n = kSms / pl.C;
+      }
+      n = std::min(n, kSms / pl.C);
+      g_max_clusters[pl.C] = n;
+    }
+    maxc = g_max_clusters[pl.C];
+  }
+  pl.clusters = std::max(1, std::min(maxc, pl.num_tiles));
+  return pl;
+}
+
+}  // namespace
+
+bool tc_supported(int variant, const EstepArgs& a, std::string* why) {
+  auto no = [&](const char* m) {
+    if (why) *why = m;
+    return false;
+  };
+  if (variant != kIso) return no("tensor-core path covers the isotropic family");
+  if (a.D > kMaxD) return no("D > 128");
+  if ((a.K + kComps - 1) / kComps > kMaxCluster) return no("K > 1024");
+  return true;
+}
+
+size_t tc_workspace_bytes(int variant, int64_t N, int K, int D) {
+  if (variant != kIso || D > kMaxD || (K + kComps - 1) / kComps > kMaxCluster) return 0;
+  TcPlan pl = plan_tc(N, K, D, false);
+  WsCarve w(nullptr);
+  w.take<int>(64);
+  w.take<__half>((size_t)pl.Kpad * pl.Dp);
+  w.take<__half>((size_t)pl.Kpad * pl.Dp);
+  w.take<float4>(pl.Kpad);
+  // partial rows for the largest cluster count a 148-SM device can run
+  w.take<float>((size_t)(kSms / pl.C) * pl.Kpad * (D + 2));
+  w.take<uint8_t>((size_t)pl.num_tiles * 2 * pl.nch * kChunkBytes);  // split X
+  w.take<float>((size_t)pl.num_tiles * kRows);                          // |x|^2
+  return w.used + 256;
+}
+
+cudaError_t tc_estep(int variant, const EstepArgs& a) {
+  (void)variant;
+  TcPlan pl = plan_tc(a.N, a.K, a.D, true);
+  WsCarve w(a.ws);
+  int* err = w.take<int>(64);
+  __half* Whi = w.take<__half>((size_t)pl.Kpad * pl.Dp);
+  __half* Wlo = w.take<__half>((size_t)pl.Kpad * pl.Dp);
+  float4* consts = w.take<float4>(pl.Kpad);
+  float* part = w.take<float>((size_t)(kSms / pl.C) * pl.Kpad * (a.D + 2));
+  uint8_t* xsplit = w.take<uint8_t>((size_t)pl.num_tiles * 2 * pl.nch * kChunkBytes);
+  float* xsq = w.take<float>((size_t)pl.num_tiles * kRows);
+
+  // err[0]: device error word, err[1]: max|mu| (float bits) for the X scale
+  cudaError_t e = cudaMemsetAsync(err, 0, 2 * sizeof(int), a.stream);
+  if (e != cudaSuccess) return e;
+  tc_prep_kernel<<<pl.Kpad, 128, 0, a.stream>>>(a.mu, a.smk, a.smd, a.cov, a.lpi, a.K, a.D,
+                                                 pl.Dp, Whi, Wlo, consts, err + 1);
+  const int64_t rows_pad = (int64_t)pl.num_tiles * kRows;
+  const int vec_ok = a.sxd == 1 && (reinterpret_cast<uintptr_t>(a.X) & 15) == 0 && a.sxn % 4 == 0;
+  const int sblocks = (int)std::min<int64_t>((rows_pad + 7) / 8, 16 * kSms);
+  tc_split_kernel<<<sblocks, 256, 0, a.stream>>>(a.X, a.sxn, a.sxd, vec_ok, a.N, a.D, pl.Dp,
+                                                  pl.nch, rows_pad, err + 1, xsplit, xsq, err);
+  TcParams p;
+  p.xsplit = xsplit;
+  p.xsq = xsq;
+  p.N = a.N;
+  p.K = a.K;
+  p.D = a.D;
+  p.Dp = pl.Dp;
+  p.nch = pl.nch;
+  p.C = pl.C;
+  p.num_tiles = pl.num_tiles;
+  p.Whi = Whi;
+  p.Wlo = Wlo;
+  p.consts = consts;
+  p.xscale = err + 1;
+  p.logZ = a.logZ;
+  p.part = part;
+  p.err = err;
+
+  e = cudaFuncSetAttribute(tc_iso_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)pl.smem);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = pl.C;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(pl.C * pl.clusters, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = pl.smem;
+  cfg.stream = a.stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  profile_mark(false, a.stream);
+  e = cudaLaunchKernelEx(&cfg, tc_iso_kernel, p);
+  profile_mark(true, a.stream);
+  if (e != cudaSuccess) return e;
+  const int64_t total = (int64_t)a.K * (a.D + 2);
+  const int rblocks = (int)std::min<int64_t>((total + 255) / 256, 1024);
+  tc_reduce_kernel<<<rblocks, 256, 0, a.stream>>>(part, pl.clusters, pl.Kpad, a.K, a.D, err,
+                                                   a.Nk, a.mu_acc, a.sig,
+                                                   (a.flags & 1u) ? 1 : 0);
+  count_launches(4);
+  return cudaGetLastError();
+}
 
 }  // namespace fgmm
