@@ -1,0 +1,410 @@
+"""Benchmark of the B200 GMM E-step (contract: one JSON line from rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload c2|c5]
+
+Metric: E-step (sample x component)/s = N*K / seconds per E-step, the
+reference's headline shape N=1M, K=1024, D=128.
+
+* ``--workload c2`` (default): every rank holds 1M rows of the C2 mixture
+  (generated on the device by the row-keyed generator; rows of rank r are
+  global rows [r*1M, (r+1)*1M)), so per-GPU work is fixed as N grows
+  ("scaling": "weak").  One step = the E-step on each rank + ONE NCCL
+  all-reduce of the packed [Nk | mu_acc | sig_acc] statistics.
+* ``--workload c5``: N = 100M rows in total (config 5), split across the ranks
+  ("scaling": "strong"); each rank runs the E-step over its rows in 10M-row
+  chunks with FGMM_FLAG_ACCUMULATE, then one all-reduce.
+* ``--impl reference``: the reference's algorithm on the host cores -- the
+  CPU restatement in oracle/ (the reference itself is Triton-only and has no
+  CPU implementation of the path), fp32 torch-CPU, chunked, all threads, on a
+  bounded sample of rows per step.  Rank 0 runs it; other ranks exit.
+
+Timing: W untimed warm-up steps, then K steps between a barrier +
+cuda.synchronize on both sides, CUDA events on the launching stream, max over
+ranks.  Inputs (512 MB of X per rank) exceed the 126 MB L2, so no flush is
+needed between steps.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "flash-gmm_b200")
+for _p in (ROOT, PKG):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "estep_pairs_per_s"
+UNIT = "(sample x component)/s"
+K_COMP, D_FEAT = 1024, 128
+ROWS_C2 = 1_000_000
+ROWS_C5 = 100_000_000
+C5_CHUNK = 10_000_000
+SEED = 1234
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return {"hbm_gbs": float(p["hbm_gbs"]), "bf16_tflops": float(p["bf16_tflops"]),
+                "bf16_tflops_sustained": float(p.get("bf16_tflops_sustained", p["bf16_tflops"])),
+                "source": "measured"}
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+                "source": "fallback"}
+
+
+def profile_traffic(name: str):
+    """dram bytes per launch from a committed ncu summary (``key: value``)."""
+    path = os.path.join(ROOT, "profiles", "tc_iso_kernel_c2.txt")
+    try:
+        for line in open(path):
+            if line.startswith(name + ":"):
+                return float(line.split(":", 1)[1].split()[0])
+    except Exception:
+        pass
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.tmp = None
+
+    def start(self):
+        try:
+            self.tmp = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=self.tmp, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.15)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.tmp.flush()
+        self.tmp.seek(0)
+        rows = [r.split(",") for r in self.tmp.read().strip().splitlines() if r.strip()]
+        os.unlink(self.tmp.name)
+        sm = []
+        smax = None
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                smax = float(r[2])
+                for nm, v in zip(names, r[5:9]):
+                    if v.strip().lower() == "active":
+                        reasons.add(nm)
+            except Exception:
+                continue
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def cpu_reference_rate(X, mu, lss, lpi, budget_s: float, chunk: int = 65536):
+    """Pairs/s of the CPU restatement (fp32 torch-CPU) over a bounded sample."""
+    import torch
+    from oracle import gmm_oracle as O
+    torch.set_num_threads(os.cpu_count() or 1)
+    n_done = 0
+    t0 = time.perf_counter()
+    start = 0
+    while True:
+        xs = X[start:start + chunk]
+        O.estep_iso_cpu_fp32(xs, mu, lss, lpi, chunk=chunk)
+        n_done += xs.shape[0]
+        start = (start + chunk) % max(1, X.shape[0] - chunk)
+        if time.perf_counter() - t0 >= budget_s:
+            break
+    dt = time.perf_counter() - t0
+    return n_done * mu.shape[0] / dt, n_done, dt
+
+
+def host_sample(rows: int, seed: int = SEED):
+    """CPU copy of `rows` rows of the benchmark mixture (same recipe)."""
+    import torch
+    import gmm_data
+    return gmm_data.iso_mixture(rows, K_COMP, D_FEAT, seed=seed)
+
+
+def run_reference(args):
+    world, rank, _ = dist_setup()
+    if rank != 0:
+        return 0
+    import torch
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    rows = 65536
+    X, mu, lss, lpi = host_sample(4 * rows)
+    from oracle import gmm_oracle as O
+    for _ in range(max(args.warmup, 0)):
+        O.estep_iso_cpu_fp32(X[:rows], mu, lss, lpi)
+    times = []
+    for s in range(args.steps):
+        xs = X[(s % 4) * rows:(s % 4 + 1) * rows]
+        t0 = time.perf_counter()
+        O.estep_iso_cpu_fp32(xs, mu, lss, lpi)
+        times.append(time.perf_counter() - t0)
+    sec = sum(times) / len(times)
+    value = rows * K_COMP / sec
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded C2 mixture rows on the host)",
+        "config": {"workload": "C2 isotropic E-step, K=1024, D=128; each step a 65,536-row "
+                               "sample on the host CPU", "K": K_COMP, "D": D_FEAT,
+                   "rows_per_step": rows},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": f"{rows} rows x {K_COMP} components per step, torch-CPU fp32"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference is Triton-only (GPU); this arm runs its algorithm's CPU "
+                "restatement from oracle/ on all host threads",
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["c2", "c5"], default="c2")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+    import torch.distributed as dist
+
+    import _fgmm_lib as L
+    import flash_gmm
+    import gmm_stream as GS
+
+    world, rank, local = dist_setup()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+
+    K, D = K_COMP, D_FEAT
+    centres = GS.mixture_centres(K, D, SEED, dev)
+    if args.workload == "c2":
+        n_global = ROWS_C2 * world
+        lo, hi = rank * ROWS_C2, (rank + 1) * ROWS_C2
+        chunk = hi - lo
+        scaling = "weak"
+    else:
+        n_global = ROWS_C5
+        lo, hi = GS.shard_rows(n_global, rank, world)
+        chunk = C5_CHUNK
+        scaling = "strong"
+    n_local = hi - lo
+    X = torch.empty(n_local, D, device=dev, dtype=torch.float32)
+    for s in range(0, n_local, C5_CHUNK):
+        GS.generate_rows(lo + s, min(C5_CHUNK, n_local - s), centres, SEED, out=X[s:s + C5_CHUNK])
+    mu = GS.generate_row_ids(GS.pick_mean_rows(min(n_global, ROWS_C2), K, SEED).to(dev),
+                             centres, SEED)
+    lss = torch.zeros(K, device=dev)
+    lpi = torch.full((K,), -math.log(K), device=dev)
+
+    buf, (Nk, mu_acc, sig) = GS.packed_stats("iso", K, D, dev)
+    logZ = torch.empty(n_local, device=dev)
+
+    def step():
+        for s in range(0, n_local, chunk):
+            e = min(n_local, s + chunk)
+            L.estep(L.FGMM_VARIANT_ISO, X[s:e], mu, lss, lpi,
+                    out=(logZ[s:e], Nk, mu_acc, sig), accumulate=s > 0)
+        if world > 1:
+            dist.all_reduce(buf)
+
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+
+    # profiling events around the dominant (fused tensor-core) kernel
+    ev_pairs = []
+    sampler = ClockSampler(local)
+    launches0 = L.launch_count()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    sampler.start()
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_stop = torch.cuda.Event(enable_timing=True)
+    t_start.record(stream)
+    for _ in range(args.steps):
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        b.record(stream)  # materialise both events before handing them to the library
+        L.set_profile_events(a, b)
+        step()
+        L.set_profile_events(None, None)
+        ev_pairs.append((a, b))
+    t_stop.record(stream)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop()
+    launches = L.launch_count() - launches0
+    ms_total = t_start.elapsed_time(t_stop)
+    kern_ms = [a.elapsed_time(b) for a, b in ev_pairs]
+    ms_step = ms_total / args.steps
+    kern_avg = sum(kern_ms) / len(kern_ms)
+    if world > 1:
+        t = torch.tensor([ms_step, kern_avg], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_step, kern_avg = float(t[0]), float(t[1])
+
+    pairs_step = n_global * K
+    value = pairs_step / (ms_step * 1e-3)
+
+    # ---- end to end through the public API: host X (pinned) -> device ->
+    # flash_gmm_estep -> results read back, every step (rank 0's shard size)
+    e2e = None
+    if not args.no_e2e and args.workload == "c2":
+        Xh = X.cpu().pin_memory()
+        out_host = [torch.empty(n_local, pin_memory=True), torch.empty(K, pin_memory=True),
+                    torch.empty(K, D, pin_memory=True), torch.empty(K, pin_memory=True)]
+        Xd = torch.empty_like(X)
+
+        def e2e_step():
+            Xd.copy_(Xh, non_blocking=True)
+            res = flash_gmm.flash_gmm_estep(Xd, mu, lss, lpi)
+            if world > 1:
+                packed = torch.cat([res[1], res[2].reshape(-1), res[3]])
+                dist.all_reduce(packed)
+            for h, r in zip(out_host, res):
+                h.copy_(r, non_blocking=True)
+
+        for _ in range(2):
+            e2e_step()
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        n_e2e = max(3, min(args.steps, 10))
+        a.record(stream)
+        for _ in range(n_e2e):
+            e2e_step()
+        b.record(stream)
+        torch.cuda.synchronize(dev)
+        ms_e2e = a.elapsed_time(b) / n_e2e
+        if world > 1:
+            t = torch.tensor([ms_e2e], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms_e2e = float(t[0])
+        h2d = X.numel() * 4
+        d2h = (n_local + K + K * D + K) * 4
+        e2e = {"value": pairs_step / (ms_e2e * 1e-3), "unit": UNIT, "h2d_bytes_per_step": h2d,
+               "d2h_bytes_per_step": d2h, "ms_per_step": ms_e2e,
+               "path": "pinned host X -> device, flash_gmm.flash_gmm_estep, outputs -> host"}
+
+    # ---- roofline of the dominant kernel
+    peaks = load_peaks()
+    flops_launch = 4.0 * D * (chunk if args.workload == "c5" else n_local) * K
+    # the events bracket the last fused-kernel launch of each step (one launch
+    # per step for c2; the last chunk's launch for c5)
+    kern_launch_ms = kern_avg
+    achieved = flops_launch / (kern_launch_ms * 1e-3) / 1e12
+    traffic = profile_traffic("dram_bytes_per_launch")
+    roofline = {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
+                "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
+                "traffic": traffic, "peak_source": peaks["source"] + " bf16 burst",
+                "kernel": "tc_iso_kernel (fused distance/LSE/statistics)",
+                "algorithmic_flops_per_launch": flops_launch,
+                "kernel_ms_per_launch": kern_launch_ms}
+    # north-star roofline: max(tensor time at TF32 peak = bf16/2, exp time at MUFU peak)
+    p_tf32 = peaks["bf16_tflops"] / 2
+    p_mufu = 148 * 16 * 1.965e9
+    t_tc = 4.0 * D * pairs_step / world / (p_tf32 * 1e12)
+    t_exp = pairs_step / world / p_mufu
+    t_roof = max(t_tc, t_exp)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        Xc, muc, lssc, lpic = X[:262144].cpu(), mu.cpu(), lss.cpu(), lpi.cpu()
+        rate, nrows, secs = cpu_reference_rate(Xc, muc, lssc, lpic, budget_s=12.0)
+        cpu = {"value": rate, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+               "sample": f"{nrows} rows x {K} components of the same workload in {secs:.1f} s, "
+                         "torch-CPU fp32 restatement (oracle/)"}
+
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+        "scaling": scaling, "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: C2 mixture (centres ~ N(0,4I), rows = centre + N(0,I)) generated "
+                "on device by row-keyed counter RNG; mu = 1024 rows of X",
+        "config": {"workload": ("C2 isotropic E-step N=1M K=1024 D=128 per GPU"
+                                if args.workload == "c2" else
+                                "C5 streaming isotropic E-step N=100M K=1024 D=128 total"),
+                   "N_global": n_global, "N_per_rank": n_local, "K": K, "D": D,
+                   "parallelism": f"dp{world} (rows sharded, one NCCL all-reduce of stats)",
+                   "l2": "inputs larger than L2 (X = %d MB per rank)" % (n_local * D * 4 >> 20)},
+        "roofline": roofline,
+        "north_star_roofline": {"t_tensor_ms": t_tc * 1e3, "t_exp_ms": t_exp * 1e3,
+                                "t_roof_ms": t_roof * 1e3, "frac": t_roof / (ms_step * 1e-3),
+                                "basis": "TF32 = bf16/2 of measured, MUFU 148x16/clk @1965 MHz"},
+        "clocks": clocks,
+        "e2e": e2e,
+        "gpu_launches": launches,
+        "cpu_baseline": cpu,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())
