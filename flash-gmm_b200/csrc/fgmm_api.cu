@@ -154,6 +154,11 @@ __global__ void gen_rows_kernel(float* __restrict__ X, const int64_t* __restrict
 
 }  // namespace
 
+// Entry helpers for the other translation units' extern "C" functions.
+int entry_fail(int code, const std::string& msg) { return fail(code, msg); }
+int entry_check_device(std::string* why) { return check_device(why); }
+int entry_run_estep(int variant, const EstepArgs& a) { return run_estep(variant, a); }
+
 static std::atomic<uint64_t> g_launches{0};
 static thread_local cudaEvent_t g_prof_start = nullptr, g_prof_stop = nullptr;
 

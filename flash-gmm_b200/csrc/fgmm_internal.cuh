@@ -66,6 +66,13 @@ cudaError_t generate_iso_rows(float* X, const int64_t* row_ids, int64_t row0,
 
 int num_sms();
 
+// Shared by the extern "C" entry points: record a failure message for
+// fgmm_last_error(), the sm_100 device check, and the validated E-step
+// dispatch (argument checks, workspace check, tensor-core or general path).
+int entry_fail(int code, const std::string& msg);
+int entry_check_device(std::string* why);
+int entry_run_estep(int variant, const EstepArgs& a);
+
 // Launch accounting and the optional profiling events around the dominant
 // kernel (see fgmm_launch_count / fgmm_set_profile_events).
 void count_launches(int n);

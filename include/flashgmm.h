@@ -111,6 +111,28 @@ FGMM_API int fgmm_estep_full(const float* X, int64_t x_stride_n, int64_t x_strid
                     void* workspace, size_t workspace_bytes,
                     unsigned flags, void* stream);
 
+/* Isotropic E-step that allocates nothing and takes no workspace: same
+ * arguments, results and paths as fgmm_estep_iso, with the scratch in a
+ * fixed device array of FGMM_NOALLOC_SCRATCH_BYTES per device owned by the
+ * library.  For callers that cannot allocate device memory at the call site
+ * (a host runtime whose device memory belongs to another pool, or a loop
+ * that must not call cudaMalloc).  No counterpart in the reference.
+ *  - Shapes whose workspace exceeds the scratch return FGMM_ERR_WORKSPACE
+ *    (about 110,000 rows at D = 128 on the tensor-core path; the general
+ *    kernels' scratch does not grow with N).
+ *  - Nothing has to be zeroed beforehand.
+ *  - The first call on a device does a one-time set-up (looks up the
+ *    array's device address); make it before any stream capture.
+ *  - All calls on one device share the array: calls that may overlap in
+ *    time (different streams or unordered host threads) race. */
+#define FGMM_NOALLOC_SCRATCH_BYTES (64u << 20)
+FGMM_API int fgmm_estep_iso_noalloc(const float* X, int64_t x_stride_n, int64_t x_stride_d,
+                   const float* mu, int64_t mu_stride_k, int64_t mu_stride_d,
+                   const float* log_sigma_sq, const float* log_pi,
+                   int64_t N, int32_t K, int32_t D,
+                   float* logZ, float* Nk, float* mu_acc, float* sig_acc,
+                   unsigned flags, void* stream);
+
 /* Number of kernels this library has launched in this process (all devices,
  * all threads).  Lets a caller count the launches inside a timed region. */
 FGMM_API uint64_t fgmm_launch_count(void);
