@@ -1,43 +1,55 @@
-// Tensor-core (tcgen05 / TMEM) isotropic E-step for sm_100a.
+// Tensor-core (tcgen05 / TMEM) E-step for sm_100a: isotropic and diagonal
+// covariance.
 //
-// One fused kernel replaces the reference's two launches (online LSE pass,
-// flash_gmm.py:50-103, and the atomic statistics pass, flash_gmm.py:110-166):
-// the distance GEMM is evaluated ONCE per (row, component) pair and the
-// responsibilities never leave the chip.
+// One fused kernel replaces the reference's two launches per family (online
+// LSE pass + statistics pass: flash_gmm.py:50-103 / 110-166, and
+// flash_gmm_diag_h100.py:63-130 / 159-282): the distance GEMM is evaluated
+// ONCE per (row, component) pair and the responsibilities never leave the
+// chip.
+//
+// Both families are the same computation over a per-row feature vector F:
+//   isotropic:  F = x                     (nfeat = Dp)
+//               ll2[k,n] = c0'_k - ish_k |x_n|^2 + sum_d (2 ish_k mu_kd) x_nd
+//   diagonal:   F = [(x-c)^2, (x-c)]      (nfeat = 2 Dp; c = mean of the mu's)
+//               ll2[k,n] = c0'_k + sum_d (-A_kd (x-c)_d^2 + B_kd (x-c)_d)
+//               A = 1/2 e^{-lss} log2 e,  B = 2 A (mu - c)
+// (log2 units: the folding of flash_gmm_h100.py:286-291 / 137-138 and
+// flash_gmm_diag_h100.py:332-339 / 116-119).  The statistics GEMM
+// T = R^T F gives mu_acc (iso) or [sum r (x-c)^2, sum r (x-c)] (diag), from
+// which the reduction forms sig = rxsq - 2 m mu + m^2 Nk (diag:258-260).
 //
 // Orientation ("components on TMEM lanes"):
 //   * a CTA owns a slice of 128 components = the 128 TMEM lanes; a cluster of
 //     C = ceil(K/128) CTAs covers all components and processes the same
-//     128-row tiles of X in lock-step;
-//   * distance GEMM  S^T[k, n] = sum_d W[k, d] X[n, d],  W = 2*ish_k*mu_k
-//       A = W (fp16 hi/lo, resident in TMEM), B = X tile (fp16 hi/lo, SMEM,
+//     row tiles of F in lock-step (128 rows iso, 64 rows diag: TMEM holds
+//     T nfeat | S rows | R^T rows | W nfeat columns = 512 at most);
+//   * distance GEMM  S^T[k, n] = sum_f W[k, f] F[n, f]
+//       A = W (fp16 hi/lo, resident in TMEM), B = F tile (fp16 hi/lo, SMEM,
 //       K-major 128B swizzle), three passes lo*hi + hi*lo + hi*hi: each
 //       operand carries 22 significant bits (fp32-level products).  fp16 is
 //       used for its 11-bit mantissa; ranges are kept in fp16 by exact
-//       power-of-two scaling: X' = X 2^-a (one a per call, from max|mu|) and
+//       power-of-two scaling: x' = x 2^-a (one a per call) and
 //       W'_k = W_k 2^-s_k (per component), undone exactly in the epilogue;
-//   * ll2[k, n] = S^T + c0'_k - ish_k * |x_n|^2 (log2 units, the folding of
-//     flash_gmm_h100.py:286-291 and 137-138);
 //   * per-row log-sum-exp over components: warp max (redux.sync.max.f32),
 //     exp2, warp sum (fixed point redux.sync.add.u32), combine the 4 warps
 //     that share a row, then exchange one (max, sum) pair per row and CTA
 //     over distributed shared memory -- no second distance pass;
-//   * r = p * 2^(m - logZ2); statistics GEMM  T[k, d] += sum_n R^T[k, n] X[n, d]
+//   * r = p * 2^(m - logZ2); statistics GEMM  T[k, f] += sum_n R^T[k, n] F[n, f]
 //       A = R^T (fp16 hi/lo written to TMEM by the epilogue warps),
-//       B = the same X' tile read MN-major, three passes again (T = T' 2^a);
-//     Nk_k = sum r and sig_k = sum r*||x - mu_k||^2 are per-thread sums
-//     (thread = component), with sig formed as (c0*Nk - sum r*ll2)/ish.
+//       B = the same F tile read MN-major, three passes again;
+//     Nk_k = sum r (and, iso, sum r*ll2 for sig) are per-thread sums
+//     (thread = component).
 //   * per-cluster partials go to the workspace; a second kernel reduces them
 //     in a fixed order (deterministic; the reference uses tl.atomic_add).
 //
-// X enters through a split pass (tc_split_kernel): one read of X writes the
-// fp16 hi/lo words already in the swizzled per-tile order the MMAs read, plus
-// |x|^2 per row, so each stage is filled by one contiguous cp.async.bulk.
+// F enters through a split pass: one read of X writes the fp16 hi/lo feature
+// words already in the swizzled per-tile order the MMAs read (plus |x|^2 per
+// row for iso), so each stage is filled by one contiguous cp.async.bulk.
 //
 // Warp roles (640 threads): warps 0-15 epilogue (warp w: lane quadrant w%4,
-// row block w/4), warp 16 loads X tiles, warp 17 issues the MMAs, warps 18-19
-// are idle.  Every wait is bounded: on timeout the kernel sets an error word (outputs become NaN) and
-// leaves its loops.
+// row block w/4), warp 16 loads F tiles, warp 17 issues the MMAs, warps 18-19
+// are idle.  Every wait is bounded: on timeout the kernel sets an error word
+// (outputs become NaN) and leaves its loops.
 #include <cuda_fp16.h>
 #include <math.h>
 
@@ -48,43 +60,58 @@
 namespace fgmm {
 namespace {
 
-constexpr int kRows = 128;           // rows per tile (MMA N of the distance GEMM)
 constexpr int kComps = 128;          // components per CTA (TMEM lanes, MMA M)
-constexpr int kMaxD = 128;
-constexpr int kStages = 3;           // X tile buffers
+constexpr int kMaxDIso = 128;        // largest D of the isotropic tensor-core path
+constexpr int kMaxDDiag = 96;        // largest D of the diagonal tensor-core path
 constexpr int kEpiWarps = 16;
 constexpr int kLoadWarp = kEpiWarps;                        // 16
 constexpr int kMmaWarp = kEpiWarps + 1;                     // 17
 constexpr int kThreads = (kEpiWarps + 4) * 32;              // 640: 5 warpgroups
 constexpr int kMaxCluster = 8;
-constexpr int kChunkBytes = kRows * 128;                    // one 64-feature chunk
+constexpr int kMaxStages = 4;
 constexpr int kSms = 148;                                   // B200
 constexpr long long kTimeoutCycles = 4000000000LL;          // ~2 s at 2 GHz
 
-// TMEM column map (512 columns allocated).
-constexpr uint32_t kColT = 0;     // statistics accumulator, up to 128 cols
-constexpr uint32_t kColS = 128;   // distance accumulator, 128 cols
-constexpr uint32_t kColR = 256;   // R^T hi (64 cols) + lo (64 cols)
-constexpr uint32_t kColW = 384;   // W hi (Dp/2 cols) + lo (Dp/2 cols)
+// Compile-time shape of one fused-kernel instantiation.
+template <int ROWS, bool DIAG>
+struct Cfg {
+  static constexpr int kRows = ROWS;                  // rows per tile (distance MMA N)
+  static constexpr bool kDiag = DIAG;
+  static constexpr int kStages = DIAG ? 4 : 3;        // F tile buffers
+  static constexpr int kMaxFeat = DIAG ? 2 * kMaxDDiag : kMaxDIso;
+  static constexpr int kChunk = ROWS * 128;           // bytes of one 64-feature chunk
+  static constexpr int kRB = ROWS / 4;                // rows per epilogue warp (phase A)
+  // TMEM column map (512 columns allocated)
+  static constexpr uint32_t kColT = 0;                // statistics accumulator
+  static constexpr uint32_t kColS = kMaxFeat;         // distance accumulator
+  static constexpr uint32_t kColR = kColS + ROWS;     // R^T hi (ROWS/2) + lo (ROWS/2)
+  static constexpr uint32_t kColW = kColR + ROWS;     // W hi (nfeat/2) + lo (nfeat/2)
+  static_assert(kColW + kMaxFeat <= 512, "TMEM budget");
+  static_assert(kStages <= kMaxStages, "stage count");
+  static_assert(kRB == 16 || kRB == 32, "epilogue row block");
+};
+using IsoCfg = Cfg<128, false>;
+using DiagCfg = Cfg<64, true>;
 
 struct TcParams {
-  const uint8_t* xsplit;     // [num_tiles][stage bytes] swizzled fp16 hi/lo
-  const float* xsq;          // [num_tiles * 128] |x|^2 (0 for padding rows)
+  const uint8_t* xsplit;     // [num_tiles][stage bytes] swizzled fp16 hi/lo features
+  const float* xsq;          // iso: [num_tiles * rows] |x|^2 (0 for padding rows)
   int64_t N;
-  int K, D, Dp, nch, C;
+  int K, D, Dp, nfeat, nch, C;
   int num_tiles;
-  const __half* Whi;         // [C*128][Dp]  W'_k = W_k 2^-s_k
+  const __half* Whi;         // [C*128][nfeat]  W'_k = W_k 2^-s_k
   const __half* Wlo;
-  const float4* consts;      // [C*128] {c0', ish, c0, s_k}
-  const int* xscale;         // [0] = a (X' = X 2^-a), set by the split pass
+  const float4* consts;      // [C*128] {c0', ish (iso), c0 (iso), s_k}
+  const int* xscale;         // [0] = max|mu| (or max|mu - c|) bits -> a
   float* logZ;
-  float* part;               // [clusters][C*128][D+2]
+  float* part;               // [clusters][C*128][plen]
+  int plen;
   int* err;
 };
 
 struct __align__(8) SmemCtl {
-  uint64_t xfull[kStages];
-  uint64_t xempty[kStages];
+  uint64_t xfull[kMaxStages];
+  uint64_t xempty[kMaxStages];
   uint64_t s_full, s_empty, r_full, r_empty, t_done;
   uint64_t xchg_full[2];
   uint64_t e_bar[2];   // epilogue-internal sync points (one arrive per warp)
@@ -215,6 +242,16 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
       : "r"(taddr)
       : "memory");
 }
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* v) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+      "%15}, [%16];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+        "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
+        "=r"(v[14]), "=r"(v[15])
+      : "r"(taddr)
+      : "memory");
+}
 __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
@@ -272,8 +309,9 @@ __device__ __forceinline__ uint64_t desc_kmajor(uint32_t addr) {
   return (uint64_t)((addr >> 4) & 0x3FFF) | (1ull << 16) | (64ull << 32) | (1ull << 46) |
          (2ull << 61);
 }
-__device__ __forceinline__ uint64_t desc_mnmajor(uint32_t addr) {
-  return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)(kChunkBytes >> 4) << 16) |
+// MN-major: LBO = byte stride between 64-element chunks along N.
+__device__ __forceinline__ uint64_t desc_mnmajor(uint32_t addr, uint32_t chunk_bytes) {
+  return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)(chunk_bytes >> 4) << 16) |
          (64ull << 32) | (1ull << 46) | (2ull << 61);
 }
 // Instruction descriptor, kind::f16: f16 x f16 -> f32 (c_format = 1,
@@ -284,26 +322,34 @@ __host__ __device__ constexpr uint32_t idesc_f16(int N, bool b_mn_major) {
 }
 
 // Byte offset of element (row, feature) inside one stage's hi (or lo) buffer:
-// chunk = feature/64 (16 KB each), 128 B per row, 16B-granule XOR swizzle.
-__device__ __forceinline__ uint32_t xoff(int row, int f) {
+// chunk = feature/64 (rows*128 bytes each), 128 B per row, 16B-granule XOR
+// swizzle.
+__device__ __forceinline__ uint32_t xoff(int row, int f, int chunk_bytes) {
   const int e = f & 63;
-  return (uint32_t)((f >> 6) * kChunkBytes + row * 128 + ((((e >> 3) ^ (row & 7))) << 4) +
+  return (uint32_t)((f >> 6) * chunk_bytes + row * 128 + ((((e >> 3) ^ (row & 7))) << 4) +
                     ((e & 7) << 1));
 }
 
 // ---------------------------------------------------------------------------
-// Power-of-two scale exponent that maps a positive maximum m into [16, 32);
+// Power-of-two scale exponent e such that m 2^-e lies in [2^(t-1), 2^t);
 // 0 for m == 0.  Exact scaling keeps fp16 hi/lo splits in their normal range.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ int scale_exp(float m) {
+__host__ __device__ __forceinline__ int scale_exp_to(float m, int t) {
   if (!(m > 0.f) || !isfinite(m)) return 0;
   int e;
   frexpf(m, &e);  // m = f * 2^e, f in [0.5, 1)
-  return e - 5;
+  return e - t;
+}
+__device__ __forceinline__ int scale_exp(float m) { return scale_exp_to(m, 5); }
+// X scale of each family: iso maps max|mu| into [16, 32); diag maps
+// max|mu - c| into [4, 8), leaving room for the squared features.
+template <bool DIAG>
+__device__ __forceinline__ int x_scale_exp(float m) {
+  return scale_exp_to(m, DIAG ? 3 : 5);
 }
 
 // ---------------------------------------------------------------------------
-// Prep, one block per component (Kpad blocks of 128 threads):
+// Isotropic prep, one block per component (Kpad blocks of 128 threads):
 //   ish = 1/2 e^{-lss} log2 e,  c0 = (log pi - D/2 (log 2pi + lss)) log2 e,
 //   c0' = c0 - ish |mu|^2            (flash_gmm_h100.py:286-291)
 //   W = 2 ish mu, W' = W 2^-s (s from max|W_k|), split into fp16 hi/lo
@@ -362,21 +408,133 @@ __global__ void __launch_bounds__(128) tc_prep_kernel(
 }
 
 // ---------------------------------------------------------------------------
+// Diagonal centre, one block per feature d (Dp blocks of 256 threads):
+// c_d = mean_k mu_kd (0 for padding features) and amax = max |mu_kd - c_d|.
+// Centring by one global vector leaves (x - mu)^2 unchanged and keeps the
+// expanded form x^2 - 2 x mu + mu^2 away from cancellation when the data sit
+// far from the origin.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) tc_diag_centre_kernel(const float* __restrict__ mu,
+                                                             int64_t smk, int64_t smd, int K,
+                                                             int D, float* __restrict__ cvec,
+                                                             int* __restrict__ amax) {
+  const int d = blockIdx.x;
+  __shared__ double s_sum[8];
+  __shared__ float s_max[8];
+  __shared__ float s_c;
+  double sum = 0.0;
+  if (d < D)
+    for (int k = threadIdx.x; k < K; k += 256) sum += (double)mu[(int64_t)k * smk + (int64_t)d * smd];
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  if ((threadIdx.x & 31) == 0) s_sum[threadIdx.x >> 5] = sum;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double t = 0.0;
+    for (int w = 0; w < 8; ++w) t += s_sum[w];
+    s_c = d < D ? (float)(t / K) : 0.f;
+    cvec[d] = s_c;
+  }
+  __syncthreads();
+  const float c = s_c;
+  float mx = 0.f;
+  if (d < D)
+    for (int k = threadIdx.x; k < K; k += 256)
+      mx = fmaxf(mx, fabsf(mu[(int64_t)k * smk + (int64_t)d * smd] - c));
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if ((threadIdx.x & 31) == 0) s_max[threadIdx.x >> 5] = mx;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float m = 0.f;
+    for (int w = 0; w < 8; ++w) m = fmaxf(m, s_max[w]);
+    atomicMax(amax, __float_as_int(m));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Diagonal prep, one block per component (Kpad blocks of 128 threads; thread
+// d < Dp):  A = 1/2 e^{-lss} log2 e,  B = 2 A (mu - c),
+//   c0  = (log pi - 1/2 (D log 2pi + sum_d lss)) log2 e     (diag:335-339)
+//   c0' = c0 - sum_d A (mu - c)^2
+//   W = [-A 2^{2a}, B 2^a] (features [(x-c)^2 2^-2a, (x-c) 2^-a]), scaled by
+//   a per-component power of two and split into fp16 hi/lo.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(128) tc_prep_diag_kernel(
+    const float* __restrict__ mu, int64_t smk, int64_t smd, const float* __restrict__ lss,
+    const float* __restrict__ lpi, const float* __restrict__ cvec, const int* __restrict__ amax,
+    int K, int D, int Dp, __half* __restrict__ Whi, __half* __restrict__ Wlo,
+    float4* __restrict__ consts) {
+  const int k = blockIdx.x;
+  const bool valid = k < K;
+  const int a = x_scale_exp<true>(__int_as_float(*amax));
+  const int d = threadIdx.x;
+  double A = 0.0, B = 0.0, l = 0.0, am2 = 0.0;
+  if (valid && d < D) {
+    l = (double)lss[(int64_t)k * D + d];
+    const double m = (double)mu[(int64_t)k * smk + (int64_t)d * smd] - (double)cvec[d];
+    A = 0.5 * exp(-l) * kLog2E;
+    B = 2.0 * A * m;
+    am2 = A * m * m;
+  }
+  const float wa = (float)ldexp(-A, 2 * a), wb = (float)ldexp(B, a);
+  __shared__ double s_l[4], s_am2[4];
+  __shared__ float s_wmax[4];
+  float wmax = fmaxf(fabsf(wa), fabsf(wb));
+  for (int o = 16; o > 0; o >>= 1) {
+    l += __shfl_xor_sync(0xffffffffu, l, o);
+    am2 += __shfl_xor_sync(0xffffffffu, am2, o);
+    wmax = fmaxf(wmax, __shfl_xor_sync(0xffffffffu, wmax, o));
+  }
+  if ((threadIdx.x & 31) == 0) {
+    s_l[threadIdx.x >> 5] = l;
+    s_am2[threadIdx.x >> 5] = am2;
+    s_wmax[threadIdx.x >> 5] = wmax;
+  }
+  __syncthreads();
+  const float wm = fmaxf(fmaxf(s_wmax[0], s_wmax[1]), fmaxf(s_wmax[2], s_wmax[3]));
+  const int sk = scale_exp(wm);
+  if (d < Dp) {
+    const int nfeat = 2 * Dp;
+    float ws = ldexpf(wa, -sk);
+    __half h = __float2half_rn(ws);
+    Whi[(size_t)k * nfeat + d] = h;
+    Wlo[(size_t)k * nfeat + d] = __float2half_rn(ws - __half2float(h));
+    ws = ldexpf(wb, -sk);
+    h = __float2half_rn(ws);
+    Whi[(size_t)k * nfeat + Dp + d] = h;
+    Wlo[(size_t)k * nfeat + Dp + d] = __float2half_rn(ws - __half2float(h));
+  }
+  if (threadIdx.x == 0) {
+    double c0 = -1e30, c0p = -1e30;
+    if (valid) {
+      const double lsum = s_l[0] + s_l[1] + s_l[2] + s_l[3];
+      const double am2s = s_am2[0] + s_am2[1] + s_am2[2] + s_am2[3];
+      c0 = ((double)lpi[k] - 0.5 * ((double)D * kLog2Pi + lsum)) * kLog2E;
+      c0p = c0 - am2s;
+      if (!(c0 > -1e30)) { c0 = -1e30; c0p = -1e30; }
+      if (c0p < -1e30) c0p = -1e30;
+    }
+    consts[k] = make_float4((float)c0p, 0.f, (float)c0, (float)sk);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // The fused kernel.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(kThreads, 1) tc_iso_kernel(const TcParams p) {
+template <class G>
+__global__ void __launch_bounds__(kThreads, 1) tc_fused_kernel(const TcParams p) {
+  constexpr int R = G::kRows, RB = G::kRB, NS = G::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  const int stage_bytes = 2 * p.nch * kChunkBytes;  // hi + lo
-  uint8_t* xs = smem;                                // [kStages][hi | lo]
-  float* xsq = reinterpret_cast<float*>(smem + kStages * stage_bytes);      // [kStages][128]
-  float* red_m = xsq + kStages * kRows;              // [16 warps][32]
-  float* red_l = red_m + kEpiWarps * 32;             // [16 warps][32]
-  float* scale_s = red_l + kEpiWarps * 32;           // [4 quadrants][128 rows]
-  float* fin = scale_s + 4 * kRows;                  // [4][128] end-of-kernel sums
-  float2* xchg = reinterpret_cast<float2*>(fin + 8 * kRows);  // [2][kMaxCluster][128]
-  SmemCtl* ctl = reinterpret_cast<SmemCtl*>(xchg + 2 * kMaxCluster * kRows);
+  const int stage_bytes = 2 * p.nch * G::kChunk;    // hi + lo
+  uint8_t* xs = smem;                                // [NS][hi | lo]
+  float* xsq = reinterpret_cast<float*>(smem + NS * stage_bytes);  // iso: [NS][R]
+  float* red_m = xsq + NS * R;                       // [16 warps][RB]
+  float* red_l = red_m + kEpiWarps * RB;             // [16 warps][RB]
+  float* scale_s = red_l + kEpiWarps * RB;           // [4 quadrants][R rows]
+  float* fin = scale_s + 4 * R;                      // [8][128] end-of-kernel sums
+  float2* xchg = reinterpret_cast<float2*>(fin + 8 * kComps);  // [2][kMaxCluster][R]
+  SmemCtl* ctl = reinterpret_cast<SmemCtl*>(xchg + 2 * kMaxCluster * R);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_rank();
@@ -385,7 +543,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_iso_kernel(const TcParams p) {
   const int ntiles = (p.num_tiles - cluster_id + num_clusters - 1) / num_clusters;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < NS; ++s) {
       mbar_init(&ctl->xfull[s], 1);   // loader's arrive.expect_tx + bulk-copy bytes
       mbar_init(&ctl->xempty[s], 1);  // commit of the stats MMA that read the stage
     }
@@ -414,29 +572,29 @@ __global__ void __launch_bounds__(kThreads, 1) tc_iso_kernel(const TcParams p) {
   const int kg = (int)rank * kComps + kl;       // global component
   float4 kc = make_float4(-1e30f, 0.f, -1e30f, 0.f);
   if (warp < kEpiWarps) kc = p.consts[kg];
-  const int xa = scale_exp(__int_as_float(*p.xscale));   // X' = X 2^-xa
+  const int xa = x_scale_exp<G::kDiag>(__int_as_float(*p.xscale));   // x' = x 2^-xa
 
-  for (int i = threadIdx.x; i < kStages * stage_bytes / 16; i += kThreads)
+  for (int i = threadIdx.x; i < NS * stage_bytes / 16; i += kThreads)
     reinterpret_cast<uint4*>(xs)[i] = make_uint4(0u, 0u, 0u, 0u);
   fence_async_smem();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = ctl->tmem_base;
-  const uint32_t wcols = (uint32_t)(p.Dp / 2);
+  const uint32_t wcols = (uint32_t)(p.nfeat / 2);
 
   // W rows into TMEM (A operand of the distance GEMM): lane = component.
   if (warp < 4) {
-    const uint4* wh = reinterpret_cast<const uint4*>(p.Whi + (size_t)kg * p.Dp);
-    const uint4* wl = reinterpret_cast<const uint4*>(p.Wlo + (size_t)kg * p.Dp);
-    for (int s = 0; s < p.Dp / 16; ++s) {
+    const uint4* wh = reinterpret_cast<const uint4*>(p.Whi + (size_t)kg * p.nfeat);
+    const uint4* wl = reinterpret_cast<const uint4*>(p.Wlo + (size_t)kg * p.nfeat);
+    for (int s = 0; s < p.nfeat / 16; ++s) {
       uint32_t v[8];
       uint4 a = wh[2 * s], b = wh[2 * s + 1];
       v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-      tmem_st8(tmem + ((uint32_t)(q * 32) << 16) + kColW + 8 * s, v);
+      tmem_st8(tmem + ((uint32_t)(q * 32) << 16) + G::kColW + 8 * s, v);
       a = wl[2 * s]; b = wl[2 * s + 1];
       v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-      tmem_st8(tmem + ((uint32_t)(q * 32) << 16) + kColW + wcols + 8 * s, v);
+      tmem_st8(tmem + ((uint32_t)(q * 32) << 16) + G::kColW + wcols + 8 * s, v);
     }
     tmem_wait_st();
   }
@@ -448,39 +606,39 @@ __global__ void __launch_bounds__(kThreads, 1) tc_iso_kernel(const TcParams p) {
   if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      const uint32_t id_dist = idesc_f16(kRows, false);
+      const uint32_t id_dist = idesc_f16(R, false);
       const uint32_t id_stat = idesc_f16(64 * p.nch, true);
-      const int ksd = p.Dp / 16;
+      const int ksd = p.nfeat / 16;
       bool first_stats = true;
       auto issue_stats = [&](int jj) -> void {
-        const uint8_t* st = xs + (jj % kStages) * stage_bytes;
-        const uint32_t xhi = smem_u32(st), xlo = smem_u32(st + p.nch * kChunkBytes);
+        const uint8_t* st = xs + (jj % NS) * stage_bytes;
+        const uint32_t xhi = smem_u32(st), xlo = smem_u32(st + p.nch * G::kChunk);
         // terms lo*hi, hi*lo, then hi*hi (smallest magnitudes first)
         for (int t = 0; t < 3; ++t) {
-          const uint32_t acol = kColR + (t == 0 ? 64u : 0u);
+          const uint32_t acol = G::kColR + (t == 0 ? (uint32_t)(R / 2) : 0u);
           const uint32_t b = t == 1 ? xlo : xhi;
-          for (int s = 0; s < kRows / 16; ++s) {
-            mma_ts(tmem + kColT, tmem + acol + 8 * s, desc_mnmajor(b + s * 2048), id_stat,
-                   (first_stats && t == 0 && s == 0) ? 0u : 1u);
+          for (int s = 0; s < R / 16; ++s) {
+            mma_ts(tmem + G::kColT, tmem + acol + 8 * s, desc_mnmajor(b + s * 2048, G::kChunk),
+                   id_stat, (first_stats && t == 0 && s == 0) ? 0u : 1u);
           }
         }
         first_stats = false;
         tc_commit(&ctl->r_empty);
-        tc_commit(&ctl->xempty[jj % kStages]);
+        tc_commit(&ctl->xempty[jj % NS]);
       };
       for (int j = 0; j < ntiles; ++j) {
-        const int b = j % kStages;
-        if (!mbar_wait(&ctl->xfull[b], (j / kStages) & 1, ctl, p.err, 1)) break;
+        const int b = j % NS;
+        if (!mbar_wait(&ctl->xfull[b], (j / NS) & 1, ctl, p.err, 1)) break;
         if (j >= 1 && !mbar_wait(&ctl->s_empty, (j - 1) & 1, ctl, p.err, 2)) break;
         tc_fence_after();
         const uint8_t* st = xs + b * stage_bytes;
-        const uint32_t xhi = smem_u32(st), xlo = smem_u32(st + p.nch * kChunkBytes);
+        const uint32_t xhi = smem_u32(st), xlo = smem_u32(st + p.nch * G::kChunk);
         for (int t = 0; t < 3; ++t) {
-          const uint32_t acol = kColW + (t == 0 ? wcols : 0u);
+          const uint32_t acol = G::kColW + (t == 0 ? wcols : 0u);
           const uint32_t bb = t == 1 ? xlo : xhi;
           for (int s = 0; s < ksd; ++s) {
-            const uint32_t baddr = bb + (s >> 2) * kChunkBytes + (s & 3) * 32;
-            mma_ts(tmem + kColS, tmem + acol + 8 * s, desc_kmajor(baddr), id_dist,
+            const uint32_t baddr = bb + (s >> 2) * G::kChunk + (s & 3) * 32;
+            mma_ts(tmem + G::kColS, tmem + acol + 8 * s, desc_kmajor(baddr), id_dist,
                    (t == 0 && s == 0) ? 0u : 1u);
           }
         }
@@ -501,16 +659,18 @@ __global__ void __launch_bounds__(kThreads, 1) tc_iso_kernel(const TcParams p) {
     }
     __syncwarp();
   } else if (warp == kLoadWarp) {
-    // ------------------------------------------------------------ X loader
+    // ------------------------------------------------------------ F loader
     if (lane == 0) {
+      const uint32_t tx = (uint32_t)stage_bytes + (G::kDiag ? 0u : (uint32_t)R * 4u);
       for (int j = 0; j < ntiles; ++j) {
-        const int b = j % kStages;
+        const int b = j % NS;
         const int64_t tile = cluster_id + (int64_t)j * num_clusters;
-        if (!mbar_wait(&ctl->xempty[b], ((j / kStages) & 1) ^ 1, ctl, p.err, 8)) break;
-        mbar_arrive_expect_tx(&ctl->xfull[b], (uint32_t)stage_bytes + kRows * 4u);
+        if (!mbar_wait(&ctl->xempty[b], ((j / NS) & 1) ^ 1, ctl, p.err, 8)) break;
+        mbar_arrive_expect_tx(&ctl->xfull[b], tx);
         bulk_g2s(smem_u32(xs + b * stage_bytes), p.xsplit + tile * stage_bytes,
                  (uint32_t)stage_bytes, &ctl->xfull[b]);
-        bulk_g2s(smem_u32(xsq + b * kRows), p.xsq + tile * kRows, kRows * 4u, &ctl->xfull[b]);
+        if (!G::kDiag)
+          bulk_g2s(smem_u32(xsq + b * R), p.xsq + tile * R, (uint32_t)R * 4u, &ctl->xfull[b]);
       }
     }
     __syncwarp();
@@ -522,39 +682,46 @@ __global__ void __launch_bounds__(kThreads, 1) tc_iso_kernel(const TcParams p) {
     // per-(quadrant, row) scale; D) r = p * scale, per-component sums, R^T
     // (fp16 hi/lo) into TMEM for the statistics GEMM.
     const float c0p = kc.x, ish = kc.y, c0 = kc.z;
-    const float sck = ldexpf(1.0f, xa + (int)kc.w);  // S = S' 2^(a + s_k)
+    const float sck = ldexpf(1.0f, (G::kDiag ? 0 : xa) + (int)kc.w);  // S = S' 2^(a + s_k)
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
     float nk_acc = 0.f, rll_acc = 0.f;
     const int tid_e = threadIdx.x;                 // 0..511
     const int g = lane >> 3;                       // lane group for row work
-    const int Rw = 32 * cb + 8 * q + (lane & 7);   // row owned in B / C
+    const bool row_owner = 8 * warp < R;           // warps that own rows in B / C
+    const int Rw = 8 * warp + (lane & 7);          // row owned in B / C
     for (int t = 0; t < ntiles; ++t) {
-      const int b = t % kStages;
-      const int64_t row0 = (int64_t)(cluster_id + (int64_t)t * num_clusters) * kRows;
+      const int b = t % NS;
+      const int64_t row0 = (int64_t)(cluster_id + (int64_t)t * num_clusters) * R;
       // ---- A
       if (!mbar_wait(&ctl->s_full, t & 1, ctl, p.err, 16)) break;
-      if (!mbar_wait(&ctl->xfull[b], (t / kStages) & 1, ctl, p.err, 4096)) break;
+      if (!mbar_wait(&ctl->xfull[b], (t / NS) & 1, ctl, p.err, 4096)) break;
       tc_fence_after();
-      float ll[32], pv[32];
+      float ll[RB], pv[RB];
       {
-        uint32_t sv[32];
-        tmem_ld32(tmem + lane_base + kColS + 32 * cb, sv);
+        uint32_t sv[RB];
+        if constexpr (RB == 32) tmem_ld32(tmem + lane_base + G::kColS + RB * cb, sv);
+        else tmem_ld16(tmem + lane_base + G::kColS + RB * cb, sv);
         tmem_wait_ld();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&ctl->s_empty);
-        const float* xq = xsq + b * kRows + 32 * cb;
+        if constexpr (G::kDiag) {
 #pragma unroll
-        for (int i = 0; i < 32; i += 4) {
-          const float4 s4 = *reinterpret_cast<const float4*>(xq + i);
-          ll[i + 0] = fmaf(__uint_as_float(sv[i + 0]), sck, fmaf(-ish, s4.x, c0p));
-          ll[i + 1] = fmaf(__uint_as_float(sv[i + 1]), sck, fmaf(-ish, s4.y, c0p));
-          ll[i + 2] = fmaf(__uint_as_float(sv[i + 2]), sck, fmaf(-ish, s4.z, c0p));
-          ll[i + 3] = fmaf(__uint_as_float(sv[i + 3]), sck, fmaf(-ish, s4.w, c0p));
+          for (int i = 0; i < RB; ++i) ll[i] = fmaf(__uint_as_float(sv[i]), sck, c0p);
+        } else {
+          const float* xq = xsq + b * R + RB * cb;
+#pragma unroll
+          for (int i = 0; i < RB; i += 4) {
+            const float4 s4 = *reinterpret_cast<const float4*>(xq + i);
+            ll[i + 0] = fmaf(__uint_as_float(sv[i + 0]), sck, fmaf(-ish, s4.x, c0p));
+            ll[i + 1] = fmaf(__uint_as_float(sv[i + 1]), sck, fmaf(-ish, s4.y, c0p));
+            ll[i + 2] = fmaf(__uint_as_float(sv[i + 2]), sck, fmaf(-ish, s4.z, c0p));
+            ll[i + 3] = fmaf(__uint_as_float(sv[i + 3]), sck, fmaf(-ish, s4.w, c0p));
+          }
         }
       }
 #pragma unroll
-      for (int gg = 0; gg < 32; gg += 8) {
+      for (int gg = 0; gg < RB; gg += 8) {
         float m8[8];
         uint32_t u8[8];
 #pragma unroll
@@ -569,8 +736,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_iso_kernel(const TcParams p) {
           u8[i] = redux_add(__float_as_uint(fmaf(pv[gg + i], 2097152.0f, 12582912.0f)));
         }
         if (lane == 0) {
-          float4* dm = reinterpret_cast<float4*>(red_m + warp * 32 + gg);
-          uint4* dl = reinterpret_cast<uint4*>(red_l + warp * 32 + gg);
+          float4* dm = reinterpret_cast<float4*>(red_m + warp * RB + gg);
+          uint4* dl = reinterpret_cast<uint4*>(red_l + warp * RB + gg);
           dm[0] = make_float4(m8[0], m8[1], m8[2], m8[3]);
           dm[1] = make_float4(m8[4], m8[5], m8[6], m8[7]);
           dl[0] = make_uint4(u8[0], u8[1], u8[2], u8[3]);
@@ -581,28 +748,28 @@ __global__ void __launch_bounds__(kThreads, 1) tc_iso_kernel(const TcParams p) {
       if (lane == 0) mbar_arrive(&ctl->e_bar[0]);
       if (!mbar_wait(&ctl->e_bar[0], t & 1, ctl, p.err, 256)) break;
 
-      // ---- B + C: warp (q, cb) owns rows Rw = 32cb + 8q + (lane & 7); lane
-      // group g handles lane quadrant g and cluster peers g and g + 4.
+      // ---- B + C: warp w < R/8 owns rows Rw = 8w + (lane & 7); lane group g
+      // handles lane quadrant g and cluster peers g and g + 4.
       const int slot = t & 1;
-      {
-        const int ri = Rw & 31;
-        const float mg = red_m[(g + 4 * cb) * 32 + ri];
-        const uint32_t raw = __float_as_uint(red_l[(g + 4 * cb) * 32 + ri]) - 32u * 0x4B400000u;
+      if (row_owner) {
+        const int ri = Rw % RB, blk = Rw / RB;
+        const float mg = red_m[(g + 4 * blk) * RB + ri];
+        const uint32_t raw = __float_as_uint(red_l[(g + 4 * blk) * RB + ri]) - 32u * 0x4B400000u;
         const float ug = (float)raw * (1.0f / 2097152.0f);
         float M = fmaxf(mg, __shfl_xor_sync(0xffffffffu, mg, 8));
         M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, 16));
         float L = ug * ex2(mg - M);
         L += __shfl_xor_sync(0xffffffffu, L, 8);
         L += __shfl_xor_sync(0xffffffffu, L, 16);
-        const uint32_t my_slot = smem_u32(&xchg[(slot * kMaxCluster + rank) * kRows + Rw]);
+        const uint32_t my_slot = smem_u32(&xchg[(slot * kMaxCluster + rank) * R + Rw]);
         const uint32_t my_bar = smem_u32(&ctl->xchg_full[slot]);
-        if (tid_e == 0) mbar_arrive_expect_tx(&ctl->xchg_full[slot], (uint32_t)(p.C * kRows * 8));
+        if (tid_e == 0) mbar_arrive_expect_tx(&ctl->xchg_full[slot], (uint32_t)(p.C * R * 8));
         if (g < p.C) st_async_f2(map_to_cta(my_slot, g), M, L, map_to_cta(my_bar, g));
         if (g + 4 < p.C) st_async_f2(map_to_cta(my_slot, g + 4), M, L, map_to_cta(my_bar, g + 4));
         const bool ok = mbar_wait<true>(&ctl->xchg_full[slot], (t >> 1) & 1, ctl, p.err, 32);
         float2 e0 = make_float2(-3e38f, 0.f), e1 = make_float2(-3e38f, 0.f);
-        if (g < p.C) e0 = xchg[(slot * kMaxCluster + g) * kRows + Rw];
-        if (g + 4 < p.C) e1 = xchg[(slot * kMaxCluster + g + 4) * kRows + Rw];
+        if (g < p.C) e0 = xchg[(slot * kMaxCluster + g) * R + Rw];
+        if (g + 4 < p.C) e1 = xchg[(slot * kMaxCluster + g + 4) * R + Rw];
         float GM = fmaxf(e0.x, e1.x);
         GM = fmaxf(GM, __shfl_xor_sync(0xffffffffu, GM, 8));
         GM = fmaxf(GM, __shfl_xor_sync(0xffffffffu, GM, 16));
@@ -612,19 +779,19 @@ __global__ void __launch_bounds__(kThreads, 1) tc_iso_kernel(const TcParams p) {
         const float lz2 = GM + lg2(GL);
         const bool valid = ok && (row0 + Rw < p.N);
         if (valid && rank == 0 && g == 0) p.logZ[row0 + Rw] = lz2 * 0.6931471805599453f;
-        scale_s[g * kRows + Rw] = valid ? ex2(mg - lz2) : 0.f;
+        scale_s[g * R + Rw] = valid ? ex2(mg - lz2) : 0.f;
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&ctl->e_bar[1]);
       if (!mbar_wait(&ctl->e_bar[1], t & 1, ctl, p.err, 512)) break;
 
       // ---- D: r = p * scale, per-component sums, R^T into TMEM (16 rows at a time)
-      const float* sc = scale_s + q * kRows + 32 * cb;
+      const float* sc = scale_s + q * R + RB * cb;
       float nk_t = 0.f, rll_t = 0.f;
       if (t >= 1 && !mbar_wait(&ctl->r_empty, (t - 1) & 1, ctl, p.err, 64)) break;
       tc_fence_after();
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
+      for (int h = 0; h < RB / 16; ++h) {
         uint32_t rh[8], rl[8];
 #pragma unroll
         for (int i = 0; i < 16; i += 4) {
@@ -633,15 +800,17 @@ __global__ void __launch_bounds__(kThreads, 1) tc_iso_kernel(const TcParams p) {
           const float r0 = pv[o + 0] * s4.x, r1 = pv[o + 1] * s4.y;
           const float r2 = pv[o + 2] * s4.z, r3 = pv[o + 3] * s4.w;
           nk_t += (r0 + r1) + (r2 + r3);
-          rll_t = fmaf(r0, ll[o + 0], rll_t);
-          rll_t = fmaf(r1, ll[o + 1], rll_t);
-          rll_t = fmaf(r2, ll[o + 2], rll_t);
-          rll_t = fmaf(r3, ll[o + 3], rll_t);
+          if constexpr (!G::kDiag) {
+            rll_t = fmaf(r0, ll[o + 0], rll_t);
+            rll_t = fmaf(r1, ll[o + 1], rll_t);
+            rll_t = fmaf(r2, ll[o + 2], rll_t);
+            rll_t = fmaf(r3, ll[o + 3], rll_t);
+          }
           split2(r0, r1, rh[i / 2], rl[i / 2]);
           split2(r2, r3, rh[i / 2 + 1], rl[i / 2 + 1]);
         }
-        tmem_st8(tmem + lane_base + kColR + 16 * cb + 8 * h, rh);
-        tmem_st8(tmem + lane_base + kColR + 64 + 16 * cb + 8 * h, rl);
+        tmem_st8(tmem + lane_base + G::kColR + (RB / 2) * cb + 8 * h, rh);
+        tmem_st8(tmem + lane_base + G::kColR + R / 2 + (RB / 2) * cb + 8 * h, rl);
       }
       nk_acc += nk_t;
       rll_acc += rll_t;
@@ -652,32 +821,43 @@ __global__ void __launch_bounds__(kThreads, 1) tc_iso_kernel(const TcParams p) {
     }
 
     // End: statistics accumulator -> per-cluster partials.
-    fin[cb * kRows + kl] = nk_acc;
-    fin[(4 + cb) * kRows + kl] = rll_acc;
+    fin[cb * kComps + kl] = nk_acc;
+    fin[(4 + cb) * kComps + kl] = rll_acc;
     __syncwarp();
     if (lane == 0) mbar_arrive(&ctl->e_end);
     const bool ok = !ctl->abort_flag && ntiles >= 1 &&
                     mbar_wait(&ctl->e_end, 0, ctl, p.err, 1024) &&
                     mbar_wait(&ctl->t_done, 0, ctl, p.err, 128);
-    const int plen = p.D + 2;
-    float* out = p.part + ((size_t)cluster_id * p.C * kComps + kg) * plen;
+    float* out = p.part + ((size_t)cluster_id * p.C * kComps + kg) * p.plen;
     if (ok) {
       tc_fence_after();
-      if (32 * cb < 64 * p.nch) {
+      for (int blk = cb; 32 * blk < 64 * p.nch; blk += 4) {
         uint32_t tv[32];
-        tmem_ld32(tmem + lane_base + kColT + 32 * cb, tv);
+        tmem_ld32(tmem + lane_base + G::kColT + 32 * blk, tv);
         tmem_wait_ld();
         for (int i = 0; i < 32; ++i) {
-          const int d = 32 * cb + i;
-          if (d < p.D) out[2 + d] = ldexpf(__uint_as_float(tv[i]), xa);  // T = T' 2^a
+          const int f = 32 * blk + i;
+          const float v = __uint_as_float(tv[i]);
+          if constexpr (G::kDiag) {
+            // partial row {Nk, sum r (x-c) [D], sum r (x-c)^2 [D]}
+            if (f < p.Dp) {
+              if (f < p.D) out[1 + p.D + f] = ldexpf(v, 2 * xa);
+            } else if (f - p.Dp < p.D) {
+              out[1 + (f - p.Dp)] = ldexpf(v, xa);
+            }
+          } else {
+            if (f < p.D) out[2 + f] = ldexpf(v, xa);  // T = T' 2^a
+          }
         }
       }
       if (cb == 0) {
-        const float nk = fin[kl] + fin[kRows + kl] + fin[2 * kRows + kl] + fin[3 * kRows + kl];
-        const float rl = fin[4 * kRows + kl] + fin[5 * kRows + kl] + fin[6 * kRows + kl] +
-                         fin[7 * kRows + kl];
+        const float nk = fin[kl] + fin[kComps + kl] + fin[2 * kComps + kl] + fin[3 * kComps + kl];
         out[0] = nk;
-        out[1] = ish > 0.f ? (c0 * nk - rl) / ish : 0.f;
+        if constexpr (!G::kDiag) {
+          const float rl = fin[4 * kComps + kl] + fin[5 * kComps + kl] + fin[6 * kComps + kl] +
+                           fin[7 * kComps + kl];
+          out[1] = ish > 0.f ? (c0 * nk - rl) / ish : 0.f;
+        }
       }
     }
   }
@@ -692,27 +872,31 @@ __global__ void __launch_bounds__(kThreads, 1) tc_iso_kernel(const TcParams p) {
 }
 
 // ---------------------------------------------------------------------------
-// Split pass: X (any strides) -> fp16 hi/lo words in the swizzled per-tile
-// order of the fused kernel's stage buffers, and |x|^2 per row.  One warp per
-// row; lane l carries features 4l..4l+3.  Rows past N and features past D
-// are zero.  x = hi + lo + O(2^-17 |x|).
+// Split pass: X (any strides) -> fp16 hi/lo feature words in the swizzled
+// per-tile order of the fused kernel's stage buffers.  One warp per row; lane
+// l carries features 4l..4l+3 of x.  Rows past N and features past D are
+// zero.  v = hi + lo + O(2^-22 |v|).
+//   iso:  features x 2^-a, plus |x|^2 per row;
+//   diag: features [((x-c) 2^-a)^2 | (x-c) 2^-a].
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(256) tc_split_kernel(const float* __restrict__ X, int64_t sxn,
-                                                       int64_t sxd, int vec_ok, int64_t N, int D,
-                                                       int Dp, int nch, int64_t rows_pad,
-                                                       const int* __restrict__ amax,
-                                                       uint8_t* __restrict__ xsplit,
-                                                       float* __restrict__ xsq,
-                                                       int* __restrict__ err) {
+template <int ROWS, bool DIAG>
+__global__ void __launch_bounds__(256) tc_split_kernel(
+    const float* __restrict__ X, int64_t sxn, int64_t sxd, int vec_ok, int64_t N, int D, int Dp,
+    int nch, int64_t rows_pad, const int* __restrict__ amax, const float* __restrict__ cvec,
+    uint8_t* __restrict__ xsplit, float* __restrict__ xsq, int* __restrict__ err) {
+  constexpr int kChunk = ROWS * 128;
   const int lane = threadIdx.x & 31;
-  const int a = scale_exp(__int_as_float(*amax));  // X' = X 2^-a
-  const int64_t stage_bytes = (int64_t)2 * nch * kChunkBytes;
+  const int a = x_scale_exp<DIAG>(__int_as_float(*amax));
+  const int64_t stage_bytes = (int64_t)2 * nch * kChunk;
   const int nact = Dp / 4;
+  const int f = 4 * lane;
+  float4 cc = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (DIAG && lane < nact) cc = *reinterpret_cast<const float4*>(cvec + f);
   for (int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5); row < rows_pad;
        row += (int64_t)gridDim.x * 8) {
-    const int f = 4 * lane;
     float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (lane < nact && row < N) {
+    const bool live = row < N;
+    if (lane < nact && live) {
       const float* src = X + row * sxn;
       if (vec_ok && f + 3 < D) {
         x = __ldg(reinterpret_cast<const float4*>(src + f));
@@ -722,31 +906,46 @@ __global__ void __launch_bounds__(256) tc_split_kernel(const float* __restrict__
         if (f + 2 < D) x.z = __ldg(src + (int64_t)(f + 2) * sxd);
         if (f + 3 < D) x.w = __ldg(src + (int64_t)(f + 3) * sxd);
       }
+      if (DIAG) {  // padding features have x = c = 0
+        x.x -= cc.x; x.y -= cc.y; x.z -= cc.z; x.w -= cc.w;
+      }
     }
-    float sq = x.x * x.x;
-    sq = fmaf(x.y, x.y, sq);
-    sq = fmaf(x.z, x.z, sq);
-    sq = fmaf(x.w, x.w, sq);
     if (lane < nact) {
       const float4 xs = make_float4(ldexpf(x.x, -a), ldexpf(x.y, -a), ldexpf(x.z, -a),
                                     ldexpf(x.w, -a));
-      const float mx = fmaxf(fmaxf(fabsf(xs.x), fabsf(xs.y)), fmaxf(fabsf(xs.z), fabsf(xs.w)));
+      float mx = fmaxf(fmaxf(fabsf(xs.x), fabsf(xs.y)), fmaxf(fabsf(xs.z), fabsf(xs.w)));
+      if (DIAG) mx = fmaxf(mx, mx * mx);
       if (!(mx < 65504.f)) atomicOr(err, 0x10000);  // outside fp16 range (or NaN)
+      uint8_t* tile = xsplit + (row / ROWS) * stage_bytes;
+      const int r = (int)(row % ROWS);
       uint32_t h0, l0, h1, l1;
       split2(xs.x, xs.y, h0, l0);
       split2(xs.z, xs.w, h1, l1);
-      uint8_t* tile = xsplit + (row / kRows) * stage_bytes;
-      const uint32_t off = xoff((int)(row % kRows), f);
+      const uint32_t off = xoff(r, DIAG ? Dp + f : f, kChunk);
       *reinterpret_cast<uint2*>(tile + off) = make_uint2(h0, h1);
-      *reinterpret_cast<uint2*>(tile + nch * kChunkBytes + off) = make_uint2(l0, l1);
+      *reinterpret_cast<uint2*>(tile + nch * kChunk + off) = make_uint2(l0, l1);
+      if (DIAG) {
+        split2(xs.x * xs.x, xs.y * xs.y, h0, l0);
+        split2(xs.z * xs.z, xs.w * xs.w, h1, l1);
+        const uint32_t off2 = xoff(r, f, kChunk);
+        *reinterpret_cast<uint2*>(tile + off2) = make_uint2(h0, h1);
+        *reinterpret_cast<uint2*>(tile + nch * kChunk + off2) = make_uint2(l0, l1);
+      }
     }
+    if (!DIAG) {
+      float sq = x.x * x.x;
+      sq = fmaf(x.y, x.y, sq);
+      sq = fmaf(x.z, x.z, sq);
+      sq = fmaf(x.w, x.w, sq);
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
-    if (lane == 0) xsq[row] = sq;
+      for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+      if (lane == 0) xsq[row] = sq;
+    }
   }
 }
 
-// Sum the per-cluster partials in cluster order; NaN on a device-side error.
+// Isotropic: sum the per-cluster partials {Nk, sig, mu_acc[D]} in cluster
+// order; NaN on a device-side error.
 __global__ void tc_reduce_kernel(const float* __restrict__ part, int clusters, int Kpad, int K,
                                  int D, const int* __restrict__ err, float* __restrict__ Nk,
                                  float* __restrict__ mu_acc, float* __restrict__ sig,
@@ -764,129 +963,113 @@ __global__ void tc_reduce_kernel(const float* __restrict__ part, int clusters, i
   }
 }
 
-struct TcPlan {
-  int C, Kpad, Dp, nch, num_tiles, clusters;
-  size_t smem;
-};
-
-size_t tc_smem_bytes(int nch) {
-  return 1024 + (size_t)kStages * 2 * nch * kChunkBytes + (size_t)kStages * kRows * 4 +
-         (size_t)2 * kEpiWarps * 32 * 4 + (size_t)4 * kRows * 4 + (size_t)8 * kRows * 4 +
-         (size_t)2 * kMaxCluster * kRows * 8 + sizeof(SmemCtl) + 64;
+// Diagonal: sum the partials {Nk, sum r (x-c), sum r (x-c)^2} in cluster
+// order, then mu_acc = Tx + c Nk and sig = Txx - 2 m Tx + m^2 Nk with
+// m = mu - c (the centred form of diag:258-260).  NaN on a device error.
+__global__ void tc_reduce_diag_kernel(const float* __restrict__ part, int clusters, int Kpad,
+                                      int K, int D, const float* __restrict__ cvec,
+                                      const float* __restrict__ mu, int64_t smk, int64_t smd,
+                                      const int* __restrict__ err, float* __restrict__ Nk,
+                                      float* __restrict__ mu_acc, float* __restrict__ sig,
+                                      int accumulate) {
+  const int plen = 1 + 2 * D;
+  const bool bad = *err != 0;
+  const float qnan = __int_as_float(0x7fc00000);
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < (int64_t)K * (D + 1);
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int k = (int)(e / (D + 1)), j = (int)(e % (D + 1));
+    double n = 0.0;
+    for (int c = 0; c < clusters; ++c) n += part[((size_t)c * Kpad + k) * plen];
+    if (j == 0) {
+      const float v = bad ? qnan : (float)n;
+      Nk[k] = accumulate ? Nk[k] + v : v;
+      continue;
+    }
+    const int d = j - 1;
+    double tx = 0.0, txx = 0.0;
+    for (int c = 0; c < clusters; ++c) {
+      const float* pr = part + ((size_t)c * Kpad + k) * plen;
+      tx += pr[1 + d];
+      txx += pr[1 + D + d];
+    }
+    const double cd = cvec[d];
+    const double m = (double)mu[(int64_t)k * smk + (int64_t)d * smd] - cd;
+    float vm = (float)(tx + cd * n);
+    float vs = (float)(txx - 2.0 * m * tx + m * m * n);
+    if (bad) vm = vs = qnan;
+    const size_t o = (size_t)k * D + d;
+    mu_acc[o] = accumulate ? mu_acc[o] + vm : vm;
+    sig[o] = accumulate ? sig[o] + vs : vs;
+  }
 }
 
-int g_max_clusters[kMaxCluster + 1] = {0};
+struct TcPlan {
+  bool diag;
+  int rows, C, Kpad, Dp, nfeat, nch, num_tiles, clusters, plen;
+  size_t stage_bytes, smem;
+};
 
-TcPlan plan_tc(int64_t N, int K, int D, bool query_device) {
+template <class G>
+size_t tc_smem_bytes(int nch) {
+  return 1024 + (size_t)G::kStages * 2 * nch * G::kChunk +
+         ((size_t)G::kStages * G::kRows + 2 * kEpiWarps * G::kRB + 4 * G::kRows + 8 * kComps) * 4 +
+         (size_t)2 * kMaxCluster * G::kRows * 8 + sizeof(SmemCtl) + 64;
+}
+
+template <class G>
+int max_active_clusters(int C) {
+  static int cache[kMaxCluster + 1] = {0};
+  if (cache[C] == 0) {
+    const int max_nch = (G::kMaxFeat + 63) / 64;
+    cudaFuncSetAttribute(tc_fused_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)tc_smem_bytes<G>(max_nch));
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = C;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(C * 64, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = tc_smem_bytes<G>(max_nch);
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, tc_fused_kernel<G>, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = kSms / C;
+    }
+    cache[C] = std::min(n, kSms / C);
+  }
+  return cache[C];
+}
+
+TcPlan plan_tc(int variant, int64_t N, int K, int D, bool query_device) {
   TcPlan pl;
-  // cluster size: a power of two so every CTA converts 128/C whole rows
+  pl.diag = variant == kDiag;
+  pl.rows = pl.diag ? DiagCfg::kRows : IsoCfg::kRows;
+  // cluster size: a power of two
   pl.C = 1;
   while (pl.C * kComps < K) pl.C *= 2;
   pl.Kpad = pl.C * kComps;
   pl.Dp = (D + 15) / 16 * 16;
-  pl.nch = (pl.Dp + 63) / 64;
-  pl.num_tiles = (int)((N + kRows - 1) / kRows);
-  pl.smem = tc_smem_bytes(pl.nch);
-  int maxc = kSms / std::max(pl.C, 1);
-  if (query_device && pl.C <= kMaxCluster) {
-    if (g_max_clusters[pl.C] == 0) {
-      cudaFuncSetAttribute(tc_iso_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)tc_smem_bytes(2));
-      cudaLaunchConfig_t cfg = {};
-      cudaLaunchAttribute attr[1];
-      attr[0].id = cudaLaunchAttributeClusterDimension;
-      attr[0].val.clusterDim.x = pl.C;
-      attr[0].val.clusterDim.y = 1;
-      attr[0].val.clusterDim.z = 1;
-      cfg.gridDim = dim3(pl.C * 64, 1, 1);
-      cfg.blockDim = dim3(kThreads, 1, 1);
-      cfg.dynamicSmemBytes = tc_smem_bytes(2);
-      cfg.attrs = attr;
-      cfg.numAttrs = 1;
-      int n = 0;
-      if (cudaOccupancyMaxActiveClusters(&n, tc_iso_kernel, &cfg) != cudaSuccess || n <= 0) {
-        cudaGetLastError();
-        n = kSms / pl.C;
-      }
-      n = std::min(n, kSms / pl.C);
-      g_max_clusters[pl.C] = n;
-    }
-    maxc = g_max_clusters[pl.C];
-  }
+  pl.nfeat = pl.diag ? 2 * pl.Dp : pl.Dp;
+  pl.nch = (pl.nfeat + 63) / 64;
+  pl.num_tiles = (int)((N + pl.rows - 1) / pl.rows);
+  pl.plen = pl.diag ? 1 + 2 * D : D + 2;
+  pl.stage_bytes = (size_t)2 * pl.nch * pl.rows * 128;
+  pl.smem = pl.diag ? tc_smem_bytes<DiagCfg>(pl.nch) : tc_smem_bytes<IsoCfg>(pl.nch);
+  int maxc = kSms / pl.C;
+  if (query_device && pl.C <= kMaxCluster)
+    maxc = pl.diag ? max_active_clusters<DiagCfg>(pl.C) : max_active_clusters<IsoCfg>(pl.C);
   pl.clusters = std::max(1, std::min(maxc, pl.num_tiles));
   return pl;
 }
 
-}  // namespace
-
-bool tc_supported(int variant, const EstepArgs& a, std::string* why) {
-  auto no = [&](const char* m) {
-    if (why) *why = m;
-    return false;
-  };
-  if (variant != kIso) return no("tensor-core path covers the isotropic family");
-  if (a.D > kMaxD) return no("D > 128");
-  if ((a.K + kComps - 1) / kComps > kMaxCluster) return no("K > 1024");
-  return true;
-}
-
-size_t tc_workspace_bytes(int variant, int64_t N, int K, int D) {
-  if (variant != kIso || D > kMaxD || (K + kComps - 1) / kComps > kMaxCluster) return 0;
-  TcPlan pl = plan_tc(N, K, D, false);
-  WsCarve w(nullptr);
-  w.take<int>(64);
-  w.take<__half>((size_t)pl.Kpad * pl.Dp);
-  w.take<__half>((size_t)pl.Kpad * pl.Dp);
-  w.take<float4>(pl.Kpad);
-  // partial rows for the largest cluster count a 148-SM device can run
-  w.take<float>((size_t)(kSms / pl.C) * pl.Kpad * (D + 2));
-  w.take<uint8_t>((size_t)pl.num_tiles * 2 * pl.nch * kChunkBytes);  // split X
-  w.take<float>((size_t)pl.num_tiles * kRows);                          // |x|^2
-  return w.used + 256;
-}
-
-cudaError_t tc_estep(int variant, const EstepArgs& a) {
-  (void)variant;
-  TcPlan pl = plan_tc(a.N, a.K, a.D, true);
-  WsCarve w(a.ws);
-  int* err = w.take<int>(64);
-  __half* Whi = w.take<__half>((size_t)pl.Kpad * pl.Dp);
-  __half* Wlo = w.take<__half>((size_t)pl.Kpad * pl.Dp);
-  float4* consts = w.take<float4>(pl.Kpad);
-  float* part = w.take<float>((size_t)(kSms / pl.C) * pl.Kpad * (a.D + 2));
-  uint8_t* xsplit = w.take<uint8_t>((size_t)pl.num_tiles * 2 * pl.nch * kChunkBytes);
-  float* xsq = w.take<float>((size_t)pl.num_tiles * kRows);
-
-  // err[0]: device error word, err[1]: max|mu| (float bits) for the X scale
-  cudaError_t e = cudaMemsetAsync(err, 0, 2 * sizeof(int), a.stream);
-  if (e != cudaSuccess) return e;
-  tc_prep_kernel<<<pl.Kpad, 128, 0, a.stream>>>(a.mu, a.smk, a.smd, a.cov, a.lpi, a.K, a.D,
-                                                 pl.Dp, Whi, Wlo, consts, err + 1);
-  const int64_t rows_pad = (int64_t)pl.num_tiles * kRows;
-  const int vec_ok = a.sxd == 1 && (reinterpret_cast<uintptr_t>(a.X) & 15) == 0 && a.sxn % 4 == 0;
-  const int sblocks = (int)std::min<int64_t>((rows_pad + 7) / 8, 16 * kSms);
-  tc_split_kernel<<<sblocks, 256, 0, a.stream>>>(a.X, a.sxn, a.sxd, vec_ok, a.N, a.D, pl.Dp,
-                                                  pl.nch, rows_pad, err + 1, xsplit, xsq, err);
-  TcParams p;
-  p.xsplit = xsplit;
-  p.xsq = xsq;
-  p.N = a.N;
-  p.K = a.K;
-  p.D = a.D;
-  p.Dp = pl.Dp;
-  p.nch = pl.nch;
-  p.C = pl.C;
-  p.num_tiles = pl.num_tiles;
-  p.Whi = Whi;
-  p.Wlo = Wlo;
-  p.consts = consts;
-  p.xscale = err + 1;
-  p.logZ = a.logZ;
-  p.part = part;
-  p.err = err;
-
-  e = cudaFuncSetAttribute(tc_iso_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)pl.smem);
+template <class G>
+cudaError_t launch_fused(const TcPlan& pl, const TcParams& p, cudaStream_t stream) {
+  cudaError_t e = cudaFuncSetAttribute(tc_fused_kernel<G>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
@@ -897,19 +1080,123 @@ cudaError_t tc_estep(int variant, const EstepArgs& a) {
   cfg.gridDim = dim3(pl.C * pl.clusters, 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = pl.smem;
-  cfg.stream = a.stream;
+  cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  profile_mark(false, a.stream);
-  e = cudaLaunchKernelEx(&cfg, tc_iso_kernel, p);
-  profile_mark(true, a.stream);
+  profile_mark(false, stream);
+  e = cudaLaunchKernelEx(&cfg, tc_fused_kernel<G>, p);
+  profile_mark(true, stream);
+  return e;
+}
+
+}  // namespace
+
+bool tc_supported(int variant, const EstepArgs& a, std::string* why) {
+  auto no = [&](const char* m) {
+    if (why) *why = m;
+    return false;
+  };
+  if (variant == kIso) {
+    if (a.D > kMaxDIso) return no("D > 128");
+  } else if (variant == kDiag) {
+    if (a.D > kMaxDDiag) return no("D > 96");
+  } else {
+    return no("tensor-core path covers the isotropic and diagonal families");
+  }
+  if ((a.K + kComps - 1) / kComps > kMaxCluster) return no("K > 1024");
+  return true;
+}
+
+size_t tc_workspace_bytes(int variant, int64_t N, int K, int D) {
+  EstepArgs probe{};
+  probe.K = K;
+  probe.D = D;
+  if (!tc_supported(variant, probe, nullptr)) return 0;
+  TcPlan pl = plan_tc(variant, N, K, D, false);
+  WsCarve w(nullptr);
+  w.take<int>(64);
+  if (pl.diag) w.take<float>(pl.Dp);                                   // centre c
+  w.take<__half>((size_t)pl.Kpad * pl.nfeat);
+  w.take<__half>((size_t)pl.Kpad * pl.nfeat);
+  w.take<float4>(pl.Kpad);
+  // partial rows for the largest cluster count a 148-SM device can run
+  w.take<float>((size_t)(kSms / pl.C) * pl.Kpad * pl.plen);
+  w.take<uint8_t>((size_t)pl.num_tiles * pl.stage_bytes);             // split features
+  if (!pl.diag) w.take<float>((size_t)pl.num_tiles * pl.rows);         // |x|^2
+  return w.used + 256;
+}
+
+cudaError_t tc_estep(int variant, const EstepArgs& a) {
+  TcPlan pl = plan_tc(variant, a.N, a.K, a.D, true);
+  WsCarve w(a.ws);
+  int* err = w.take<int>(64);
+  float* cvec = pl.diag ? w.take<float>(pl.Dp) : nullptr;
+  __half* Whi = w.take<__half>((size_t)pl.Kpad * pl.nfeat);
+  __half* Wlo = w.take<__half>((size_t)pl.Kpad * pl.nfeat);
+  float4* consts = w.take<float4>(pl.Kpad);
+  float* part = w.take<float>((size_t)(kSms / pl.C) * pl.Kpad * pl.plen);
+  uint8_t* xsplit = w.take<uint8_t>((size_t)pl.num_tiles * pl.stage_bytes);
+  float* xsq = pl.diag ? nullptr : w.take<float>((size_t)pl.num_tiles * pl.rows);
+
+  // err[0]: device error word, err[1]: max|mu| (iso) or max|mu - c| (diag),
+  // float bits, for the X scale
+  cudaError_t e = cudaMemsetAsync(err, 0, 2 * sizeof(int), a.stream);
   if (e != cudaSuccess) return e;
-  const int64_t total = (int64_t)a.K * (a.D + 2);
-  const int rblocks = (int)std::min<int64_t>((total + 255) / 256, 1024);
-  tc_reduce_kernel<<<rblocks, 256, 0, a.stream>>>(part, pl.clusters, pl.Kpad, a.K, a.D, err,
-                                                   a.Nk, a.mu_acc, a.sig,
-                                                   (a.flags & 1u) ? 1 : 0);
-  count_launches(4);
+  const int64_t rows_pad = (int64_t)pl.num_tiles * pl.rows;
+  const int vec_ok = a.sxd == 1 && (reinterpret_cast<uintptr_t>(a.X) & 15) == 0 && a.sxn % 4 == 0;
+  const int sblocks = (int)std::min<int64_t>((rows_pad + 7) / 8, 16 * kSms);
+  if (pl.diag) {
+    tc_diag_centre_kernel<<<pl.Dp, 256, 0, a.stream>>>(a.mu, a.smk, a.smd, a.K, a.D, cvec,
+                                                       err + 1);
+    tc_prep_diag_kernel<<<pl.Kpad, 128, 0, a.stream>>>(a.mu, a.smk, a.smd, a.cov, a.lpi, cvec,
+                                                       err + 1, a.K, a.D, pl.Dp, Whi, Wlo,
+                                                       consts);
+    tc_split_kernel<DiagCfg::kRows, true><<<sblocks, 256, 0, a.stream>>>(
+        a.X, a.sxn, a.sxd, vec_ok, a.N, a.D, pl.Dp, pl.nch, rows_pad, err + 1, cvec, xsplit,
+        nullptr, err);
+  } else {
+    tc_prep_kernel<<<pl.Kpad, 128, 0, a.stream>>>(a.mu, a.smk, a.smd, a.cov, a.lpi, a.K, a.D,
+                                                   pl.Dp, Whi, Wlo, consts, err + 1);
+    tc_split_kernel<IsoCfg::kRows, false><<<sblocks, 256, 0, a.stream>>>(
+        a.X, a.sxn, a.sxd, vec_ok, a.N, a.D, pl.Dp, pl.nch, rows_pad, err + 1, nullptr, xsplit,
+        xsq, err);
+  }
+  TcParams p;
+  p.xsplit = xsplit;
+  p.xsq = xsq;
+  p.N = a.N;
+  p.K = a.K;
+  p.D = a.D;
+  p.Dp = pl.Dp;
+  p.nfeat = pl.nfeat;
+  p.nch = pl.nch;
+  p.C = pl.C;
+  p.num_tiles = pl.num_tiles;
+  p.Whi = Whi;
+  p.Wlo = Wlo;
+  p.consts = consts;
+  p.xscale = err + 1;
+  p.logZ = a.logZ;
+  p.part = part;
+  p.plen = pl.plen;
+  p.err = err;
+  e = pl.diag ? launch_fused<DiagCfg>(pl, p, a.stream) : launch_fused<IsoCfg>(pl, p, a.stream);
+  if (e != cudaSuccess) return e;
+  const int accumulate = (a.flags & 1u) ? 1 : 0;
+  if (pl.diag) {
+    const int64_t total = (int64_t)a.K * (a.D + 1);
+    const int rblocks = (int)std::min<int64_t>((total + 255) / 256, 1024);
+    tc_reduce_diag_kernel<<<rblocks, 256, 0, a.stream>>>(part, pl.clusters, pl.Kpad, a.K, a.D,
+                                                         cvec, a.mu, a.smk, a.smd, err, a.Nk,
+                                                         a.mu_acc, a.sig, accumulate);
+    count_launches(5);
+  } else {
+    const int64_t total = (int64_t)a.K * (a.D + 2);
+    const int rblocks = (int)std::min<int64_t>((total + 255) / 256, 1024);
+    tc_reduce_kernel<<<rblocks, 256, 0, a.stream>>>(part, pl.clusters, pl.Kpad, a.K, a.D, err,
+                                                     a.Nk, a.mu_acc, a.sig, accumulate);
+    count_launches(4);
+  }
   return cudaGetLastError();
 }
 

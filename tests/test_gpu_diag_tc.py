@@ -1,0 +1,94 @@
+"""Diagonal-covariance tensor-core path (features [(x-c)^2, (x-c)]) against
+the fp64 oracle and the general CUDA-core kernels.
+
+Tolerances: logZ elementwise rel 1e-5, statistics normwise rel 1e-4
+(tests/parity.py)."""
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+import _fgmm_lib as L
+import flash_gmm_diag_h100
+import gmm_data
+from oracle import gmm_oracle as O
+from parity import assert_parity
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _np(out):
+    torch.cuda.synchronize()
+    return tuple(t.detach().cpu().numpy() for t in out)
+
+
+def _case(N, K, D, seed, offset=0.0, spread=2.0):
+    g = torch.Generator().manual_seed(seed)
+    centres = spread * torch.randn(K, D, generator=g) + offset
+    lab = torch.randint(0, K, (N,), generator=g)
+    std = torch.exp(torch.rand(D, generator=g) - 0.5)
+    X = centres[lab] + torch.randn(N, D, generator=g) * std
+    # means near data rows (not equal to them: sig = 0 exactly would make the
+    # normwise relative comparison ill-posed)
+    mu = X[torch.randperm(N, generator=g)[:K]] + 0.3 * torch.randn(K, D, generator=g)
+    lss = 2.0 * torch.rand(K, D, generator=g) - 1.0
+    lpi = torch.log_softmax(torch.randn(K, generator=g), 0)
+    return X, mu, lss, lpi
+
+
+SHAPES = [(1, 1, 1), (257, 3, 5), (3000, 129, 17), (5000, 200, 64), (4000, 1000, 96),
+          (2500, 1024, 80)]
+
+
+@pytest.mark.parametrize("N,K,D", SHAPES)
+def test_tc_diag_vs_oracle_and_general(N, K, D):
+    X, mu, lss, lpi = _case(N, K, D, seed=N + K + D)
+    ref = O.estep_diag(X.numpy(), mu.numpy(), lss.numpy(), lpi.numpy())
+    Xd, mud, lssd, lpid = (t.to(DEV) for t in (X, mu, lss, lpi))
+    tc = _np(flash_gmm_diag_h100.flash_gmm_estep_diag(Xd, mud, lssd, lpid))
+    gen = _np(L.estep(L.FGMM_VARIANT_DIAG, Xd, mud, lssd, lpid, force_general=True))
+    assert_parity(tc, ref, what=f"tc diag {N}x{K}x{D} vs oracle")
+    assert_parity(tc, gen, what=f"tc diag {N}x{K}x{D} vs general")
+
+
+def test_tc_diag_offset_data_and_strided_inputs():
+    """Data far from the origin (all features ~ +60) exercise the centring;
+    X transposed in memory and mu with a row stride exercise the strides."""
+    N, K, D = 6000, 300, 48
+    X, mu, lss, lpi = _case(N, K, D, seed=11, offset=60.0)
+    ref = O.estep_diag(X.numpy(), mu.numpy(), lss.numpy(), lpi.numpy())
+    Xt = X.t().contiguous().to(DEV).t()                     # strides (1, N)
+    mu_big = torch.zeros(K, 2 * D)
+    mu_big[:, :D] = mu
+    mud = mu_big.to(DEV)[:, :D]                             # strides (2D, 1)
+    out = _np(L.estep(L.FGMM_VARIANT_DIAG, Xt, mud, lss.to(DEV), lpi.to(DEV)))
+    assert_parity(out, ref, what="offset diag, strided")
+
+
+def test_tc_diag_neg_inf_weight():
+    N, K, D = 2000, 40, 16
+    X, mu, lss, lpi = _case(N, K, D, seed=3)
+    lpi[5] = -math.inf
+    lpi[17] = -math.inf
+    ref = O.estep_diag(X.numpy(), mu.numpy(), lss.numpy(), lpi.numpy())
+    out = _np(flash_gmm_diag_h100.flash_gmm_estep_diag(*(t.to(DEV) for t in (X, mu, lss, lpi))))
+    assert_parity(out, ref, what="diag -inf log_pi")
+    assert out[1][5] == 0.0 and out[1][17] == 0.0
+
+
+def test_c3_full_size():
+    """C3 at full size (N=1M, K=1024, D=96) against the fp64 oracle, plus
+    sum_k Nk = N and sum_k mu_acc = sum_n x_n."""
+    X, mu, lss, lpi = gmm_data.make_config("c3", device=DEV)
+    out = _np(flash_gmm_diag_h100.flash_gmm_estep_diag(X, mu, lss, lpi))
+    logZ, Nk, mu_acc, sig = out
+    N = X.shape[0]
+    assert abs(Nk.astype(np.float64).sum() - N) <= 1e-5 * N
+    xs = X.double().sum(0).cpu().numpy()
+    np.testing.assert_allclose(mu_acc.astype(np.float64).sum(0), xs,
+                               atol=1e-4 * np.abs(mu_acc).max() * 4)
+    ref = O.estep_diag(X.cpu().numpy(), mu.cpu().numpy(), lss.cpu().numpy(), lpi.cpu().numpy())
+    assert_parity(out, ref, what="C3 full size")
