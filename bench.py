@@ -1,7 +1,7 @@
 """Benchmark of the B200 GMM E-step (contract: one JSON line from rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload c2|c5]
+                    [--workload c2|c3|c4|c5]
 
 Metric: E-step (sample x component)/s = N*K / seconds per E-step, the
 reference's headline shape N=1M, K=1024, D=128.
@@ -11,6 +11,9 @@ reference's headline shape N=1M, K=1024, D=128.
   global rows [r*1M, (r+1)*1M)), so per-GPU work is fixed as N grows
   ("scaling": "weak").  One step = the E-step on each rank + ONE NCCL
   all-reduce of the packed [Nk | mu_acc | sig_acc] statistics.
+* ``--workload c3`` / ``c4``: the diagonal (N=1M, K=1024, D=96) and full
+  covariance (N=250K, K=256, D=64) configurations per rank, from the seeded
+  recipes of ``gmm_data`` (weak scaling; the same rows on every rank).
 * ``--workload c5``: N = 100M rows in total (config 5), split across the ranks
   ("scaling": "strong"); each rank runs the E-step over its rows in 10M-row
   chunks with FGMM_FLAG_ACCUMULATE, then one all-reduce.
@@ -20,9 +23,10 @@ reference's headline shape N=1M, K=1024, D=128.
   bounded sample of rows per step.  Rank 0 runs it; other ranks exit.
 
 Timing: W untimed warm-up steps, then K steps between a barrier +
-cuda.synchronize on both sides, CUDA events on the launching stream, max over
-ranks.  Inputs (512 MB of X per rank) exceed the 126 MB L2, so no flush is
-needed between steps.
+cuda.synchronize on both sides, CUDA events on the launching stream (one
+pair per step), max over ranks.  Inputs of C2/C3/C5 (384-512 MB of X per
+rank) exceed the 126 MB L2; for C4 (64 MB) a 256 MB buffer is rewritten
+between the timed steps.
 """
 
 from __future__ import annotations
@@ -45,11 +49,33 @@ for _p in (ROOT, PKG):
 
 METRIC = "estep_pairs_per_s"
 UNIT = "(sample x component)/s"
-K_COMP, D_FEAT = 1024, 128
-ROWS_C2 = 1_000_000
 ROWS_C5 = 100_000_000
 C5_CHUNK = 10_000_000
 SEED = 1234
+
+# Benchmark workloads.  flops_per_pair is the
+# algorithmic work per (row, component) pair: iso 4D, diag 8D, full 4D^2 + 2D.
+WORKLOADS = {
+    "c2": dict(kind="iso", rows=1_000_000, K=1024, D=128, scaling="weak",
+               title="C2 isotropic E-step N=1M K=1024 D=128 per GPU",
+               profile="tc_iso_kernel_c2.txt", kernel="tc_fused_kernel<iso> "
+               "(fused distance/LSE/statistics, tcgen05)"),
+    "c3": dict(kind="diag", rows=1_000_000, K=1024, D=96, scaling="weak",
+               title="C3 diagonal-covariance E-step N=1M K=1024 D=96 per GPU",
+               profile="tc_diag_kernel_c3.txt", kernel="tc_fused_kernel<diag> "
+               "(fused distance/LSE/statistics, tcgen05)"),
+    "c4": dict(kind="full", rows=250_000, K=256, D=64, scaling="weak",
+               title="C4 full-covariance E-step N=250K K=256 D=64 per GPU",
+               profile="full_kernel_c4.txt", kernel="full-covariance statistics pass"),
+    "c5": dict(kind="iso", rows=ROWS_C5, K=1024, D=128, scaling="strong",
+               title="C5 streaming isotropic E-step N=100M K=1024 D=128 total",
+               profile="tc_iso_kernel_c2.txt", kernel="tc_fused_kernel<iso> "
+               "(fused distance/LSE/statistics, tcgen05), one 10M-row chunk"),
+}
+
+
+def flops_per_pair(kind: str, D: int) -> float:
+    return {"iso": 4.0 * D, "diag": 8.0 * D, "full": 4.0 * D * D + 2.0 * D}[kind]
 
 
 def load_peaks():
@@ -65,9 +91,9 @@ def load_peaks():
                 "source": "fallback"}
 
 
-def profile_traffic(name: str):
+def profile_traffic(profile: str, name: str = "dram_bytes_per_launch"):
     """dram bytes per launch from a committed ncu summary (``key: value``)."""
-    path = os.path.join(ROOT, "profiles", "tc_iso_kernel_c2.txt")
+    path = os.path.join(ROOT, "profiles", profile)
     try:
         for line in open(path):
             if line.startswith(name + ":"):
@@ -138,17 +164,26 @@ def dist_setup():
     return world, rank, local
 
 
-def cpu_reference_rate(X, mu, lss, lpi, budget_s: float, chunk: int = 65536):
+CPU_PORT = {"iso": "estep_iso_cpu_fp32", "diag": "estep_diag_cpu_fp32",
+            "full": "estep_full_cpu_fp32"}
+
+
+def cpu_port(kind: str):
+    from oracle import gmm_oracle as O
+    return getattr(O, CPU_PORT[kind])
+
+
+def cpu_reference_rate(kind, X, mu, cov, lpi, budget_s: float, chunk: int = 16384):
     """Pairs/s of the CPU restatement (fp32 torch-CPU) over a bounded sample."""
     import torch
-    from oracle import gmm_oracle as O
+    fn = cpu_port(kind)
     torch.set_num_threads(os.cpu_count() or 1)
     n_done = 0
     t0 = time.perf_counter()
     start = 0
     while True:
         xs = X[start:start + chunk]
-        O.estep_iso_cpu_fp32(xs, mu, lss, lpi, chunk=chunk)
+        fn(xs, mu, cov, lpi, chunk=chunk)
         n_done += xs.shape[0]
         start = (start + chunk) % max(1, X.shape[0] - chunk)
         if time.perf_counter() - t0 >= budget_s:
@@ -157,11 +192,14 @@ def cpu_reference_rate(X, mu, lss, lpi, budget_s: float, chunk: int = 65536):
     return n_done * mu.shape[0] / dt, n_done, dt
 
 
-def host_sample(rows: int, seed: int = SEED):
-    """CPU copy of `rows` rows of the benchmark mixture (same recipe)."""
-    import torch
+def host_sample(w: dict, rows: int):
+    """CPU rows of the workload's mixture (same recipe, seeded)."""
     import gmm_data
-    return gmm_data.iso_mixture(rows, K_COMP, D_FEAT, seed=seed)
+    if w["kind"] == "iso":
+        return gmm_data.iso_mixture(rows, w["K"], w["D"], seed=SEED)
+    if w["kind"] == "diag":
+        return gmm_data.diag_mixture(rows, w["K"], w["D"])
+    return gmm_data.full_mixture(rows, w["K"], w["D"])
 
 
 def run_reference(args):
@@ -169,31 +207,32 @@ def run_reference(args):
     if rank != 0:
         return 0
     import torch
+    w = WORKLOADS[args.workload]
+    K = w["K"]
     cores = os.cpu_count() or 1
     torch.set_num_threads(cores)
-    rows = 65536
-    X, mu, lss, lpi = host_sample(4 * rows)
-    from oracle import gmm_oracle as O
+    rows = {"iso": 65536, "diag": 65536, "full": 8192}[w["kind"]]
+    X, mu, cov, lpi = host_sample(w, 4 * rows)
+    fn = cpu_port(w["kind"])
     for _ in range(max(args.warmup, 0)):
-        O.estep_iso_cpu_fp32(X[:rows], mu, lss, lpi)
+        fn(X[:rows], mu, cov, lpi)
     times = []
     for s in range(args.steps):
         xs = X[(s % 4) * rows:(s % 4 + 1) * rows]
         t0 = time.perf_counter()
-        O.estep_iso_cpu_fp32(xs, mu, lss, lpi)
+        fn(xs, mu, cov, lpi)
         times.append(time.perf_counter() - t0)
     sec = sum(times) / len(times)
-    value = rows * K_COMP / sec
+    value = rows * K / sec
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic (seeded C2 mixture rows on the host)",
-        "config": {"workload": "C2 isotropic E-step, K=1024, D=128; each step a 65,536-row "
-                               "sample on the host CPU", "K": K_COMP, "D": D_FEAT,
-                   "rows_per_step": rows},
+        "higher_is_better": True, "scaling": w["scaling"], "vs_baseline": None, "dtype": "f32",
+        "data": f"synthetic (seeded {args.workload.upper()} mixture rows on the host)",
+        "config": {"workload": f"{w['title']}; each step a {rows:,}-row sample on the host CPU",
+                   "K": K, "D": w["D"], "rows_per_step": rows},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
-                         "sample": f"{rows} rows x {K_COMP} components per step, torch-CPU fp32"},
+                         "sample": f"{rows} rows x {K} components per step, torch-CPU fp32"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "the reference is Triton-only (GPU); this arm runs its algorithm's CPU "
                 "restatement from oracle/ on all host threads",
@@ -208,7 +247,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["c2", "c5"], default="c2")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="c2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     args = ap.parse_args()
@@ -221,6 +260,9 @@ def main():
 
     import _fgmm_lib as L
     import flash_gmm
+    import flash_gmm_diag_h100
+    import flash_gmm_full_h100
+    import gmm_data
     import gmm_stream as GS
 
     world, rank, local = dist_setup()
@@ -231,34 +273,45 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=dev)
 
-    K, D = K_COMP, D_FEAT
-    centres = GS.mixture_centres(K, D, SEED, dev)
-    if args.workload == "c2":
-        n_global = ROWS_C2 * world
-        lo, hi = rank * ROWS_C2, (rank + 1) * ROWS_C2
-        chunk = hi - lo
-        scaling = "weak"
-    else:
+    w = WORKLOADS[args.workload]
+    kind, K, D = w["kind"], w["K"], w["D"]
+    variant = {"iso": L.FGMM_VARIANT_ISO, "diag": L.FGMM_VARIANT_DIAG,
+               "full": L.FGMM_VARIANT_FULL}[kind]
+    if args.workload == "c5":
         n_global = ROWS_C5
         lo, hi = GS.shard_rows(n_global, rank, world)
         chunk = C5_CHUNK
-        scaling = "strong"
+    else:
+        n_global = w["rows"] * world
+        lo, hi = rank * w["rows"], (rank + 1) * w["rows"]
+        chunk = hi - lo
     n_local = hi - lo
-    X = torch.empty(n_local, D, device=dev, dtype=torch.float32)
-    for s in range(0, n_local, C5_CHUNK):
-        GS.generate_rows(lo + s, min(C5_CHUNK, n_local - s), centres, SEED, out=X[s:s + C5_CHUNK])
-    mu = GS.generate_row_ids(GS.pick_mean_rows(min(n_global, ROWS_C2), K, SEED).to(dev),
-                             centres, SEED)
-    lss = torch.zeros(K, device=dev)
-    lpi = torch.full((K,), -math.log(K), device=dev)
+    if kind == "iso":
+        # rows of the C2 mixture keyed by global row index (rank r owns its own rows)
+        centres = GS.mixture_centres(K, D, SEED, dev)
+        X = torch.empty(n_local, D, device=dev, dtype=torch.float32)
+        for s in range(0, n_local, C5_CHUNK):
+            GS.generate_rows(lo + s, min(C5_CHUNK, n_local - s), centres, SEED,
+                             out=X[s:s + C5_CHUNK])
+        mu = GS.generate_row_ids(GS.pick_mean_rows(min(n_global, 1_000_000), K, SEED).to(dev),
+                                 centres, SEED)
+        cov = torch.zeros(K, device=dev)
+        lpi = torch.full((K,), -math.log(K), device=dev)
+        data = ("synthetic: C2 mixture (centres ~ N(0,4I), rows = centre + N(0,I)) generated "
+                "on device by row-keyed counter RNG; mu = 1024 rows of X")
+    else:
+        # the seeded config recipe (gmm_data), the same rows on every rank
+        X, mu, cov, lpi = gmm_data.make_config(args.workload, device=dev)
+        data = (f"synthetic: seeded {args.workload.upper()} recipe (gmm_data.make_config) "
+                "generated on device; every rank holds the same rows")
 
-    buf, (Nk, mu_acc, sig) = GS.packed_stats("iso", K, D, dev)
+    buf, (Nk, mu_acc, sig) = GS.packed_stats(kind, K, D, dev)
     logZ = torch.empty(n_local, device=dev)
 
     def step():
         for s in range(0, n_local, chunk):
             e = min(n_local, s + chunk)
-            L.estep(L.FGMM_VARIANT_ISO, X[s:e], mu, lss, lpi,
+            L.estep(variant, X[s:e], mu, cov, lpi,
                     out=(logZ[s:e], Nk, mu_acc, sig), accumulate=s > 0)
         if world > 1:
             dist.all_reduce(buf)
@@ -268,7 +321,7 @@ def main():
         step()
     torch.cuda.synchronize(dev)
 
-    # profiling events around the dominant (fused tensor-core) kernel
+    # profiling events around the dominant kernel of each E-step call
     ev_pairs = []
     sampler = ClockSampler(local)
     launches0 = L.launch_count()
@@ -276,25 +329,34 @@ def main():
         dist.barrier()
     torch.cuda.synchronize(dev)
     sampler.start()
-    t_start = torch.cuda.Event(enable_timing=True)
-    t_stop = torch.cuda.Event(enable_timing=True)
-    t_start.record(stream)
+    # X smaller than L2 (C4: 64 MB): each step is timed on its own and a
+    # 256 MB buffer is rewritten between steps, outside the timed spans
+    flush = None
+    if n_local * D * 4 < (192 << 20):
+        flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    step_ev = []
     for _ in range(args.steps):
+        if flush is not None:
+            flush.fill_(1)
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
         a = torch.cuda.Event(enable_timing=True)
         b = torch.cuda.Event(enable_timing=True)
         a.record(stream)
         b.record(stream)  # materialise both events before handing them to the library
+        t0.record(stream)
         L.set_profile_events(a, b)
         step()
         L.set_profile_events(None, None)
+        t1.record(stream)
         ev_pairs.append((a, b))
-    t_stop.record(stream)
+        step_ev.append((t0, t1))
     torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
     clocks = sampler.stop()
     launches = L.launch_count() - launches0
-    ms_total = t_start.elapsed_time(t_stop)
+    ms_total = sum(t0.elapsed_time(t1) for t0, t1 in step_ev)
     kern_ms = [a.elapsed_time(b) for a, b in ev_pairs]
     ms_step = ms_total / args.steps
     kern_avg = sum(kern_ms) / len(kern_ms)
@@ -307,22 +369,26 @@ def main():
     value = pairs_step / (ms_step * 1e-3)
 
     # ---- end to end through the public API: host X (pinned) -> device ->
-    # flash_gmm_estep -> results read back, every step (rank 0's shard size)
+    # the reference-named entry point -> results read back, every step
     e2e = None
-    if not args.no_e2e and args.workload == "c2":
+    if not args.no_e2e and args.workload != "c5":
+        entry = {"iso": flash_gmm.flash_gmm_estep,
+                 "diag": flash_gmm_diag_h100.flash_gmm_estep_diag,
+                 "full": flash_gmm_full_h100.flash_gmm_estep_full}[kind]
         Xh = X.cpu().pin_memory()
+        n_sig = {"iso": K, "diag": K * D, "full": K * D * D}[kind]
         out_host = [torch.empty(n_local, pin_memory=True), torch.empty(K, pin_memory=True),
-                    torch.empty(K, D, pin_memory=True), torch.empty(K, pin_memory=True)]
+                    torch.empty(K * D, pin_memory=True), torch.empty(n_sig, pin_memory=True)]
         Xd = torch.empty_like(X)
 
         def e2e_step():
             Xd.copy_(Xh, non_blocking=True)
-            res = flash_gmm.flash_gmm_estep(Xd, mu, lss, lpi)
+            res = entry(Xd, mu, cov, lpi)
             if world > 1:
-                packed = torch.cat([res[1], res[2].reshape(-1), res[3]])
+                packed = torch.cat([res[1], res[2].reshape(-1), res[3].reshape(-1)])
                 dist.all_reduce(packed)
             for h, r in zip(out_host, res):
-                h.copy_(r, non_blocking=True)
+                h.copy_(r.reshape(-1), non_blocking=True)
 
         for _ in range(2):
             e2e_step()
@@ -343,36 +409,40 @@ def main():
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             ms_e2e = float(t[0])
         h2d = X.numel() * 4
-        d2h = (n_local + K + K * D + K) * 4
+        d2h = (n_local + K + K * D + n_sig) * 4
         e2e = {"value": pairs_step / (ms_e2e * 1e-3), "unit": UNIT, "h2d_bytes_per_step": h2d,
                "d2h_bytes_per_step": d2h, "ms_per_step": ms_e2e,
-               "path": "pinned host X -> device, flash_gmm.flash_gmm_estep, outputs -> host"}
+               "path": "pinned host X -> device, " + entry.__module__ + "." + entry.__name__
+                       + ", outputs -> host"}
 
     # ---- roofline of the dominant kernel
     peaks = load_peaks()
-    flops_launch = 4.0 * D * (chunk if args.workload == "c5" else n_local) * K
-    # the events bracket the last fused-kernel launch of each step (one launch
-    # per step for c2; the last chunk's launch for c5)
+    fpp = flops_per_pair(kind, D)
+    flops_launch = fpp * chunk * K
+    # the events bracket the last dominant-kernel launch of each step (one
+    # E-step call per step, except c5: the last chunk's call)
     kern_launch_ms = kern_avg
     achieved = flops_launch / (kern_launch_ms * 1e-3) / 1e12
-    traffic = profile_traffic("dram_bytes_per_launch")
+    traffic = profile_traffic(w["profile"])
     roofline = {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
                 "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
                 "traffic": traffic, "peak_source": peaks["source"] + " bf16 burst",
-                "kernel": "tc_iso_kernel (fused distance/LSE/statistics)",
+                "kernel": w["kernel"],
                 "algorithmic_flops_per_launch": flops_launch,
                 "kernel_ms_per_launch": kern_launch_ms}
     # north-star roofline: max(tensor time at TF32 peak = bf16/2, exp time at MUFU peak)
     p_tf32 = peaks["bf16_tflops"] / 2
     p_mufu = 148 * 16 * 1.965e9
-    t_tc = 4.0 * D * pairs_step / world / (p_tf32 * 1e12)
+    t_tc = fpp * pairs_step / world / (p_tf32 * 1e12)
     t_exp = pairs_step / world / p_mufu
     t_roof = max(t_tc, t_exp)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        Xc, muc, lssc, lpic = X[:262144].cpu(), mu.cpu(), lss.cpu(), lpi.cpu()
-        rate, nrows, secs = cpu_reference_rate(Xc, muc, lssc, lpic, budget_s=12.0)
+        ncpu = min(n_local, 262144)
+        Xc, muc, covc, lpic = X[:ncpu].cpu(), mu.cpu(), cov.cpu(), lpi.cpu()
+        rate, nrows, secs = cpu_reference_rate(kind, Xc, muc, covc, lpic, budget_s=12.0,
+                                               chunk=16384 if kind != "full" else 4096)
         cpu = {"value": rate, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
                "sample": f"{nrows} rows x {K} components of the same workload in {secs:.1f} s, "
                          "torch-CPU fp32 restatement (oracle/)"}
@@ -380,15 +450,15 @@ def main():
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
-        "scaling": scaling, "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic: C2 mixture (centres ~ N(0,4I), rows = centre + N(0,I)) generated "
-                "on device by row-keyed counter RNG; mu = 1024 rows of X",
-        "config": {"workload": ("C2 isotropic E-step N=1M K=1024 D=128 per GPU"
-                                if args.workload == "c2" else
-                                "C5 streaming isotropic E-step N=100M K=1024 D=128 total"),
-                   "N_global": n_global, "N_per_rank": n_local, "K": K, "D": D,
+        "scaling": w["scaling"], "vs_baseline": None, "dtype": "f32",
+        "data": data,
+        "config": {"workload": w["title"], "N_global": n_global, "N_per_rank": n_local, "K": K,
+                   "D": D, "covariance": kind,
                    "parallelism": f"dp{world} (rows sharded, one NCCL all-reduce of stats)",
-                   "l2": "inputs larger than L2 (X = %d MB per rank)" % (n_local * D * 4 >> 20)},
+                   "l2": ("inputs larger than L2 (X = %d MB per rank)" % (n_local * D * 4 >> 20)
+                          if flush is None else
+                          "X = %d MB fits L2: 256 MB buffer rewritten between timed steps"
+                          % (n_local * D * 4 >> 20))},
         "roofline": roofline,
         "north_star_roofline": {"t_tensor_ms": t_tc * 1e3, "t_exp_ms": t_exp * 1e3,
                                 "t_roof_ms": t_roof * 1e3, "frac": t_roof / (ms_step * 1e-3),

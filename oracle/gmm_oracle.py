@@ -212,3 +212,61 @@ def estep_iso_cpu_fp32(X, mu, log_sigma_sq, log_pi, chunk: int = 65536):
         mu_acc += r.T @ xs
         sig += (r * sq).sum(0)
     return logZ, Nk, mu_acc, sig
+
+
+def estep_diag_cpu_fp32(X, mu, log_sigma_sq, log_pi, chunk: int = 65536):
+    """fp32 torch-CPU restatement of flash_gmm_diag_h100.py:332-339, 116-119
+    (ll2 = c0 - x^2 . inv^T + 2 x . (mu*inv)^T) and 258-260 (sig from raw
+    moments)."""
+    import torch
+    N, D = X.shape
+    K = mu.shape[0]
+    mu = mu.float()
+    lss = log_sigma_sq.float()
+    inv = torch.exp(-lss)
+    const = log_pi.float() - 0.5 * (D * LOG_2PI + lss.sum(1)) - 0.5 * (mu * mu * inv).sum(1)
+    w = mu * inv
+    logZ = torch.empty(N)
+    Nk = torch.zeros(K)
+    mu_acc = torch.zeros(K, D)
+    rx2 = torch.zeros(K, D)
+    for s in range(0, N, chunk):
+        xs = X[s:s + chunk].float()
+        x2 = xs * xs
+        ll = const[None, :] - 0.5 * (x2 @ inv.T) + xs @ w.T
+        lz = torch.logsumexp(ll, dim=1)
+        r = torch.exp(ll - lz[:, None])
+        logZ[s:s + chunk] = lz
+        Nk += r.sum(0)
+        mu_acc += r.T @ xs
+        rx2 += r.T @ x2
+    sig = rx2 - 2.0 * mu * mu_acc + mu * mu * Nk[:, None]
+    return logZ, Nk, mu_acc, sig
+
+
+def estep_full_cpu_fp32(X, mu, prec_chol, log_pi, chunk: int = 16384):
+    """fp32 torch-CPU restatement of flash_gmm_full_h100.py:288-296, 124-129
+    (maha = ||L_k^T (x - mu_k)||^2) and 213-228 (sig_outer = sum r x x^T)."""
+    import torch
+    N, D = X.shape
+    K = mu.shape[0]
+    mu = mu.float()
+    L = prec_chol.float()
+    log_diag = torch.log(torch.diagonal(L, dim1=1, dim2=2).abs() + 1e-30).sum(1)
+    c = log_pi.float() + log_diag - 0.5 * D * LOG_2PI
+    b = torch.einsum("kd,kde->ke", mu, L)          # (L_k^T mu_k)^T
+    logZ = torch.empty(N)
+    Nk = torch.zeros(K)
+    mu_acc = torch.zeros(K, D)
+    sig = torch.zeros(K, D, D)
+    for s in range(0, N, chunk):
+        xs = X[s:s + chunk].float()
+        v = torch.einsum("nd,kde->nke", xs, L) - b[None]   # (n, K, D)
+        ll = c[None, :] - 0.5 * (v * v).sum(2)
+        lz = torch.logsumexp(ll, dim=1)
+        r = torch.exp(ll - lz[:, None])
+        logZ[s:s + chunk] = lz
+        Nk += r.sum(0)
+        mu_acc += r.T @ xs
+        sig += torch.einsum("nk,ni,nj->kij", r, xs, xs)
+    return logZ, Nk, mu_acc, sig
