@@ -114,21 +114,27 @@ class ClockSampler:
         self.gpu = gpu_index
         self.proc = None
         self.tmp = None
+        self.skip = 0
 
     def start(self):
         try:
             self.tmp = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
+                 "--format=csv,noheader,nounits", "-lms", "20"],
                 stdout=self.tmp, stderr=subprocess.DEVNULL)
+            # the timed region starts once the sampler is producing lines
+            t0 = time.time()
+            while time.time() - t0 < 5.0 and os.path.getsize(self.tmp.name) == 0:
+                time.sleep(0.02)
+            self.skip = sum(1 for _ in open(self.tmp.name))
         except Exception:
             self.proc = None
 
     def stop(self):
         if self.proc is None:
             return None
-        time.sleep(0.15)
+        time.sleep(0.05)
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
@@ -137,6 +143,7 @@ class ClockSampler:
         self.tmp.flush()
         self.tmp.seek(0)
         rows = [r.split(",") for r in self.tmp.read().strip().splitlines() if r.strip()]
+        rows = rows[self.skip:] or rows[-1:]  # samples taken after the timed region began
         os.unlink(self.tmp.name)
         sm = []
         smax = None

@@ -59,6 +59,16 @@ bool tc_supported(int variant, const EstepArgs& a, std::string* why);
 size_t tc_workspace_bytes(int variant, int64_t N, int K, int D);
 cudaError_t tc_estep(int variant, const EstepArgs& a);
 
+// Tensor-core full-covariance path (fgmm_tc_full.cu).
+bool full_tc_supported(const EstepArgs& a);
+size_t full_tc_workspace_bytes(int64_t N, int K, int D);
+cudaError_t full_tc_estep(const EstepArgs& a);
+
+// c_d = mean_k mu_kd (0 for d >= D) and *amax |= max |mu_kd - c_d| (float
+// bits, atomicMax; *amax must start at 0).  Grid: Dp blocks of 256 threads.
+__global__ void centre_kernel(const float* __restrict__ mu, int64_t smk, int64_t smd, int K,
+                              int D, float* __restrict__ cvec, int* __restrict__ amax);
+
 // Row generator for the streaming configuration.
 cudaError_t generate_iso_rows(float* X, const int64_t* row_ids, int64_t row0,
                               int64_t nrows, int D, const float* centres, int K,

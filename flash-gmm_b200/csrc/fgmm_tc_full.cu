@@ -1,0 +1,863 @@
+// Tensor-core (tcgen05 / TMEM) full-covariance E-step for sm_100a, D <= 64.
+//
+// The reference evaluates the Mahalanobis term with one (BLOCK_N x D) x
+// (D x D) dot per component and d2 slice (flash_gmm_full_h100.py:71-139) and
+// accumulates sig_outer with per-d2 outer products and atomics (full:146-228).
+// Here the E-step is two tensor-core passes plus small set-up / reduction
+// kernels:
+//
+// Pass 1 (full_ll_kernel, rows on TMEM lanes): for a 128-row tile of
+//   x~ = x - c (c = mean of the means), V = x~ [L_G1 | L_G2 | ...] is one
+//   M=128, N=G*Dp (256 for D=64: 4 components), K=Dp GEMM per group of G
+//   components, A = the x~ tile and B = the group's L columns, both fp16 hi/lo
+//   in shared memory (three passes lo*hi + hi*lo + hi*hi, 22-bit operands).
+//   The epilogue (thread = row) forms v = V - b_k (b_k = (mu_k - c)^T L_k),
+//   maha = |v|^2, ll2 = const_k - maha/2 * log2 e (full:124-129, 289-296, log2
+//   units), keeps an online log-sum-exp per row and writes ll2 for pass 2.
+//   Two accumulators (2 x 256 TMEM columns) let the MMAs of group g+1 run
+//   while the epilogue drains group g.
+//
+// Pass 2 (full_stats_kernel, components on TMEM lanes): per 64-row chunk,
+//   T[k, f] += sum_n r_nk z_nf with z = [x~_i x~_j (i <= j), x~_i, 1]
+//   (D(D+1)/2 + D + 1 features; the last two give mu_acc and Nk).  A = R^T
+//   (fp16 hi/lo written to TMEM from ll2 and logZ), B = the z chunk (fp16
+//   hi/lo, generated on chip from x~ into the MN-major shared-memory layout),
+//   N = 256 features per CTA.  CTAs tile (feature block, component block,
+//   row slab); partials are reduced in slab order (deterministic).
+//
+// Every wait is bounded (timeout -> error word -> NaN outputs).
+#include <cuda_fp16.h>
+#include <math.h>
+
+#include <algorithm>
+
+#include "fgmm_internal.cuh"
+#include "fgmm_ptx.cuh"
+
+namespace fgmm {
+namespace {
+
+constexpr int kFullMaxD = 64;
+constexpr int kSmsFull = 148;
+
+// ---- pass 1
+constexpr int kP1Rows = 128;
+constexpr int kP1EpiWarps = 8;               // two warps per TMEM lane quadrant
+constexpr int kP1LoadWarp = 8;
+constexpr int kP1MmaWarp = 9;
+constexpr int kP1Threads = 10 * 32;
+constexpr int kP1LStages = 2;
+constexpr int kXTile = kP1Rows * 128;        // 16 KB: one hi (or lo) x~ tile, 64 features
+constexpr int kLGroup = 256 * 128;           // 32 KB: one hi (or lo) group of L columns
+
+// ---- pass 2
+constexpr int kP2Rows = 64;                  // rows per chunk (MMA K extent)
+constexpr int kP2Feat = 256;                 // features per CTA (MMA N)
+constexpr int kP2Comps = 128;                // components per CTA (TMEM lanes, MMA M)
+constexpr int kP2RWarps = 4;                 // warps 0-3: R^T (thread = component)
+constexpr int kP2ZWarps = 8;                 // warps 4-11: z chunks
+constexpr int kP2MmaWarp = 12;
+constexpr int kP2Threads = 13 * 32;
+constexpr int kZChunk = kP2Rows * 128;       // 8 KB: 64 rows x 64 features (fp16)
+constexpr int kZStage = 2 * 4 * kZChunk;     // hi + lo, 256 features: 64 KB
+constexpr int kXsStride = 68;                // floats per staged x~ row (D + one + zero, padded)
+constexpr uint32_t kColT2 = 0;               // statistics accumulator, 256 columns
+constexpr uint32_t kColR2 = 256;             // 2 x (R^T hi 32 + lo 32 columns)
+
+struct P1Params {
+  const uint8_t* xsplit;   // [num_tiles][hi 16 KB | lo 16 KB]  x~ 2^-a1, swizzled K-major
+  const uint8_t* lgroups;  // [num_groups][hi 32 KB | lo 32 KB] L columns 2^-s_k, K-major
+  const float* bvec;       // [Kpad][Dp]  b_k = (mu_k - c)^T L_k
+  const float2* kconst;    // [Kpad]  {const_k in log2 units, s_k}
+  const int* amax;         // max|mu - c| (float bits) -> a1
+  int64_t N;
+  int K, Dp, G, num_groups, num_tiles;
+  int64_t ld_ll;           // row stride of ll2 (= num_tiles * 128)
+  float* ll2;              // [Kpad][ld_ll]
+  float* lz2;              // [ld_ll]  logZ in log2 units (for pass 2)
+  float* logZ;             // [N]      natural log
+  int* err;
+};
+
+struct __align__(8) P1Ctl {
+  uint64_t xfull[2], xempty[2];
+  uint64_t lfull[kP1LStages], lempty[kP1LStages];
+  uint64_t afull[2], aempty[2];
+  uint64_t lse_bar;
+  uint32_t tmem_base;
+  volatile int abort_flag;
+};
+
+struct P2Params {
+  const float* X;
+  int64_t sxn, sxd;
+  const float* cvec;
+  const float* ll2;
+  int64_t ld_ll;
+  const float* lz2;
+  const int* amax;
+  int64_t N;
+  int K, Kll, D, nf, nfb, ncb, slabs;
+  int64_t rows_per_slab;   // multiple of 64
+  float* part;             // [slabs][ncb*128][nfb*256]
+  int* err;
+};
+
+struct __align__(8) P2Ctl {
+  uint64_t zfull[2], zempty[2], rfull[2], rempty[2], tdone;
+  uint32_t tmem_base;
+  volatile int abort_flag;
+};
+
+__device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                       uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
+  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
+}
+
+// ---------------------------------------------------------------------------
+// Prep, one block per component k < Kpad (64 threads; thread e = output index):
+//   s_k from max|L_k| (exact power of two), group layout of the L columns
+//   (row (k % G)*Dp + e of group k/G holds L_k[:, e] 2^-s_k, fp16 hi/lo),
+//   b_k[e] = sum_d (mu_kd - c_d) L_k[d, e],
+//   const_k = (log pi_k + sum_d log(|L_kdd| + 1e-30) - D/2 log 2pi) log2 e.
+// Components >= K get zero columns and const = -1e30.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(64) full_prep_kernel(
+    const float* __restrict__ mu, int64_t smk, int64_t smd, const float* __restrict__ L,
+    const float* __restrict__ lpi, const float* __restrict__ cvec, int K, int D, int Dp, int G,
+    uint8_t* __restrict__ lgroups, float* __restrict__ bvec, float2* __restrict__ kconst) {
+  const int k = blockIdx.x;
+  const int e = threadIdx.x;
+  const bool valid = k < K;
+  const bool col = valid && e < D;
+  const float* Lk = L + (size_t)k * D * D;
+  float lmax = 0.f;
+  double b = 0.0, logd = 0.0;
+  if (col) {
+    for (int d = 0; d < D; ++d) {
+      const float v = Lk[(size_t)d * D + e];
+      lmax = fmaxf(lmax, fabsf(v));
+      b += ((double)mu[(int64_t)k * smk + (int64_t)d * smd] - (double)cvec[d]) * (double)v;
+    }
+    logd = log(fabs((double)Lk[(size_t)e * D + e]) + 1e-30);
+  }
+  __shared__ float s_max[2];
+  __shared__ double s_logd[2];
+  for (int o = 16; o > 0; o >>= 1) {
+    lmax = fmaxf(lmax, __shfl_xor_sync(0xffffffffu, lmax, o));
+    logd += __shfl_xor_sync(0xffffffffu, logd, o);
+  }
+  if ((threadIdx.x & 31) == 0) {
+    s_max[threadIdx.x >> 5] = lmax;
+    s_logd[threadIdx.x >> 5] = logd;
+  }
+  __syncthreads();
+  const int sk = scale_exp_to(fmaxf(s_max[0], s_max[1]), 5);
+  if (e < Dp) {
+    uint8_t* grp = lgroups + (size_t)(k / G) * 2 * kLGroup;
+    const int rr = (k % G) * Dp + e;
+    for (int d0 = 0; d0 < 64; d0 += 8) {
+      uint32_t hi[4], lo[4];
+      for (int u = 0; u < 8; u += 2) {
+        const float v0 = (col && d0 + u < D) ? ldexpf(Lk[(size_t)(d0 + u) * D + e], -sk) : 0.f;
+        const float v1 =
+            (col && d0 + u + 1 < D) ? ldexpf(Lk[(size_t)(d0 + u + 1) * D + e], -sk) : 0.f;
+        split2(v0, v1, hi[u / 2], lo[u / 2]);
+      }
+      const uint32_t off = xoff(rr, d0, kLGroup);
+      *reinterpret_cast<uint4*>(grp + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+      *reinterpret_cast<uint4*>(grp + kLGroup + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    }
+    bvec[(size_t)k * Dp + e] = col ? (float)b : 0.f;
+  }
+  if (threadIdx.x == 0) {
+    double c = -1e30;
+    if (valid) {
+      c = ((double)lpi[k] + s_logd[0] + s_logd[1] - 0.5 * D * kLog2Pi) * kLog2E;
+      if (!(c > -1e30)) c = -1e30;
+    }
+    kconst[k] = make_float2((float)c, (float)sk);
+  }
+}
+
+// Split pass: x~ 2^-a1 (any X strides) -> fp16 hi/lo in 128-row swizzled
+// K-major tiles (64 features; features >= D and rows >= N are zero).  One warp
+// per row, lane l carries features 4l..4l+3.
+__global__ void __launch_bounds__(256) full_split_kernel(
+    const float* __restrict__ X, int64_t sxn, int64_t sxd, int vec_ok, int64_t N, int D,
+    int64_t rows_pad, const float* __restrict__ cvec, const int* __restrict__ amax,
+    uint8_t* __restrict__ xsplit, int* __restrict__ err) {
+  const int lane = threadIdx.x & 31;
+  const int a = scale_exp_to(__int_as_float(*amax), 5);
+  const int f = 4 * lane;
+  const bool active = lane < 16;  // 64 features
+  float4 cc = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (active) {
+    if (f + 0 < D) cc.x = cvec[f + 0];
+    if (f + 1 < D) cc.y = cvec[f + 1];
+    if (f + 2 < D) cc.z = cvec[f + 2];
+    if (f + 3 < D) cc.w = cvec[f + 3];
+  }
+  for (int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5); row < rows_pad;
+       row += (int64_t)gridDim.x * 8) {
+    if (!active) continue;
+    float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (row < N) {
+      const float* src = X + row * sxn;
+      if (vec_ok && f + 3 < D) {
+        x = __ldg(reinterpret_cast<const float4*>(src + f));
+      } else {
+        if (f + 0 < D) x.x = __ldg(src + (int64_t)(f + 0) * sxd);
+        if (f + 1 < D) x.y = __ldg(src + (int64_t)(f + 1) * sxd);
+        if (f + 2 < D) x.z = __ldg(src + (int64_t)(f + 2) * sxd);
+        if (f + 3 < D) x.w = __ldg(src + (int64_t)(f + 3) * sxd);
+      }
+      x.x = ldexpf(x.x - cc.x, -a);
+      x.y = ldexpf(x.y - cc.y, -a);
+      x.z = ldexpf(x.z - cc.z, -a);
+      x.w = ldexpf(x.w - cc.w, -a);
+      if (f + 0 >= D) x.x = 0.f;
+      if (f + 1 >= D) x.y = 0.f;
+      if (f + 2 >= D) x.z = 0.f;
+      if (f + 3 >= D) x.w = 0.f;
+    }
+    const float mx = fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w)));
+    if (!(mx < 65504.f)) atomicOr(err, 0x10000);  // outside fp16 range (or NaN)
+    uint32_t h0, l0, h1, l1;
+    split2(x.x, x.y, h0, l0);
+    split2(x.z, x.w, h1, l1);
+    uint8_t* tile = xsplit + (row / kP1Rows) * (2 * kXTile);
+    const uint32_t off = xoff((int)(row % kP1Rows), f, kXTile);
+    *reinterpret_cast<uint2*>(tile + off) = make_uint2(h0, h1);
+    *reinterpret_cast<uint2*>(tile + kXTile + off) = make_uint2(l0, l1);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Pass 1: distances, per-row log-sum-exp, ll2 for pass 2.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kP1Threads, 1) full_ll_kernel(const P1Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint8_t* xs = smem;                                         // [2][hi | lo] x~ tiles
+  uint8_t* lsm = smem + 4 * kXTile;                           // [stages][hi | lo] L groups
+  float2* red = reinterpret_cast<float2*>(lsm + kP1LStages * 2 * kLGroup);  // [2][2][128]
+  P1Ctl* ctl = reinterpret_cast<P1Ctl*>(red + 4 * kP1Rows);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ntiles = (p.num_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+  volatile int* abort_flag = &ctl->abort_flag;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&ctl->xfull[i], 1);
+      mbar_init(&ctl->xempty[i], 1);
+      mbar_init(&ctl->afull[i], 1);
+      mbar_init(&ctl->aempty[i], kP1EpiWarps);
+    }
+    for (int i = 0; i < kP1LStages; ++i) {
+      mbar_init(&ctl->lfull[i], 1);
+      mbar_init(&ctl->lempty[i], 1);
+    }
+    mbar_init(&ctl->lse_bar, kP1EpiWarps);
+    ctl->abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(
+                     smem_u32(&ctl->tmem_base))
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = ctl->tmem_base;
+  const int xa = scale_exp_to(__int_as_float(*p.amax), 5);
+
+  if (warp == kP1MmaWarp) {
+    if (lane == 0) {
+      const uint32_t idesc = idesc_f16(p.G * p.Dp, false);
+      const int ks = p.Dp / 16;
+      int gi = 0;
+      bool ok = true;
+      for (int t = 0; t < ntiles && ok; ++t) {
+        const int xb = t & 1;
+        if (!mbar_wait_flag(&ctl->xfull[xb], (t >> 1) & 1, abort_flag, p.err, 1)) break;
+        for (int g = 0; g < p.num_groups; ++g, ++gi) {
+          const int st = gi % kP1LStages, acc = gi & 1;
+          if (!mbar_wait_flag(&ctl->lfull[st], (gi / kP1LStages) & 1, abort_flag, p.err, 2) ||
+              !mbar_wait_flag(&ctl->aempty[acc], ((gi >> 1) & 1) ^ 1, abort_flag, p.err, 4)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t xhi = smem_u32(xs + xb * 2 * kXTile), xlo = xhi + kXTile;
+          const uint32_t lhi = smem_u32(lsm + st * 2 * kLGroup), llo = lhi + kLGroup;
+          // terms x_lo*L_hi, x_hi*L_lo, x_hi*L_hi (smallest magnitudes first)
+          for (int term = 0; term < 3; ++term) {
+            const uint32_t a = term == 0 ? xlo : xhi;
+            const uint32_t b = term == 1 ? llo : lhi;
+            for (int s = 0; s < ks; ++s)
+              mma_ss(tmem + acc * 256, desc_kmajor(a + 32 * s), desc_kmajor(b + 32 * s), idesc,
+                     (term == 0 && s == 0) ? 0u : 1u);
+          }
+          tc_commit(&ctl->afull[acc]);
+          tc_commit(&ctl->lempty[st]);
+        }
+        tc_commit(&ctl->xempty[xb]);
+      }
+    }
+    __syncwarp();
+  } else if (warp == kP1LoadWarp) {
+    if (lane == 0) {
+      auto load_x = [&](int t) -> bool {
+        const int xb = t & 1;
+        if (!mbar_wait_flag(&ctl->xempty[xb], ((t >> 1) & 1) ^ 1, abort_flag, p.err, 8))
+          return false;
+        const int64_t tile = (int64_t)blockIdx.x + (int64_t)t * gridDim.x;
+        mbar_arrive_expect_tx(&ctl->xfull[xb], 2 * kXTile);
+        bulk_g2s(smem_u32(xs + xb * 2 * kXTile), p.xsplit + tile * (2 * kXTile), 2 * kXTile,
+                 &ctl->xfull[xb]);
+        return true;
+      };
+      int gi = 0;
+      bool ok = ntiles > 0 ? load_x(0) : true;
+      for (int t = 0; t < ntiles && ok; ++t) {
+        for (int g = 0; g < p.num_groups; ++g, ++gi) {
+          const int st = gi % kP1LStages;
+          if (!mbar_wait_flag(&ctl->lempty[st], ((gi / kP1LStages) & 1) ^ 1, abort_flag, p.err,
+                              16)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&ctl->lfull[st], 2 * kLGroup);
+          bulk_g2s(smem_u32(lsm + st * 2 * kLGroup), p.lgroups + (size_t)g * (2 * kLGroup),
+                   2 * kLGroup, &ctl->lfull[st]);
+          if (g == 0 && t + 1 < ntiles && !load_x(t + 1)) {
+            ok = false;
+            break;
+          }
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp < kP1EpiWarps) {
+    // thread = row (TMEM lane); warp half h takes components i = h, h+2, ...
+    const int q = warp & 3, h = warp >> 2;
+    const int row = q * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    const float kHalfLog2E = 0.72134752044448170f;
+    int gi = 0;
+    for (int t = 0; t < ntiles; ++t) {
+      const int64_t n = ((int64_t)blockIdx.x + (int64_t)t * gridDim.x) * kP1Rows + row;
+      const bool live = n < p.N;
+      float m = -3.0e38f, l = 0.f;
+      bool ok = true;
+      for (int g = 0; g < p.num_groups; ++g, ++gi) {
+        const int acc = gi & 1;
+        if (!mbar_wait_flag(&ctl->afull[acc], (gi >> 1) & 1, abort_flag, p.err, 32)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        for (int i = h; i < p.G; i += 2) {
+          const int k = g * p.G + i;
+          if (k >= p.K) break;
+          const float2 kc = p.kconst[k];
+          const float sc = ldexpf(1.0f, xa + (int)kc.y);  // V = V' 2^(a1 + s_k)
+          const float4* bk = reinterpret_cast<const float4*>(p.bvec + (size_t)k * p.Dp);
+          float maha = 0.f;
+          for (int c = 0; c < p.Dp; c += 16) {
+            uint32_t v[16];
+            tmem_ld16(tmem + lane_base + acc * 256 + i * p.Dp + c, v);
+            float bb[16];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const float4 b4 = __ldg(bk + c / 4 + u);
+              bb[4 * u + 0] = b4.x;
+              bb[4 * u + 1] = b4.y;
+              bb[4 * u + 2] = b4.z;
+              bb[4 * u + 3] = b4.w;
+            }
+            tmem_wait_ld();
+#pragma unroll
+            for (int u = 0; u < 16; ++u) {
+              const float dv = fmaf(__uint_as_float(v[u]), sc, -bb[u]);
+              maha = fmaf(dv, dv, maha);
+            }
+          }
+          const float ll2 = fmaf(-kHalfLog2E, maha, kc.x);
+          if (ll2 > m) {
+            l = fmaf(l, ex2(m - ll2), 1.0f);
+            m = ll2;
+          } else {
+            l += ex2(ll2 - m);
+          }
+          if (live) p.ll2[(size_t)k * p.ld_ll + n] = ll2;
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ctl->aempty[acc]);
+      }
+      if (!ok) break;
+      // combine the two halves of each row (red double-buffered by tile parity)
+      red[((t & 1) * 2 + h) * kP1Rows + row] = make_float2(m, l);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ctl->lse_bar);
+      if (!mbar_wait_flag(&ctl->lse_bar, t & 1, abort_flag, p.err, 64)) break;
+      if (h == 0) {
+        const float2 o = red[((t & 1) * 2 + 1) * kP1Rows + row];
+        const float M = fmaxf(m, o.x);
+        const float Ls = l * ex2(m - M) + o.y * ex2(o.x - M);
+        const float lz2 = M + lg2(Ls);
+        if (live) {
+          p.logZ[n] = lz2 * 0.6931471805599453f;
+          p.lz2[n] = lz2;
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
+  }
+}
+
+// Feature f of the pass-2 feature vector -> the two x~ slots it multiplies:
+// triangle features (i <= j) first, then x~_i (times the constant-1 slot D),
+// then 1 (slot D times slot D); past nf both slots are the zero slot D + 1.
+__device__ __forceinline__ uint32_t feature_slots(int f, int D, int nf) {
+  const int tri = D * (D + 1) / 2;
+  int i, j;
+  if (f < tri) {
+    i = 0;
+    int rem = f;
+    while (rem >= D - i) {
+      rem -= D - i;
+      ++i;
+    }
+    j = i + rem;
+  } else if (f < tri + D) {
+    i = f - tri;
+    j = D;
+  } else if (f < nf) {
+    i = D;
+    j = D;
+  } else {
+    i = D + 1;
+    j = D + 1;
+  }
+  return (uint32_t)i | ((uint32_t)j << 8);
+}
+
+// ---------------------------------------------------------------------------
+// Pass 2: T[k, f] = sum_n r_nk z_nf for one (feature block, component block,
+// row slab) per CTA.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kP2Threads, 1) full_stats_kernel(const P2Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint8_t* zst = smem;                                              // [2][hi | lo] 64 KB each
+  float* xsf = reinterpret_cast<float*>(smem + 2 * kZStage);        // [2][64][kXsStride]
+  uint32_t* ftab = reinterpret_cast<uint32_t*>(xsf + 2 * kP2Rows * kXsStride);  // [256]
+  P2Ctl* ctl = reinterpret_cast<P2Ctl*>(ftab + kP2Feat);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int fb = (int)blockIdx.x % p.nfb;
+  const int cbk = ((int)blockIdx.x / p.nfb) % p.ncb;
+  const int slab = (int)blockIdx.x / (p.nfb * p.ncb);
+  const int64_t row_begin = (int64_t)slab * p.rows_per_slab;
+  const int64_t row_end = p.N < row_begin + p.rows_per_slab ? p.N : row_begin + p.rows_per_slab;
+  const int nchunks = row_end > row_begin ? (int)((row_end - row_begin + kP2Rows - 1) / kP2Rows) : 0;
+  volatile int* abort_flag = &ctl->abort_flag;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&ctl->zfull[i], kP2ZWarps);
+      mbar_init(&ctl->zempty[i], 1);
+      mbar_init(&ctl->rfull[i], kP2RWarps);
+      mbar_init(&ctl->rempty[i], 1);
+    }
+    mbar_init(&ctl->tdone, 1);
+    ctl->abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  for (int f = threadIdx.x; f < kP2Feat; f += kP2Threads)
+    ftab[f] = feature_slots(fb * kP2Feat + f, p.D, p.nf);
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(
+                     smem_u32(&ctl->tmem_base))
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = ctl->tmem_base;
+  const int a2 = scale_exp_to(__int_as_float(*p.amax), 3);  // z uses x~ 2^-a2
+
+  if (warp == kP2MmaWarp) {
+    if (lane == 0) {
+      const uint32_t idesc = idesc_f16(kP2Feat, true);
+      for (int c = 0; c < nchunks; ++c) {
+        const int b = c & 1;
+        if (!mbar_wait_flag(&ctl->zfull[b], (c >> 1) & 1, abort_flag, p.err, 1) ||
+            !mbar_wait_flag(&ctl->rfull[b], (c >> 1) & 1, abort_flag, p.err, 2))
+          break;
+        tc_fence_after();
+        const uint32_t zhi = smem_u32(zst + b * kZStage), zlo = zhi + 4 * kZChunk;
+        for (int term = 0; term < 3; ++term) {  // r_lo*z_hi, r_hi*z_lo, r_hi*z_hi
+          const uint32_t acol = kColR2 + b * 64 + (term == 0 ? 32u : 0u);
+          const uint32_t bb = term == 1 ? zlo : zhi;
+          for (int s = 0; s < kP2Rows / 16; ++s)
+            mma_ts(tmem + kColT2, tmem + acol + 8 * s, desc_mnmajor(bb + s * 2048, kZChunk), idesc,
+                   (c == 0 && term == 0 && s == 0) ? 0u : 1u);
+        }
+        tc_commit(&ctl->zempty[b]);
+        tc_commit(&ctl->rempty[b]);
+      }
+      tc_commit(&ctl->tdone);
+    }
+    __syncwarp();
+  } else if (warp >= kP2RWarps && warp < kP2RWarps + kP2ZWarps) {
+    // ---- z chunks: warp zw stages rows 8zw..8zw+7 of x~ (its own rows, buffer by
+    // chunk parity) and writes their features
+    const int zw = warp - kP2RWarps;
+    for (int c = 0; c < nchunks; ++c) {
+      const int b = c & 1;
+      const int64_t r0 = row_begin + (int64_t)c * kP2Rows;
+      float* xsb = xsf + b * kP2Rows * kXsStride;
+      for (int rr = 0; rr < 8; ++rr) {
+        const int r = zw * 8 + rr;
+        const int64_t n = r0 + r;
+        for (int d = lane; d < kXsStride; d += 32) {
+          float v = 0.f;
+          if (d < p.D) {
+            if (n < row_end) v = ldexpf(p.X[n * p.sxn + (int64_t)d * p.sxd] - p.cvec[d], -a2);
+          } else if (d == p.D) {
+            v = 1.0f;
+          }
+          xsb[r * kXsStride + d] = v;
+        }
+      }
+      __syncwarp();  // each warp reads only the rows it staged
+      if (!mbar_wait_flag(&ctl->zempty[b], ((c >> 1) & 1) ^ 1, abort_flag, p.err, 8)) break;
+      uint8_t* zs = zst + b * kZStage;
+      bool over = false;
+      for (int rr = 0; rr < 8; ++rr) {
+        const int r = zw * 8 + rr;
+        const float* xr = xsb + r * kXsStride;
+#pragma unroll
+        for (int grp = 0; grp < 2; ++grp) {
+          const int f0 = grp * 128 + 4 * lane;
+          float z[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const uint32_t ij = ftab[f0 + u];
+            z[u] = xr[ij & 0xffu] * xr[ij >> 8];
+            over |= !(fabsf(z[u]) < 65504.f);
+          }
+          uint32_t h0, l0, h1, l1;
+          split2(z[0], z[1], h0, l0);
+          split2(z[2], z[3], h1, l1);
+          const uint32_t off = xoff(r, f0, kZChunk);
+          *reinterpret_cast<uint2*>(zs + off) = make_uint2(h0, h1);
+          *reinterpret_cast<uint2*>(zs + 4 * kZChunk + off) = make_uint2(l0, l1);
+        }
+      }
+      if (over) atomicOr(p.err, 0x20000);
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ctl->zfull[b]);
+    }
+  } else if (warp < kP2RWarps) {
+    // ---- R^T: thread = component k, 64 rows per chunk into TMEM (fp16 hi/lo)
+    const int kl = warp * 32 + lane;
+    const int k = cbk * kP2Comps + kl;
+    const bool kvalid = k < p.K;
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    const float* llk = p.ll2 + (size_t)(kvalid ? k : 0) * p.ld_ll;
+    int c = 0;
+    for (; c < nchunks; ++c) {
+      const int b = c & 1;
+      const int64_t r0 = row_begin + (int64_t)c * kP2Rows;
+      if (!mbar_wait_flag(&ctl->rempty[b], ((c >> 1) & 1) ^ 1, abort_flag, p.err, 16)) break;
+      tc_fence_after();
+      const uint32_t rb = tmem + lane_base + kColR2 + b * 64;
+#pragma unroll 1
+      for (int hh = 0; hh < 4; ++hh) {
+        const int64_t rs = r0 + 16 * hh;
+        float rv[16];
+        if (rs + 16 <= row_end) {
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            float4 l4 = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (kvalid) l4 = __ldg(reinterpret_cast<const float4*>(llk + rs) + u);
+            const float4 z4 = __ldg(reinterpret_cast<const float4*>(p.lz2 + rs) + u);
+            rv[4 * u + 0] = kvalid ? ex2(l4.x - z4.x) : 0.f;
+            rv[4 * u + 1] = kvalid ? ex2(l4.y - z4.y) : 0.f;
+            rv[4 * u + 2] = kvalid ? ex2(l4.z - z4.z) : 0.f;
+            rv[4 * u + 3] = kvalid ? ex2(l4.w - z4.w) : 0.f;
+          }
+        } else {
+#pragma unroll
+          for (int u = 0; u < 16; ++u) {
+            const int64_t n = rs + u;
+            rv[u] = (kvalid && n < row_end) ? ex2(llk[n] - p.lz2[n]) : 0.f;
+          }
+        }
+        uint32_t rh[8], rl[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) split2(rv[2 * u], rv[2 * u + 1], rh[u], rl[u]);
+        tmem_st8(rb + 8 * hh, rh);
+        tmem_st8(rb + 32 + 8 * hh, rl);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ctl->rfull[b]);
+    }
+    // partial statistics of this CTA -> workspace
+    const int ldp = p.nfb * kP2Feat;
+    float* out = p.part + ((size_t)slab * p.ncb * kP2Comps + (size_t)cbk * kP2Comps + kl) * ldp +
+                 (size_t)fb * kP2Feat;
+    const bool ok = c == nchunks && mbar_wait_flag(&ctl->tdone, 0, abort_flag, p.err, 32);
+    if (nchunks > 0 && ok) {
+      tc_fence_after();
+      for (int blk = 0; blk < kP2Feat / 32; ++blk) {
+        uint32_t tv[32];
+        tmem_ld32(tmem + lane_base + kColT2 + 32 * blk, tv);
+        tmem_wait_ld();
+        float4* o4 = reinterpret_cast<float4*>(out + 32 * blk);
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          o4[u] = make_float4(__uint_as_float(tv[4 * u]), __uint_as_float(tv[4 * u + 1]),
+                              __uint_as_float(tv[4 * u + 2]), __uint_as_float(tv[4 * u + 3]));
+      }
+    } else {
+      const float v = nchunks > 0 ? __int_as_float(0x7fc00000) : 0.f;
+      for (int f = 0; f < kP2Feat; ++f) out[f] = v;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
+  }
+}
+
+// Sum the pass-2 partials over slabs (in order) and undo the centring and
+// scaling:  Nk = S1,  mu_acc = Sx 2^a2 + c Nk,
+//   sig_outer[i][j] = Sxx[min(i,j)][max(i,j)] 2^(2 a2) + c_i mu~_j + mu~_i c_j
+//                     + Nk c_i c_j        (mu~ = Sx 2^a2, uncentred: full:213-228)
+// NaN everywhere on a device-side error.
+__global__ void full_reduce_kernel(const float* __restrict__ part, int slabs, int Kp, int ldp,
+                                   int K, int D, const float* __restrict__ cvec,
+                                   const int* __restrict__ amax, const int* __restrict__ err,
+                                   float* __restrict__ Nk, float* __restrict__ mu_acc,
+                                   float* __restrict__ sig, int accumulate) {
+  const int a2 = scale_exp_to(__int_as_float(*amax), 3);
+  const double s1 = ldexp(1.0, a2), s2 = ldexp(1.0, 2 * a2);
+  const bool bad = *err != 0;
+  const float qnan = __int_as_float(0x7fc00000);
+  const int tri = D * (D + 1) / 2;
+  const int per_k = D * D + D + 1;
+  auto feat_sum = [&](int k, int f) -> double {
+    double s = 0.0;
+    for (int sl = 0; sl < slabs; ++sl) s += part[((size_t)sl * Kp + k) * ldp + f];
+    return s;
+  };
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < (int64_t)K * per_k;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int k = (int)(e / per_k), w = (int)(e % per_k);
+    const double n = feat_sum(k, tri + D);
+    if (w == D * D + D) {
+      const float v = bad ? qnan : (float)n;
+      Nk[k] = accumulate ? Nk[k] + v : v;
+    } else if (w >= D * D) {
+      const int i = w - D * D;
+      const float v = bad ? qnan : (float)(feat_sum(k, tri + i) * s1 + (double)cvec[i] * n);
+      float* dst = mu_acc + (size_t)k * D + i;
+      *dst = accumulate ? *dst + v : v;
+    } else {
+      const int i = w / D, j = w % D;
+      const int a = min(i, j), b = max(i, j);
+      const double sxx = feat_sum(k, a * D - a * (a - 1) / 2 + (b - a)) * s2;
+      const double mi = feat_sum(k, tri + i) * s1, mj = feat_sum(k, tri + j) * s1;
+      const double ci = cvec[i], cj = cvec[j];
+      const float v = bad ? qnan : (float)(sxx + ci * mj + mi * cj + n * ci * cj);
+      float* dst = sig + (size_t)k * D * D + w;
+      *dst = accumulate ? *dst + v : v;
+    }
+  }
+}
+
+struct FullPlan {
+  int Dp, G, num_groups, Kpad, num_tiles, nf, nfb, ncb, slabs;
+  int64_t Npad, rows_per_slab;
+};
+
+FullPlan plan_full(int64_t N, int K, int D) {
+  FullPlan pl;
+  pl.Dp = (D + 15) / 16 * 16;
+  pl.G = 256 / pl.Dp;
+  pl.num_groups = (K + pl.G - 1) / pl.G;
+  pl.Kpad = pl.num_groups * pl.G;
+  pl.num_tiles = (int)((N + kP1Rows - 1) / kP1Rows);
+  pl.Npad = (int64_t)pl.num_tiles * kP1Rows;
+  pl.nf = D * (D + 1) / 2 + D + 1;
+  pl.nfb = (pl.nf + kP2Feat - 1) / kP2Feat;
+  pl.ncb = (K + kP2Comps - 1) / kP2Comps;
+  const int64_t nch_total = (N + kP2Rows - 1) / kP2Rows;
+  pl.slabs = (int)std::max<int64_t>(1, std::min<int64_t>(kSmsFull / (pl.nfb * pl.ncb), nch_total));
+  pl.rows_per_slab = ((nch_total + pl.slabs - 1) / pl.slabs) * kP2Rows;
+  return pl;
+}
+
+size_t p1_smem_bytes() {
+  return 1024 + (size_t)4 * kXTile + (size_t)kP1LStages * 2 * kLGroup +
+         (size_t)4 * kP1Rows * sizeof(float2) + sizeof(P1Ctl) + 64;
+}
+size_t p2_smem_bytes() {
+  return 1024 + (size_t)2 * kZStage + (size_t)2 * kP2Rows * kXsStride * 4 + (size_t)kP2Feat * 4 +
+         sizeof(P2Ctl) + 64;
+}
+
+struct FullWs {
+  int* err;
+  float* cvec;
+  uint8_t* lgroups;
+  float* bvec;
+  float2* kconst;
+  uint8_t* xsplit;
+  float* ll2;
+  float* lz2;
+  float* part;
+  size_t bytes;
+};
+
+FullWs carve_full(void* base, const FullPlan& pl, int64_t N) {
+  (void)N;
+  WsCarve w(base);
+  FullWs ws;
+  ws.err = w.take<int>(64);
+  ws.cvec = w.take<float>(kFullMaxD);
+  ws.lgroups = w.take<uint8_t>((size_t)pl.num_groups * 2 * kLGroup);
+  ws.bvec = w.take<float>((size_t)pl.Kpad * pl.Dp);
+  ws.kconst = w.take<float2>(pl.Kpad);
+  ws.xsplit = w.take<uint8_t>((size_t)pl.num_tiles * 2 * kXTile);
+  ws.ll2 = w.take<float>((size_t)pl.Kpad * pl.Npad);
+  ws.lz2 = w.take<float>((size_t)pl.Npad);
+  ws.part = w.take<float>((size_t)pl.slabs * pl.ncb * kP2Comps * pl.nfb * kP2Feat);
+  ws.bytes = w.used + 256;
+  return ws;
+}
+
+}  // namespace
+
+bool full_tc_supported(const EstepArgs& a) {
+  if (a.D > kFullMaxD || a.N <= 0) return false;
+  const FullPlan pl = plan_full(a.N, a.K, a.D);
+  return (double)pl.Kpad * (double)pl.Npad * 4.0 <= 8.0e9;  // ll2 scratch bound
+}
+
+size_t full_tc_workspace_bytes(int64_t N, int K, int D) {
+  EstepArgs probe{};
+  probe.N = N;
+  probe.K = K;
+  probe.D = D;
+  if (K < 1 || !full_tc_supported(probe)) return 0;
+  return carve_full(nullptr, plan_full(N, K, D), N).bytes;
+}
+
+cudaError_t full_tc_estep(const EstepArgs& a) {
+  const FullPlan pl = plan_full(a.N, a.K, a.D);
+  const FullWs ws = carve_full(a.ws, pl, a.N);
+  cudaStream_t st = a.stream;
+  // err[0]: device error word; err[1]: max|mu - c| (float bits)
+  cudaError_t e = cudaMemsetAsync(ws.err, 0, 2 * sizeof(int), st);
+  if (e != cudaSuccess) return e;
+  int* amax = ws.err + 1;
+  centre_kernel<<<pl.Dp, 256, 0, st>>>(a.mu, a.smk, a.smd, a.K, a.D, ws.cvec, amax);
+  full_prep_kernel<<<pl.Kpad, 64, 0, st>>>(a.mu, a.smk, a.smd, a.cov, a.lpi, ws.cvec, a.K, a.D,
+                                           pl.Dp, pl.G, ws.lgroups, ws.bvec, ws.kconst);
+  const int vec_ok = a.sxd == 1 && (reinterpret_cast<uintptr_t>(a.X) & 15) == 0 && a.sxn % 4 == 0;
+  const int sblocks = (int)std::min<int64_t>((pl.Npad + 7) / 8, 16 * kSmsFull);
+  full_split_kernel<<<sblocks, 256, 0, st>>>(a.X, a.sxn, a.sxd, vec_ok, a.N, a.D, pl.Npad,
+                                             ws.cvec, amax, ws.xsplit, ws.err);
+
+  P1Params p1;
+  p1.xsplit = ws.xsplit;
+  p1.lgroups = ws.lgroups;
+  p1.bvec = ws.bvec;
+  p1.kconst = ws.kconst;
+  p1.amax = amax;
+  p1.N = a.N;
+  p1.K = a.K;
+  p1.Dp = pl.Dp;
+  p1.G = pl.G;
+  p1.num_groups = pl.num_groups;
+  p1.num_tiles = pl.num_tiles;
+  p1.ld_ll = pl.Npad;
+  p1.ll2 = ws.ll2;
+  p1.lz2 = ws.lz2;
+  p1.logZ = a.logZ;
+  p1.err = ws.err;
+  const size_t sm1 = p1_smem_bytes();
+  e = cudaFuncSetAttribute(full_ll_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm1);
+  if (e != cudaSuccess) return e;
+  profile_mark(false, st);
+  full_ll_kernel<<<std::min(pl.num_tiles, kSmsFull), kP1Threads, sm1, st>>>(p1);
+
+  P2Params p2;
+  p2.X = a.X;
+  p2.sxn = a.sxn;
+  p2.sxd = a.sxd;
+  p2.cvec = ws.cvec;
+  p2.ll2 = ws.ll2;
+  p2.ld_ll = pl.Npad;
+  p2.lz2 = ws.lz2;
+  p2.amax = amax;
+  p2.N = a.N;
+  p2.K = a.K;
+  p2.Kll = pl.Kpad;
+  p2.D = a.D;
+  p2.nf = pl.nf;
+  p2.nfb = pl.nfb;
+  p2.ncb = pl.ncb;
+  p2.slabs = pl.slabs;
+  p2.rows_per_slab = pl.rows_per_slab;
+  p2.part = ws.part;
+  p2.err = ws.err;
+  const size_t sm2 = p2_smem_bytes();
+  e = cudaFuncSetAttribute(full_stats_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)sm2);
+  if (e != cudaSuccess) return e;
+  full_stats_kernel<<<pl.nfb * pl.ncb * pl.slabs, kP2Threads, sm2, st>>>(p2);
+  profile_mark(true, st);
+
+  const int64_t total = (int64_t)a.K * (a.D * a.D + a.D + 1);
+  const int rblocks = (int)std::min<int64_t>((total + 255) / 256, 8 * kSmsFull);
+  full_reduce_kernel<<<rblocks, 256, 0, st>>>(ws.part, pl.slabs, pl.ncb * kP2Comps,
+                                              pl.nfb * kP2Feat, a.K, a.D, ws.cvec, amax, ws.err,
+                                              a.Nk, a.mu_acc, a.sig, (a.flags & 1u) ? 1 : 0);
+  count_launches(6);
+  return cudaGetLastError();
+}
+
+}  // namespace fgmm
