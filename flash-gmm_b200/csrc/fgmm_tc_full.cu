@@ -42,10 +42,10 @@ constexpr int kSmsFull = 148;
 
 // ---- pass 1
 constexpr int kP1Rows = 128;
-constexpr int kP1EpiWarps = 8;               // two warps per TMEM lane quadrant
-constexpr int kP1LoadWarp = 8;
-constexpr int kP1MmaWarp = 9;
-constexpr int kP1Threads = 10 * 32;
+constexpr int kP1EpiWarps = 16;              // four warps per TMEM lane quadrant
+constexpr int kP1LoadWarp = 16;
+constexpr int kP1MmaWarp = 17;
+constexpr int kP1Threads = 18 * 32;
 constexpr int kP1LStages = 2;
 constexpr int kXTile = kP1Rows * 128;        // 16 KB: one hi (or lo) x~ tile, 64 features
 constexpr int kLGroup = 256 * 128;           // 32 KB: one hi (or lo) group of L columns
@@ -53,16 +53,15 @@ constexpr int kLGroup = 256 * 128;           // 32 KB: one hi (or lo) group of L
 // ---- pass 2
 constexpr int kP2Rows = 64;                  // rows per chunk (MMA K extent)
 constexpr int kP2Feat = 256;                 // features per CTA (MMA N)
-constexpr int kP2Comps = 128;                // components per CTA (TMEM lanes, MMA M)
-constexpr int kP2RWarps = 4;                 // warps 0-3: R^T (thread = component)
-constexpr int kP2ZWarps = 8;                 // warps 4-11: z chunks
-constexpr int kP2MmaWarp = 12;
-constexpr int kP2Threads = 13 * 32;
+constexpr int kP2Comps = 128;                // components per CTA (MMA M)
+constexpr int kP2ZWarps = 16;                // warps 0-15: z chunks (4 rows each)
+constexpr int kP2LoadWarp = 16;
+constexpr int kP2MmaWarp = 17;
+constexpr int kP2Threads = 18 * 32;
 constexpr int kZChunk = kP2Rows * 128;       // 8 KB: 64 rows x 64 features (fp16)
 constexpr int kZStage = 2 * 4 * kZChunk;     // hi + lo, 256 features: 64 KB
-constexpr int kXsStride = 68;                // floats per staged x~ row (D + one + zero, padded)
-constexpr uint32_t kColT2 = 0;               // statistics accumulator, 256 columns
-constexpr uint32_t kColR2 = 256;             // 2 x (R^T hi 32 + lo 32 columns)
+constexpr int kRBlock = kP2Comps * 128;      // 16 KB: R^T hi (or lo), 128 components x 64 rows
+constexpr uint32_t kPadFeature = 0xFFFFu;    // feature slot code of a zero (padding) feature
 
 struct P1Params {
   const uint8_t* xsplit;   // [num_tiles][hi 16 KB | lo 16 KB]  x~ 2^-a1, swizzled K-major
@@ -89,22 +88,17 @@ struct __align__(8) P1Ctl {
 };
 
 struct P2Params {
-  const float* X;
-  int64_t sxn, sxd;
-  const float* cvec;
-  const float* ll2;
-  int64_t ld_ll;
-  const float* lz2;
-  const int* amax;
+  const uint8_t* rt;       // [chunks][ncb][hi 16 KB | lo 16 KB]  R^T, K-major swizzled
+  const float* xs2;        // [Npad][D+1]  x~ 2^-a2 and a constant 1
   int64_t N;
-  int K, Kll, D, nf, nfb, ncb, slabs;
+  int D, nf, nfb, ncb, slabs;
   int64_t rows_per_slab;   // multiple of 64
   float* part;             // [slabs][ncb*128][nfb*256]
   int* err;
 };
 
 struct __align__(8) P2Ctl {
-  uint64_t zfull[2], zempty[2], rfull[2], rempty[2], tdone;
+  uint64_t in_full[2], in_empty[2], zfull[2], zempty[2], tdone;
   uint32_t tmem_base;
   volatile int abort_flag;
 };
@@ -189,15 +183,17 @@ __global__ void __launch_bounds__(64) full_prep_kernel(
   }
 }
 
-// Split pass: x~ 2^-a1 (any X strides) -> fp16 hi/lo in 128-row swizzled
-// K-major tiles (64 features; features >= D and rows >= N are zero).  One warp
-// per row, lane l carries features 4l..4l+3.
+// Split pass (any X strides), one warp per row, lane l carries features
+// 4l..4l+3 (features >= D and rows >= N are zero):
+//   xsplit: x~ 2^-a1 as fp16 hi/lo in 128-row swizzled K-major tiles (pass 1);
+//   xs2:    x~ 2^-a2 in fp32, D values then a constant 1 per row (pass 2).
 __global__ void __launch_bounds__(256) full_split_kernel(
     const float* __restrict__ X, int64_t sxn, int64_t sxd, int vec_ok, int64_t N, int D,
     int64_t rows_pad, const float* __restrict__ cvec, const int* __restrict__ amax,
-    uint8_t* __restrict__ xsplit, int* __restrict__ err) {
+    uint8_t* __restrict__ xsplit, float* __restrict__ xs2, int* __restrict__ err) {
   const int lane = threadIdx.x & 31;
-  const int a = scale_exp_to(__int_as_float(*amax), 5);
+  const float am = __int_as_float(*amax);
+  const int a1 = scale_exp_to(am, 5), a2 = scale_exp_to(am, 3);
   const int f = 4 * lane;
   const bool active = lane < 16;  // 64 features
   float4 cc = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -209,6 +205,8 @@ __global__ void __launch_bounds__(256) full_split_kernel(
   }
   for (int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5); row < rows_pad;
        row += (int64_t)gridDim.x * 8) {
+    float* x2row = xs2 + row * (D + 1);
+    if (lane == 16) x2row[D] = 1.0f;
     if (!active) continue;
     float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
     if (row < N) {
@@ -221,15 +219,20 @@ __global__ void __launch_bounds__(256) full_split_kernel(
         if (f + 2 < D) x.z = __ldg(src + (int64_t)(f + 2) * sxd);
         if (f + 3 < D) x.w = __ldg(src + (int64_t)(f + 3) * sxd);
       }
-      x.x = ldexpf(x.x - cc.x, -a);
-      x.y = ldexpf(x.y - cc.y, -a);
-      x.z = ldexpf(x.z - cc.z, -a);
-      x.w = ldexpf(x.w - cc.w, -a);
+      x.x -= cc.x;
+      x.y -= cc.y;
+      x.z -= cc.z;
+      x.w -= cc.w;
       if (f + 0 >= D) x.x = 0.f;
       if (f + 1 >= D) x.y = 0.f;
       if (f + 2 >= D) x.z = 0.f;
       if (f + 3 >= D) x.w = 0.f;
     }
+    if (f + 0 < D) x2row[f + 0] = ldexpf(x.x, -a2);
+    if (f + 1 < D) x2row[f + 1] = ldexpf(x.y, -a2);
+    if (f + 2 < D) x2row[f + 2] = ldexpf(x.z, -a2);
+    if (f + 3 < D) x2row[f + 3] = ldexpf(x.w, -a2);
+    x = make_float4(ldexpf(x.x, -a1), ldexpf(x.y, -a1), ldexpf(x.z, -a1), ldexpf(x.w, -a1));
     const float mx = fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w)));
     if (!(mx < 65504.f)) atomicOr(err, 0x10000);  // outside fp16 range (or NaN)
     uint32_t h0, l0, h1, l1;
@@ -250,8 +253,8 @@ __global__ void __launch_bounds__(kP1Threads, 1) full_ll_kernel(const P1Params p
   uint8_t* smem = align1024(smem_raw);
   uint8_t* xs = smem;                                         // [2][hi | lo] x~ tiles
   uint8_t* lsm = smem + 4 * kXTile;                           // [stages][hi | lo] L groups
-  float2* red = reinterpret_cast<float2*>(lsm + kP1LStages * 2 * kLGroup);  // [2][2][128]
-  P1Ctl* ctl = reinterpret_cast<P1Ctl*>(red + 4 * kP1Rows);
+  float2* red = reinterpret_cast<float2*>(lsm + kP1LStages * 2 * kLGroup);  // [2][4][128]
+  P1Ctl* ctl = reinterpret_cast<P1Ctl*>(red + 8 * kP1Rows);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ntiles = (p.num_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
@@ -352,7 +355,7 @@ __global__ void __launch_bounds__(kP1Threads, 1) full_ll_kernel(const P1Params p
     }
     __syncwarp();
   } else if (warp < kP1EpiWarps) {
-    // thread = row (TMEM lane); warp half h takes components i = h, h+2, ...
+    // thread = row (TMEM lane); warp quarter h takes components i = h, h+4, ...
     const int q = warp & 3, h = warp >> 2;
     const int row = q * 32 + lane;
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
@@ -370,32 +373,39 @@ __global__ void __launch_bounds__(kP1Threads, 1) full_ll_kernel(const P1Params p
           break;
         }
         tc_fence_after();
-        for (int i = h; i < p.G; i += 2) {
+        for (int i = h; i < p.G; i += 4) {
           const int k = g * p.G + i;
           if (k >= p.K) break;
           const float2 kc = p.kconst[k];
           const float sc = ldexpf(1.0f, xa + (int)kc.y);  // V = V' 2^(a1 + s_k)
           const float4* bk = reinterpret_cast<const float4*>(p.bvec + (size_t)k * p.Dp);
-          float maha = 0.f;
-          for (int c = 0; c < p.Dp; c += 16) {
-            uint32_t v[16];
+          float mh[4] = {0.f, 0.f, 0.f, 0.f};  // independent partial sums of maha
+          for (int c = 0; c < p.Dp; c += 32) {
+            uint32_t v[32];
+            float bb[32];
+            const bool two = c + 16 < p.Dp;
             tmem_ld16(tmem + lane_base + acc * 256 + i * p.Dp + c, v);
-            float bb[16];
+            if (two) tmem_ld16(tmem + lane_base + acc * 256 + i * p.Dp + c + 16, v + 16);
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              const float4 b4 = __ldg(bk + c / 4 + u);
+            for (int u = 0; u < 8; ++u) {
+              const float4 b4 = (u < 4 || two) ? __ldg(bk + c / 4 + u) : make_float4(0.f, 0.f, 0.f, 0.f);
               bb[4 * u + 0] = b4.x;
               bb[4 * u + 1] = b4.y;
               bb[4 * u + 2] = b4.z;
               bb[4 * u + 3] = b4.w;
             }
             tmem_wait_ld();
+            if (!two) {
 #pragma unroll
-            for (int u = 0; u < 16; ++u) {
+              for (int u = 16; u < 32; ++u) v[u] = 0u;
+            }
+#pragma unroll
+            for (int u = 0; u < 32; ++u) {
               const float dv = fmaf(__uint_as_float(v[u]), sc, -bb[u]);
-              maha = fmaf(dv, dv, maha);
+              mh[u & 3] = fmaf(dv, dv, mh[u & 3]);
             }
           }
+          const float maha = (mh[0] + mh[1]) + (mh[2] + mh[3]);
           const float ll2 = fmaf(-kHalfLog2E, maha, kc.x);
           if (ll2 > m) {
             l = fmaf(l, ex2(m - ll2), 1.0f);
@@ -410,15 +420,18 @@ __global__ void __launch_bounds__(kP1Threads, 1) full_ll_kernel(const P1Params p
         if (lane == 0) mbar_arrive(&ctl->aempty[acc]);
       }
       if (!ok) break;
-      // combine the two halves of each row (red double-buffered by tile parity)
-      red[((t & 1) * 2 + h) * kP1Rows + row] = make_float2(m, l);
+      // combine the four quarters of each row (red double-buffered by tile parity)
+      red[((t & 1) * 4 + h) * kP1Rows + row] = make_float2(m, l);
       __syncwarp();
       if (lane == 0) mbar_arrive(&ctl->lse_bar);
       if (!mbar_wait_flag(&ctl->lse_bar, t & 1, abort_flag, p.err, 64)) break;
       if (h == 0) {
-        const float2 o = red[((t & 1) * 2 + 1) * kP1Rows + row];
-        const float M = fmaxf(m, o.x);
-        const float Ls = l * ex2(m - M) + o.y * ex2(o.x - M);
+        float2 o[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) o[u] = red[((t & 1) * 4 + u) * kP1Rows + row];
+        const float M = fmaxf(fmaxf(o[0].x, o[1].x), fmaxf(o[2].x, o[3].x));
+        const float Ls = (o[0].y * ex2(o[0].x - M) + o[1].y * ex2(o[1].x - M)) +
+                         (o[2].y * ex2(o[2].x - M) + o[3].y * ex2(o[3].x - M));
         const float lz2 = M + lg2(Ls);
         if (live) {
           p.logZ[n] = lz2 * 0.6931471805599453f;
@@ -438,7 +451,7 @@ __global__ void __launch_bounds__(kP1Threads, 1) full_ll_kernel(const P1Params p
 
 // Feature f of the pass-2 feature vector -> the two x~ slots it multiplies:
 // triangle features (i <= j) first, then x~_i (times the constant-1 slot D),
-// then 1 (slot D times slot D); past nf both slots are the zero slot D + 1.
+// then 1 (slot D times slot D); past nf a zero feature.
 __device__ __forceinline__ uint32_t feature_slots(int f, int D, int nf) {
   const int tri = D * (D + 1) / 2;
   int i, j;
@@ -457,22 +470,75 @@ __device__ __forceinline__ uint32_t feature_slots(int f, int D, int nf) {
     i = D;
     j = D;
   } else {
-    i = D + 1;
-    j = D + 1;
+    return kPadFeature;
   }
   return (uint32_t)i | ((uint32_t)j << 8);
 }
 
 // ---------------------------------------------------------------------------
+// Responsibilities for pass 2, one block per (64-row chunk, component block),
+// thread = component: r = 2^(ll2 - lz2) (0 past N or K), split into fp16
+// hi/lo and written as the K-major, 128B-swizzled A operand of pass 2 (one
+// 128-byte row of 64 rows per component).
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kP2Comps) full_resp_kernel(const float* __restrict__ ll2,
+                                                             int64_t ld_ll,
+                                                             const float* __restrict__ lz2,
+                                                             int64_t N, int K, int ncb,
+                                                             uint8_t* __restrict__ rt) {
+  const int chunk = (int)blockIdx.x / ncb, cbk = (int)blockIdx.x % ncb;
+  const int t = threadIdx.x;
+  const int k = cbk * kP2Comps + t;
+  const int64_t r0 = (int64_t)chunk * kP2Rows;
+  __shared__ float lz[kP2Rows];
+  if (t < kP2Rows) lz[t] = r0 + t < N ? lz2[r0 + t] : 0.f;
+  __syncthreads();
+  const bool kvalid = k < K;
+  const float* llk = ll2 + (size_t)(kvalid ? k : 0) * ld_ll + r0;
+  uint8_t* blk = rt + ((size_t)chunk * ncb + cbk) * (2 * kRBlock);
+#pragma unroll 1
+  for (int g = 0; g < kP2Rows / 8; ++g) {
+    float rv[8];
+    if (kvalid && r0 + 8 * g + 8 <= N) {
+      const float4 a = __ldg(reinterpret_cast<const float4*>(llk + 8 * g));
+      const float4 b = __ldg(reinterpret_cast<const float4*>(llk + 8 * g + 4));
+      rv[0] = ex2(a.x - lz[8 * g + 0]);
+      rv[1] = ex2(a.y - lz[8 * g + 1]);
+      rv[2] = ex2(a.z - lz[8 * g + 2]);
+      rv[3] = ex2(a.w - lz[8 * g + 3]);
+      rv[4] = ex2(b.x - lz[8 * g + 4]);
+      rv[5] = ex2(b.y - lz[8 * g + 5]);
+      rv[6] = ex2(b.z - lz[8 * g + 6]);
+      rv[7] = ex2(b.w - lz[8 * g + 7]);
+    } else {
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        rv[u] = (kvalid && r0 + 8 * g + u < N) ? ex2(llk[8 * g + u] - lz[8 * g + u]) : 0.f;
+    }
+    uint32_t hi[4], lo[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) split2(rv[2 * u], rv[2 * u + 1], hi[u], lo[u]);
+    const uint32_t off = xoff(t, 8 * g, kRBlock);
+    *reinterpret_cast<uint4*>(blk + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+    *reinterpret_cast<uint4*>(blk + kRBlock + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Pass 2: T[k, f] = sum_n r_nk z_nf for one (feature block, component block,
-// row slab) per CTA.
+// row slab) per CTA.  Per 64-row chunk a loader thread bulk-copies R^T
+// (32 KB) and the x~ rows (64 x (D+1) floats); 16 warps build the z chunk;
+// one thread issues the MMAs (A = R^T, B = z, both from shared memory).
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(kP2Threads, 1) full_stats_kernel(const P2Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
-  uint8_t* zst = smem;                                              // [2][hi | lo] 64 KB each
-  float* xsf = reinterpret_cast<float*>(smem + 2 * kZStage);        // [2][64][kXsStride]
-  uint32_t* ftab = reinterpret_cast<uint32_t*>(xsf + 2 * kP2Rows * kXsStride);  // [256]
+  const int xs_stride = p.D + 1;
+  const uint32_t xs_bytes = (uint32_t)(kP2Rows * xs_stride * 4);
+  uint8_t* rst = smem;                                        // [2][hi | lo] R^T, 32 KB each
+  uint8_t* zst = smem + 4 * kRBlock;                          // [2][hi | lo] z, 64 KB each
+  float* xst = reinterpret_cast<float*>(zst + 2 * kZStage);   // [2][64][D+1]
+  uint32_t* ftab = reinterpret_cast<uint32_t*>(xst + 2 * kP2Rows * xs_stride);  // [256]
   P2Ctl* ctl = reinterpret_cast<P2Ctl*>(ftab + kP2Feat);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -481,15 +547,16 @@ __global__ void __launch_bounds__(kP2Threads, 1) full_stats_kernel(const P2Param
   const int slab = (int)blockIdx.x / (p.nfb * p.ncb);
   const int64_t row_begin = (int64_t)slab * p.rows_per_slab;
   const int64_t row_end = p.N < row_begin + p.rows_per_slab ? p.N : row_begin + p.rows_per_slab;
-  const int nchunks = row_end > row_begin ? (int)((row_end - row_begin + kP2Rows - 1) / kP2Rows) : 0;
+  const int nchunks =
+      row_end > row_begin ? (int)((row_end - row_begin + kP2Rows - 1) / kP2Rows) : 0;
   volatile int* abort_flag = &ctl->abort_flag;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
+      mbar_init(&ctl->in_full[i], 1);
+      mbar_init(&ctl->in_empty[i], kP2ZWarps + 1);  // z warps (x rows) + MMA commit (R^T)
       mbar_init(&ctl->zfull[i], kP2ZWarps);
       mbar_init(&ctl->zempty[i], 1);
-      mbar_init(&ctl->rfull[i], kP2RWarps);
-      mbar_init(&ctl->rempty[i], 1);
     }
     mbar_init(&ctl->tdone, 1);
     ctl->abort_flag = 0;
@@ -498,7 +565,7 @@ __global__ void __launch_bounds__(kP2Threads, 1) full_stats_kernel(const P2Param
   for (int f = threadIdx.x; f < kP2Feat; f += kP2Threads)
     ftab[f] = feature_slots(fb * kP2Feat + f, p.D, p.nf);
   if (warp == 0) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;" ::"r"(
                      smem_u32(&ctl->tmem_base))
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
@@ -507,59 +574,63 @@ __global__ void __launch_bounds__(kP2Threads, 1) full_stats_kernel(const P2Param
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = ctl->tmem_base;
-  const int a2 = scale_exp_to(__int_as_float(*p.amax), 3);  // z uses x~ 2^-a2
 
-  if (warp == kP2MmaWarp) {
+  if (warp == kP2LoadWarp) {
     if (lane == 0) {
-      const uint32_t idesc = idesc_f16(kP2Feat, true);
       for (int c = 0; c < nchunks; ++c) {
         const int b = c & 1;
-        if (!mbar_wait_flag(&ctl->zfull[b], (c >> 1) & 1, abort_flag, p.err, 1) ||
-            !mbar_wait_flag(&ctl->rfull[b], (c >> 1) & 1, abort_flag, p.err, 2))
+        if (!mbar_wait_flag(&ctl->in_empty[b], ((c >> 1) & 1) ^ 1, abort_flag, p.err, 1)) break;
+        const int64_t r0 = row_begin + (int64_t)c * kP2Rows;
+        const int64_t chunk = r0 / kP2Rows;
+        mbar_arrive_expect_tx(&ctl->in_full[b], 2 * kRBlock + xs_bytes);
+        bulk_g2s(smem_u32(rst + b * 2 * kRBlock),
+                 p.rt + ((size_t)chunk * p.ncb + cbk) * (2 * kRBlock), 2 * kRBlock,
+                 &ctl->in_full[b]);
+        bulk_g2s(smem_u32(xst + b * kP2Rows * xs_stride), p.xs2 + r0 * xs_stride, xs_bytes,
+                 &ctl->in_full[b]);
+      }
+    }
+    __syncwarp();
+  } else if (warp == kP2MmaWarp) {
+    if (lane == 0) {
+      const uint32_t idesc = idesc_f16(kP2Feat, true);  // A K-major, B MN-major
+      for (int c = 0; c < nchunks; ++c) {
+        const int b = c & 1;
+        if (!mbar_wait_flag(&ctl->zfull[b], (c >> 1) & 1, abort_flag, p.err, 2) ||
+            !mbar_wait_flag(&ctl->in_full[b], (c >> 1) & 1, abort_flag, p.err, 4))
           break;
         tc_fence_after();
+        const uint32_t rhi = smem_u32(rst + b * 2 * kRBlock), rlo = rhi + kRBlock;
         const uint32_t zhi = smem_u32(zst + b * kZStage), zlo = zhi + 4 * kZChunk;
         for (int term = 0; term < 3; ++term) {  // r_lo*z_hi, r_hi*z_lo, r_hi*z_hi
-          const uint32_t acol = kColR2 + b * 64 + (term == 0 ? 32u : 0u);
-          const uint32_t bb = term == 1 ? zlo : zhi;
+          const uint32_t ra = term == 0 ? rlo : rhi;
+          const uint32_t zb = term == 1 ? zlo : zhi;
           for (int s = 0; s < kP2Rows / 16; ++s)
-            mma_ts(tmem + kColT2, tmem + acol + 8 * s, desc_mnmajor(bb + s * 2048, kZChunk), idesc,
+            mma_ss(tmem, desc_kmajor(ra + 32 * s), desc_mnmajor(zb + s * 2048, kZChunk), idesc,
                    (c == 0 && term == 0 && s == 0) ? 0u : 1u);
         }
         tc_commit(&ctl->zempty[b]);
-        tc_commit(&ctl->rempty[b]);
+        tc_commit(&ctl->in_empty[b]);
       }
       tc_commit(&ctl->tdone);
     }
     __syncwarp();
-  } else if (warp >= kP2RWarps && warp < kP2RWarps + kP2ZWarps) {
-    // ---- z chunks: warp zw stages rows 8zw..8zw+7 of x~ (its own rows, buffer by
-    // chunk parity) and writes their features
-    const int zw = warp - kP2RWarps;
-    for (int c = 0; c < nchunks; ++c) {
+  } else {
+    // ---- z chunks: warp zw builds rows 4zw..4zw+3; lane l features 4l.. and 128+4l..
+    const int zw = warp;
+    int c = 0;
+    for (; c < nchunks; ++c) {
       const int b = c & 1;
-      const int64_t r0 = row_begin + (int64_t)c * kP2Rows;
-      float* xsb = xsf + b * kP2Rows * kXsStride;
-      for (int rr = 0; rr < 8; ++rr) {
-        const int r = zw * 8 + rr;
-        const int64_t n = r0 + r;
-        for (int d = lane; d < kXsStride; d += 32) {
-          float v = 0.f;
-          if (d < p.D) {
-            if (n < row_end) v = ldexpf(p.X[n * p.sxn + (int64_t)d * p.sxd] - p.cvec[d], -a2);
-          } else if (d == p.D) {
-            v = 1.0f;
-          }
-          xsb[r * kXsStride + d] = v;
-        }
-      }
-      __syncwarp();  // each warp reads only the rows it staged
-      if (!mbar_wait_flag(&ctl->zempty[b], ((c >> 1) & 1) ^ 1, abort_flag, p.err, 8)) break;
+      if (!mbar_wait_flag(&ctl->in_full[b], (c >> 1) & 1, abort_flag, p.err, 8) ||
+          !mbar_wait_flag(&ctl->zempty[b], ((c >> 1) & 1) ^ 1, abort_flag, p.err, 16))
+        break;
+      const float* xsb = xst + b * kP2Rows * xs_stride;
       uint8_t* zs = zst + b * kZStage;
       bool over = false;
-      for (int rr = 0; rr < 8; ++rr) {
-        const int r = zw * 8 + rr;
-        const float* xr = xsb + r * kXsStride;
+#pragma unroll 1
+      for (int rr = 0; rr < 4; ++rr) {
+        const int r = zw * 4 + rr;
+        const float* xr = xsb + r * xs_stride;
 #pragma unroll
         for (int grp = 0; grp < 2; ++grp) {
           const int f0 = grp * 128 + 4 * lane;
@@ -567,7 +638,7 @@ __global__ void __launch_bounds__(kP2Threads, 1) full_stats_kernel(const P2Param
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
             const uint32_t ij = ftab[f0 + u];
-            z[u] = xr[ij & 0xffu] * xr[ij >> 8];
+            z[u] = ij == kPadFeature ? 0.f : xr[ij & 0xffu] * xr[ij >> 8];
             over |= !(fabsf(z[u]) < 65504.f);
           }
           uint32_t h0, l0, h1, l1;
@@ -581,65 +652,24 @@ __global__ void __launch_bounds__(kP2Threads, 1) full_stats_kernel(const P2Param
       if (over) atomicOr(p.err, 0x20000);
       fence_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&ctl->zfull[b]);
-    }
-  } else if (warp < kP2RWarps) {
-    // ---- R^T: thread = component k, 64 rows per chunk into TMEM (fp16 hi/lo)
-    const int kl = warp * 32 + lane;
-    const int k = cbk * kP2Comps + kl;
-    const bool kvalid = k < p.K;
-    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-    const float* llk = p.ll2 + (size_t)(kvalid ? k : 0) * p.ld_ll;
-    int c = 0;
-    for (; c < nchunks; ++c) {
-      const int b = c & 1;
-      const int64_t r0 = row_begin + (int64_t)c * kP2Rows;
-      if (!mbar_wait_flag(&ctl->rempty[b], ((c >> 1) & 1) ^ 1, abort_flag, p.err, 16)) break;
-      tc_fence_after();
-      const uint32_t rb = tmem + lane_base + kColR2 + b * 64;
-#pragma unroll 1
-      for (int hh = 0; hh < 4; ++hh) {
-        const int64_t rs = r0 + 16 * hh;
-        float rv[16];
-        if (rs + 16 <= row_end) {
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            float4 l4 = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (kvalid) l4 = __ldg(reinterpret_cast<const float4*>(llk + rs) + u);
-            const float4 z4 = __ldg(reinterpret_cast<const float4*>(p.lz2 + rs) + u);
-            rv[4 * u + 0] = kvalid ? ex2(l4.x - z4.x) : 0.f;
-            rv[4 * u + 1] = kvalid ? ex2(l4.y - z4.y) : 0.f;
-            rv[4 * u + 2] = kvalid ? ex2(l4.z - z4.z) : 0.f;
-            rv[4 * u + 3] = kvalid ? ex2(l4.w - z4.w) : 0.f;
-          }
-        } else {
-#pragma unroll
-          for (int u = 0; u < 16; ++u) {
-            const int64_t n = rs + u;
-            rv[u] = (kvalid && n < row_end) ? ex2(llk[n] - p.lz2[n]) : 0.f;
-          }
-        }
-        uint32_t rh[8], rl[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) split2(rv[2 * u], rv[2 * u + 1], rh[u], rl[u]);
-        tmem_st8(rb + 8 * hh, rh);
-        tmem_st8(rb + 32 + 8 * hh, rl);
+      if (lane == 0) {
+        mbar_arrive(&ctl->zfull[b]);
+        mbar_arrive(&ctl->in_empty[b]);
       }
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&ctl->rfull[b]);
     }
-    // partial statistics of this CTA -> workspace
+    // partial statistics of this CTA -> workspace: warp (quadrant q, quarter h)
+    // reads TMEM lanes 32q.. and columns 64h..64h+63
+    const int q = warp & 3, h = warp >> 2;
+    const int kl = q * 32 + lane;
     const int ldp = p.nfb * kP2Feat;
     float* out = p.part + ((size_t)slab * p.ncb * kP2Comps + (size_t)cbk * kP2Comps + kl) * ldp +
-                 (size_t)fb * kP2Feat;
+                 (size_t)fb * kP2Feat + 64 * h;
     const bool ok = c == nchunks && mbar_wait_flag(&ctl->tdone, 0, abort_flag, p.err, 32);
     if (nchunks > 0 && ok) {
       tc_fence_after();
-      for (int blk = 0; blk < kP2Feat / 32; ++blk) {
+      for (int blk = 0; blk < 2; ++blk) {
         uint32_t tv[32];
-        tmem_ld32(tmem + lane_base + kColT2 + 32 * blk, tv);
+        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + 64 * h + 32 * blk, tv);
         tmem_wait_ld();
         float4* o4 = reinterpret_cast<float4*>(out + 32 * blk);
 #pragma unroll
@@ -649,7 +679,7 @@ __global__ void __launch_bounds__(kP2Threads, 1) full_stats_kernel(const P2Param
       }
     } else {
       const float v = nchunks > 0 ? __int_as_float(0x7fc00000) : 0.f;
-      for (int f = 0; f < kP2Feat; ++f) out[f] = v;
+      for (int f = 0; f < 64; ++f) out[f] = v;
     }
   }
 
@@ -657,7 +687,7 @@ __global__ void __launch_bounds__(kP2Threads, 1) full_stats_kernel(const P2Param
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;" ::"r"(tmem) : "memory");
   }
 }
 
@@ -731,11 +761,11 @@ FullPlan plan_full(int64_t N, int K, int D) {
 
 size_t p1_smem_bytes() {
   return 1024 + (size_t)4 * kXTile + (size_t)kP1LStages * 2 * kLGroup +
-         (size_t)4 * kP1Rows * sizeof(float2) + sizeof(P1Ctl) + 64;
+         (size_t)8 * kP1Rows * sizeof(float2) + sizeof(P1Ctl) + 64;
 }
-size_t p2_smem_bytes() {
-  return 1024 + (size_t)2 * kZStage + (size_t)2 * kP2Rows * kXsStride * 4 + (size_t)kP2Feat * 4 +
-         sizeof(P2Ctl) + 64;
+size_t p2_smem_bytes(int D) {
+  return 1024 + (size_t)4 * kRBlock + (size_t)2 * kZStage + (size_t)2 * kP2Rows * (D + 1) * 4 +
+         (size_t)kP2Feat * 4 + sizeof(P2Ctl) + 16;
 }
 
 struct FullWs {
@@ -745,14 +775,15 @@ struct FullWs {
   float* bvec;
   float2* kconst;
   uint8_t* xsplit;
+  float* xs2;
   float* ll2;
   float* lz2;
+  uint8_t* rt;
   float* part;
   size_t bytes;
 };
 
-FullWs carve_full(void* base, const FullPlan& pl, int64_t N) {
-  (void)N;
+FullWs carve_full(void* base, const FullPlan& pl, int D) {
   WsCarve w(base);
   FullWs ws;
   ws.err = w.take<int>(64);
@@ -761,8 +792,10 @@ FullWs carve_full(void* base, const FullPlan& pl, int64_t N) {
   ws.bvec = w.take<float>((size_t)pl.Kpad * pl.Dp);
   ws.kconst = w.take<float2>(pl.Kpad);
   ws.xsplit = w.take<uint8_t>((size_t)pl.num_tiles * 2 * kXTile);
+  ws.xs2 = w.take<float>((size_t)pl.Npad * (D + 1));
   ws.ll2 = w.take<float>((size_t)pl.Kpad * pl.Npad);
   ws.lz2 = w.take<float>((size_t)pl.Npad);
+  ws.rt = w.take<uint8_t>((size_t)(pl.Npad / kP2Rows) * pl.ncb * 2 * kRBlock);
   ws.part = w.take<float>((size_t)pl.slabs * pl.ncb * kP2Comps * pl.nfb * kP2Feat);
   ws.bytes = w.used + 256;
   return ws;
@@ -782,12 +815,12 @@ size_t full_tc_workspace_bytes(int64_t N, int K, int D) {
   probe.K = K;
   probe.D = D;
   if (K < 1 || !full_tc_supported(probe)) return 0;
-  return carve_full(nullptr, plan_full(N, K, D), N).bytes;
+  return carve_full(nullptr, plan_full(N, K, D), D).bytes;
 }
 
 cudaError_t full_tc_estep(const EstepArgs& a) {
   const FullPlan pl = plan_full(a.N, a.K, a.D);
-  const FullWs ws = carve_full(a.ws, pl, a.N);
+  const FullWs ws = carve_full(a.ws, pl, a.D);
   cudaStream_t st = a.stream;
   // err[0]: device error word; err[1]: max|mu - c| (float bits)
   cudaError_t e = cudaMemsetAsync(ws.err, 0, 2 * sizeof(int), st);
@@ -799,7 +832,7 @@ cudaError_t full_tc_estep(const EstepArgs& a) {
   const int vec_ok = a.sxd == 1 && (reinterpret_cast<uintptr_t>(a.X) & 15) == 0 && a.sxn % 4 == 0;
   const int sblocks = (int)std::min<int64_t>((pl.Npad + 7) / 8, 16 * kSmsFull);
   full_split_kernel<<<sblocks, 256, 0, st>>>(a.X, a.sxn, a.sxd, vec_ok, a.N, a.D, pl.Npad,
-                                             ws.cvec, amax, ws.xsplit, ws.err);
+                                             ws.cvec, amax, ws.xsplit, ws.xs2, ws.err);
 
   P1Params p1;
   p1.xsplit = ws.xsplit;
@@ -824,18 +857,13 @@ cudaError_t full_tc_estep(const EstepArgs& a) {
   profile_mark(false, st);
   full_ll_kernel<<<std::min(pl.num_tiles, kSmsFull), kP1Threads, sm1, st>>>(p1);
 
+  const int nchunk_total = (int)((a.N + kP2Rows - 1) / kP2Rows);
+  full_resp_kernel<<<nchunk_total * pl.ncb, kP2Comps, 0, st>>>(ws.ll2, pl.Npad, ws.lz2, a.N, a.K,
+                                                                pl.ncb, ws.rt);
   P2Params p2;
-  p2.X = a.X;
-  p2.sxn = a.sxn;
-  p2.sxd = a.sxd;
-  p2.cvec = ws.cvec;
-  p2.ll2 = ws.ll2;
-  p2.ld_ll = pl.Npad;
-  p2.lz2 = ws.lz2;
-  p2.amax = amax;
+  p2.rt = ws.rt;
+  p2.xs2 = ws.xs2;
   p2.N = a.N;
-  p2.K = a.K;
-  p2.Kll = pl.Kpad;
   p2.D = a.D;
   p2.nf = pl.nf;
   p2.nfb = pl.nfb;
@@ -844,7 +872,7 @@ cudaError_t full_tc_estep(const EstepArgs& a) {
   p2.rows_per_slab = pl.rows_per_slab;
   p2.part = ws.part;
   p2.err = ws.err;
-  const size_t sm2 = p2_smem_bytes();
+  const size_t sm2 = p2_smem_bytes(a.D);
   e = cudaFuncSetAttribute(full_stats_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)sm2);
   if (e != cudaSuccess) return e;
@@ -856,7 +884,7 @@ cudaError_t full_tc_estep(const EstepArgs& a) {
   full_reduce_kernel<<<rblocks, 256, 0, st>>>(ws.part, pl.slabs, pl.ncb * kP2Comps,
                                               pl.nfb * kP2Feat, a.K, a.D, ws.cvec, amax, ws.err,
                                               a.Nk, a.mu_acc, a.sig, (a.flags & 1u) ? 1 : 0);
-  count_launches(6);
+  count_launches(7);
   return cudaGetLastError();
 }
 
