@@ -31,7 +31,7 @@
 //       power-of-two scaling: x' = x 2^-a (one a per call) and
 //       W'_k = W_k 2^-s_k (per component), undone exactly in the epilogue;
 //   * per-row log-sum-exp over components: warp max (redux.sync.max.f32),
-//     exp2, warp sum (fixed point redux.sync.add.u32), combine the 4 warps
+//     exp2, warp sum (fp32 transpose-reduce over shuffles), combine the 4 warps
 //     that share a row, then exchange one (max, sum) pair per row and CTA
 //     over distributed shared memory -- no second distance pass;
 //   * r = p * 2^(m - logZ2); statistics GEMM  T[k, f] += sum_n R^T[k, n] F[n, f]
@@ -89,6 +89,7 @@ struct Cfg {
   static_assert(kColW + kMaxFeat <= 512, "TMEM budget");
   static_assert(kStages <= kMaxStages, "stage count");
   static_assert(kRB == 16 || kRB == 32, "epilogue row block");
+  static constexpr int kGroups = ROWS == 128 ? 4 : 1;  // independent epilogue row groups
 };
 using IsoCfg = Cfg<128, false>;
 using DiagCfg = Cfg<64, true>;
@@ -113,8 +114,8 @@ struct __align__(8) SmemCtl {
   uint64_t xfull[kMaxStages];
   uint64_t xempty[kMaxStages];
   uint64_t s_full, s_empty, r_full, r_empty, t_done;
-  uint64_t xchg_full[2];
-  uint64_t e_bar[2];   // epilogue-internal sync points (one arrive per warp)
+  uint64_t xchg_full[2][4];  // [tile parity][row group]
+  uint64_t e_bar[2][4];      // epilogue sync points per row group (one arrive per warp)
   uint64_t e_end;
   uint32_t tmem_base;
   volatile int abort_flag;
@@ -288,10 +289,12 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fused_kernel(const TcParams p)
     mbar_init(&ctl->r_full, kEpiWarps);
     mbar_init(&ctl->r_empty, 1);
     mbar_init(&ctl->t_done, 1);
-    mbar_init(&ctl->xchg_full[0], 1);     // local arrive.expect_tx + st.async bytes
-    mbar_init(&ctl->xchg_full[1], 1);
-    mbar_init(&ctl->e_bar[0], kEpiWarps);
-    mbar_init(&ctl->e_bar[1], kEpiWarps);
+    for (int gq = 0; gq < G::kGroups; ++gq) {
+      mbar_init(&ctl->xchg_full[0][gq], 1);   // local arrive.expect_tx + st.async bytes
+      mbar_init(&ctl->xchg_full[1][gq], 1);
+      mbar_init(&ctl->e_bar[0][gq], kEpiWarps / G::kGroups);
+      mbar_init(&ctl->e_bar[1][gq], kEpiWarps / G::kGroups);
+    }
     mbar_init(&ctl->e_end, kEpiWarps);
     ctl->abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -412,7 +415,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fused_kernel(const TcParams p)
     __syncwarp();
   } else if (warp < kEpiWarps) {
     // ------------------------------------------------------------- epilogue
-    // Per tile: A) S^T -> ll, warp max / exp2 / fixed-point warp sum per row;
+    // Per tile: A) S^T -> ll, warp max / exp2 / warp sum per row;
     // B) combine the 4 lane quadrants per row and send one (max, sum) pair to
     // every CTA of the cluster; C) combine the cluster's pairs -> logZ2 and a
     // per-(quadrant, row) scale; D) r = p * scale, per-component sums, R^T
@@ -424,6 +427,12 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fused_kernel(const TcParams p)
     const int tid_e = threadIdx.x;                 // 0..511
     const int g = lane >> 3;                       // lane group for row work
     const bool row_owner = 8 * warp < R;           // warps that own rows in B / C
+    // Row groups: with 128-row tiles the 4 warps of row block cb own its 32
+    // rows end to end (A, B/C and D), so each block synchronises and
+    // exchanges on its own and the blocks drift out of phase; 64-row tiles
+    // use one group.
+    const int grp = G::kGroups == 4 ? cb : 0;
+    constexpr int kGroupRows = R / G::kGroups;
     const int Rw = 8 * warp + (lane & 7);          // row owned in B / C
     for (int t = 0; t < ntiles; ++t) {
       const int b = t % NS;
@@ -456,33 +465,51 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fused_kernel(const TcParams p)
           }
         }
       }
+      // Row maxima over this warp's 32 components (uniform across lanes),
+      // p = 2^(ll - m), then the row sums by a transpose-reduce: log2(32)
+      // shuffle rounds, each halving the rows a lane carries, leave the sum
+      // of row r in lane r (RB = 16: lane r & 15).  Deterministic fp32 order.
+      // The first round is fused with the exponentials to keep registers low.
+      {
+        constexpr int H = RB / 2;
+        float sv[H];
 #pragma unroll
-      for (int gg = 0; gg < RB; gg += 8) {
-        float m8[8];
-        uint32_t u8[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) m8[i] = redux_max(ll[gg + i]);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          // Fixed-point warp sum of p = 2^(ll - m) at 2^-21 resolution:
-          // p*2^21 + 1.5*2^23 holds the rounded integer in the low mantissa
-          // bits; the raw words are summed exactly (mod 2^32) and the 32
-          // copies of the 0x4B400000 bias are removed when decoded.
-          pv[gg + i] = ex2(ll[gg + i] - m8[i]);
-          u8[i] = redux_add(__float_as_uint(fmaf(pv[gg + i], 2097152.0f, 12582912.0f)));
+        for (int i = 0; i < H; ++i) {
+          const float ma = redux_max(ll[i]), mb = redux_max(ll[i + H]);
+          pv[i] = ex2(ll[i] - ma);
+          pv[i + H] = ex2(ll[i + H] - mb);
+          if (lane == 0) {
+            red_m[warp * RB + i] = ma;
+            red_m[warp * RB + i + H] = mb;
+          }
+          if constexpr (RB == 32) {
+            const bool upper = (lane & 16) != 0;
+            const float send = upper ? pv[i] : pv[i + H];
+            const float keep = upper ? pv[i + H] : pv[i];
+            sv[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+          } else {
+            // 16 rows on 32 lanes: fold lanes l and l^16 first, then halve
+            float u = pv[i] + __shfl_xor_sync(0xffffffffu, pv[i], 16);
+            float w = pv[i + H] + __shfl_xor_sync(0xffffffffu, pv[i + H], 16);
+            const bool upper = (lane & 8) != 0;
+            sv[i] = (upper ? w : u) + __shfl_xor_sync(0xffffffffu, upper ? u : w, 8);
+          }
         }
-        if (lane == 0) {
-          float4* dm = reinterpret_cast<float4*>(red_m + warp * RB + gg);
-          uint4* dl = reinterpret_cast<uint4*>(red_l + warp * RB + gg);
-          dm[0] = make_float4(m8[0], m8[1], m8[2], m8[3]);
-          dm[1] = make_float4(m8[4], m8[5], m8[6], m8[7]);
-          dl[0] = make_uint4(u8[0], u8[1], u8[2], u8[3]);
-          dl[1] = make_uint4(u8[4], u8[5], u8[6], u8[7]);
+#pragma unroll
+        for (int half = H / 2; half >= 1; half >>= 1) {  // lane bit of the round = half
+          const bool upper = (lane & half) != 0;
+#pragma unroll
+          for (int i = 0; i < half; ++i) {
+            const float send = upper ? sv[i] : sv[i + half];
+            const float keep = upper ? sv[i + half] : sv[i];
+            sv[i] = keep + __shfl_xor_sync(0xffffffffu, send, half);
+          }
         }
+        if (lane < RB) red_l[warp * RB + lane] = sv[0];
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(&ctl->e_bar[0]);
-      if (!mbar_wait(&ctl->e_bar[0], t & 1, ctl, p.err, 256)) break;
+      if (lane == 0) mbar_arrive(&ctl->e_bar[0][grp]);
+      if (!mbar_wait(&ctl->e_bar[0][grp], t & 1, ctl, p.err, 256)) break;
 
       // ---- B + C: warp w < R/8 owns rows Rw = 8w + (lane & 7); lane group g
       // handles lane quadrant g and cluster peers g and g + 4.
@@ -490,19 +517,20 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fused_kernel(const TcParams p)
       if (row_owner) {
         const int ri = Rw % RB, blk = Rw / RB;
         const float mg = red_m[(g + 4 * blk) * RB + ri];
-        const uint32_t raw = __float_as_uint(red_l[(g + 4 * blk) * RB + ri]) - 32u * 0x4B400000u;
-        const float ug = (float)raw * (1.0f / 2097152.0f);
+        const float ug = red_l[(g + 4 * blk) * RB + ri];
         float M = fmaxf(mg, __shfl_xor_sync(0xffffffffu, mg, 8));
         M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, 16));
         float L = ug * ex2(mg - M);
         L += __shfl_xor_sync(0xffffffffu, L, 8);
         L += __shfl_xor_sync(0xffffffffu, L, 16);
         const uint32_t my_slot = smem_u32(&xchg[(slot * kMaxCluster + rank) * R + Rw]);
-        const uint32_t my_bar = smem_u32(&ctl->xchg_full[slot]);
-        if (tid_e == 0) mbar_arrive_expect_tx(&ctl->xchg_full[slot], (uint32_t)(p.C * R * 8));
+        const int rg = Rw / kGroupRows;               // row group of this row (== grp)
+        const uint32_t my_bar = smem_u32(&ctl->xchg_full[slot][rg]);
+        if (tid_e == 32 * (rg * kGroupRows / 8))      // first owner warp of the group, lane 0
+          mbar_arrive_expect_tx(&ctl->xchg_full[slot][rg], (uint32_t)(p.C * kGroupRows * 8));
         if (g < p.C) st_async_f2(map_to_cta(my_slot, g), M, L, map_to_cta(my_bar, g));
         if (g + 4 < p.C) st_async_f2(map_to_cta(my_slot, g + 4), M, L, map_to_cta(my_bar, g + 4));
-        const bool ok = mbar_wait<true>(&ctl->xchg_full[slot], (t >> 1) & 1, ctl, p.err, 32);
+        const bool ok = mbar_wait<true>(&ctl->xchg_full[slot][rg], (t >> 1) & 1, ctl, p.err, 32);
         float2 e0 = make_float2(-3e38f, 0.f), e1 = make_float2(-3e38f, 0.f);
         if (g < p.C) e0 = xchg[(slot * kMaxCluster + g) * R + Rw];
         if (g + 4 < p.C) e1 = xchg[(slot * kMaxCluster + g + 4) * R + Rw];
@@ -518,8 +546,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fused_kernel(const TcParams p)
         scale_s[g * R + Rw] = valid ? ex2(mg - lz2) : 0.f;
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(&ctl->e_bar[1]);
-      if (!mbar_wait(&ctl->e_bar[1], t & 1, ctl, p.err, 512)) break;
+      if (lane == 0) mbar_arrive(&ctl->e_bar[1][grp]);
+      if (!mbar_wait(&ctl->e_bar[1][grp], t & 1, ctl, p.err, 512)) break;
 
       // ---- D: r = p * scale, per-component sums, R^T into TMEM (16 rows at a time)
       const float* sc = scale_s + q * R + RB * cb;

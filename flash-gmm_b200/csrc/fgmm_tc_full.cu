@@ -496,28 +496,28 @@ __global__ void __launch_bounds__(kP2Comps) full_resp_kernel(const float* __rest
   const bool kvalid = k < K;
   const float* llk = ll2 + (size_t)(kvalid ? k : 0) * ld_ll + r0;
   uint8_t* blk = rt + ((size_t)chunk * ncb + cbk) * (2 * kRBlock);
-#pragma unroll 1
-  for (int g = 0; g < kP2Rows / 8; ++g) {
-    float rv[8];
-    if (kvalid && r0 + 8 * g + 8 <= N) {
-      const float4 a = __ldg(reinterpret_cast<const float4*>(llk + 8 * g));
-      const float4 b = __ldg(reinterpret_cast<const float4*>(llk + 8 * g + 4));
-      rv[0] = ex2(a.x - lz[8 * g + 0]);
-      rv[1] = ex2(a.y - lz[8 * g + 1]);
-      rv[2] = ex2(a.z - lz[8 * g + 2]);
-      rv[3] = ex2(a.w - lz[8 * g + 3]);
-      rv[4] = ex2(b.x - lz[8 * g + 4]);
-      rv[5] = ex2(b.y - lz[8 * g + 5]);
-      rv[6] = ex2(b.z - lz[8 * g + 6]);
-      rv[7] = ex2(b.w - lz[8 * g + 7]);
-    } else {
+  float rv[kP2Rows];
+  if (kvalid && r0 + kP2Rows <= N) {
+    float4 v4[kP2Rows / 4];
 #pragma unroll
-      for (int u = 0; u < 8; ++u)
-        rv[u] = (kvalid && r0 + 8 * g + u < N) ? ex2(llk[8 * g + u] - lz[8 * g + u]) : 0.f;
+    for (int u = 0; u < kP2Rows / 4; ++u) v4[u] = __ldg(reinterpret_cast<const float4*>(llk) + u);
+#pragma unroll
+    for (int u = 0; u < kP2Rows / 4; ++u) {
+      rv[4 * u + 0] = ex2(v4[u].x - lz[4 * u + 0]);
+      rv[4 * u + 1] = ex2(v4[u].y - lz[4 * u + 1]);
+      rv[4 * u + 2] = ex2(v4[u].z - lz[4 * u + 2]);
+      rv[4 * u + 3] = ex2(v4[u].w - lz[4 * u + 3]);
     }
+  } else {
+#pragma unroll
+    for (int u = 0; u < kP2Rows; ++u)
+      rv[u] = (kvalid && r0 + u < N) ? ex2(llk[u] - lz[u]) : 0.f;
+  }
+#pragma unroll
+  for (int g = 0; g < kP2Rows / 8; ++g) {
     uint32_t hi[4], lo[4];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) split2(rv[2 * u], rv[2 * u + 1], hi[u], lo[u]);
+    for (int u = 0; u < 4; ++u) split2(rv[8 * g + 2 * u], rv[8 * g + 2 * u + 1], hi[u], lo[u]);
     const uint32_t off = xoff(t, 8 * g, kRBlock);
     *reinterpret_cast<uint4*>(blk + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
     *reinterpret_cast<uint4*>(blk + kRBlock + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
