@@ -70,6 +70,7 @@ constexpr int kMmaWarp = kEpiWarps + 1;                     // 17
 constexpr int kThreads = (kEpiWarps + 4) * 32;              // 640: 5 warpgroups
 constexpr int kMaxCluster = 8;
 constexpr int kMaxStages = 4;
+constexpr int kSplitRows = 4;                               // rows per warp step (split pass)
 constexpr int kSms = 148;                                   // B200
 
 // Compile-time shape of one fused-kernel instantiation.
@@ -656,54 +657,67 @@ __global__ void __launch_bounds__(256) tc_split_kernel(
   const int f = 4 * lane;
   float4 cc = make_float4(0.f, 0.f, 0.f, 0.f);
   if (DIAG && lane < nact) cc = *reinterpret_cast<const float4*>(cvec + f);
-  for (int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5); row < rows_pad;
-       row += (int64_t)gridDim.x * 8) {
-    float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-    const bool live = row < N;
-    if (lane < nact && live) {
-      const float* src = X + row * sxn;
-      if (vec_ok && f + 3 < D) {
-        x = __ldg(reinterpret_cast<const float4*>(src + f));
-      } else {
-        if (f + 0 < D) x.x = __ldg(src + (int64_t)(f + 0) * sxd);
-        if (f + 1 < D) x.y = __ldg(src + (int64_t)(f + 1) * sxd);
-        if (f + 2 < D) x.z = __ldg(src + (int64_t)(f + 2) * sxd);
-        if (f + 3 < D) x.w = __ldg(src + (int64_t)(f + 3) * sxd);
-      }
-      if (DIAG) {  // padding features have x = c = 0
-        x.x -= cc.x; x.y -= cc.y; x.z -= cc.z; x.w -= cc.w;
-      }
-    }
-    if (lane < nact) {
-      const float4 xs = make_float4(ldexpf(x.x, -a), ldexpf(x.y, -a), ldexpf(x.z, -a),
-                                    ldexpf(x.w, -a));
-      float mx = fmaxf(fmaxf(fabsf(xs.x), fabsf(xs.y)), fmaxf(fabsf(xs.z), fabsf(xs.w)));
-      if (DIAG) mx = fmaxf(mx, mx * mx);
-      if (!(mx < 65504.f)) atomicOr(err, 0x10000);  // outside fp16 range (or NaN)
-      uint8_t* tile = xsplit + (row / ROWS) * stage_bytes;
-      const int r = (int)(row % ROWS);
-      uint32_t h0, l0, h1, l1;
-      split2(xs.x, xs.y, h0, l0);
-      split2(xs.z, xs.w, h1, l1);
-      const uint32_t off = xoff(r, DIAG ? Dp + f : f, kChunk);
-      *reinterpret_cast<uint2*>(tile + off) = make_uint2(h0, h1);
-      *reinterpret_cast<uint2*>(tile + nch * kChunk + off) = make_uint2(l0, l1);
-      if (DIAG) {
-        split2(xs.x * xs.x, xs.y * xs.y, h0, l0);
-        split2(xs.z * xs.z, xs.w * xs.w, h1, l1);
-        const uint32_t off2 = xoff(r, f, kChunk);
-        *reinterpret_cast<uint2*>(tile + off2) = make_uint2(h0, h1);
-        *reinterpret_cast<uint2*>(tile + nch * kChunk + off2) = make_uint2(l0, l1);
-      }
-    }
-    if (!DIAG) {
-      float sq = x.x * x.x;
-      sq = fmaf(x.y, x.y, sq);
-      sq = fmaf(x.z, x.z, sq);
-      sq = fmaf(x.w, x.w, sq);
+  // Each warp takes kSplitRows consecutive rows per step and issues all of
+  // their loads before converting, to keep enough bytes in flight for HBM.
+  for (int64_t row0 = ((int64_t)blockIdx.x * 8 + (threadIdx.x >> 5)) * kSplitRows; row0 < rows_pad;
+       row0 += (int64_t)gridDim.x * 8 * kSplitRows) {
+    float4 xr[kSplitRows];
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
-      if (lane == 0) xsq[row] = sq;
+    for (int u = 0; u < kSplitRows; ++u) {
+      const int64_t row = row0 + u;
+      float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (lane < nact && row < N) {
+        const float* src = X + row * sxn;
+        if (vec_ok && f + 3 < D) {
+          x = __ldg(reinterpret_cast<const float4*>(src + f));
+        } else {
+          if (f + 0 < D) x.x = __ldg(src + (int64_t)(f + 0) * sxd);
+          if (f + 1 < D) x.y = __ldg(src + (int64_t)(f + 1) * sxd);
+          if (f + 2 < D) x.z = __ldg(src + (int64_t)(f + 2) * sxd);
+          if (f + 3 < D) x.w = __ldg(src + (int64_t)(f + 3) * sxd);
+        }
+        if (DIAG) {  // padding features have x = c = 0
+          x.x -= cc.x; x.y -= cc.y; x.z -= cc.z; x.w -= cc.w;
+        }
+      }
+      xr[u] = x;
+    }
+#pragma unroll
+    for (int u = 0; u < kSplitRows; ++u) {
+      const int64_t row = row0 + u;
+      if (row >= rows_pad) break;
+      const float4 x = xr[u];
+      if (lane < nact) {
+        const float4 xs = make_float4(ldexpf(x.x, -a), ldexpf(x.y, -a), ldexpf(x.z, -a),
+                                      ldexpf(x.w, -a));
+        float mx = fmaxf(fmaxf(fabsf(xs.x), fabsf(xs.y)), fmaxf(fabsf(xs.z), fabsf(xs.w)));
+        if (DIAG) mx = fmaxf(mx, mx * mx);
+        if (!(mx < 65504.f)) atomicOr(err, 0x10000);  // outside fp16 range (or NaN)
+        uint8_t* tile = xsplit + (row / ROWS) * stage_bytes;
+        const int r = (int)(row % ROWS);
+        uint32_t h0, l0, h1, l1;
+        split2(xs.x, xs.y, h0, l0);
+        split2(xs.z, xs.w, h1, l1);
+        const uint32_t off = xoff(r, DIAG ? Dp + f : f, kChunk);
+        *reinterpret_cast<uint2*>(tile + off) = make_uint2(h0, h1);
+        *reinterpret_cast<uint2*>(tile + nch * kChunk + off) = make_uint2(l0, l1);
+        if (DIAG) {
+          split2(xs.x * xs.x, xs.y * xs.y, h0, l0);
+          split2(xs.z * xs.z, xs.w * xs.w, h1, l1);
+          const uint32_t off2 = xoff(r, f, kChunk);
+          *reinterpret_cast<uint2*>(tile + off2) = make_uint2(h0, h1);
+          *reinterpret_cast<uint2*>(tile + nch * kChunk + off2) = make_uint2(l0, l1);
+        }
+      }
+      if (!DIAG) {
+        float sq = x.x * x.x;
+        sq = fmaf(x.y, x.y, sq);
+        sq = fmaf(x.z, x.z, sq);
+        sq = fmaf(x.w, x.w, sq);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+        if (lane == 0) xsq[row] = sq;
+      }
     }
   }
 }
@@ -954,7 +968,7 @@ cudaError_t tc_estep(int variant, const EstepArgs& a) {
   if (e != cudaSuccess) return e;
   const int64_t rows_pad = (int64_t)pl.num_tiles * pl.rows;
   const int vec_ok = a.sxd == 1 && (reinterpret_cast<uintptr_t>(a.X) & 15) == 0 && a.sxn % 4 == 0;
-  const int sblocks = (int)std::min<int64_t>((rows_pad + 7) / 8, 16 * kSms);
+  const int sblocks = (int)std::min<int64_t>((rows_pad + 8 * kSplitRows - 1) / (8 * kSplitRows), 16 * kSms);
   if (pl.diag) {
     centre_kernel<<<pl.Dp, 256, 0, a.stream>>>(a.mu, a.smk, a.smd, a.K, a.D, cvec,
                                                        err + 1);
