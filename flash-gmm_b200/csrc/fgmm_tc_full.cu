@@ -18,8 +18,9 @@
 //   while the epilogue drains group g.
 //
 // Pass 2 (full_stats_kernel, components on TMEM lanes): per 64-row chunk,
-//   T[k, f] += sum_n r_nk z_nf with z = [x~_i x~_j (i <= j), x~_i, 1]
-//   (D(D+1)/2 + D + 1 features; the last two give mu_acc and Nk).  A = R^T
+//   T[k, f] += sum_n r_nk z_nf with z = [x~_i x~_j (i <= j), x~_i, 1] laid out
+//   in quads of 4 columns (2244 columns at D = 64; mu_acc and Nk come from the
+//   same GEMM).  A = R^T
 //   (fp16 hi/lo written to TMEM from ll2 and logZ), B = the z chunk (fp16
 //   hi/lo, generated on chip from x~ into the MN-major shared-memory layout),
 //   N = 256 features per CTA.  CTAs tile (feature block, component block,
@@ -49,6 +50,8 @@ constexpr int kP1Threads = 18 * 32;
 constexpr int kP1LStages = 2;
 constexpr int kXTile = kP1Rows * 128;        // 16 KB: one hi (or lo) x~ tile, 64 features
 constexpr int kLGroup = 256 * 128;           // 32 KB: one hi (or lo) group of L columns
+constexpr int kP1BSlots = 4;                 // ring of per-group b vectors + constants
+constexpr int kBSlot = 256 * 4 + 16 * 8;     // bytes: b (G*Dp <= 256 floats) + 16 float2
 
 // ---- pass 2
 constexpr int kP2Rows = 64;                  // rows per chunk (MMA K extent)
@@ -61,13 +64,12 @@ constexpr int kP2Threads = 18 * 32;
 constexpr int kZChunk = kP2Rows * 128;       // 8 KB: 64 rows x 64 features (fp16)
 constexpr int kZStage = 2 * 4 * kZChunk;     // hi + lo, 256 features: 64 KB
 constexpr int kRBlock = kP2Comps * 128;      // 16 KB: R^T hi (or lo), 128 components x 64 rows
-constexpr uint32_t kPadFeature = 0xFFFFu;    // feature slot code of a zero (padding) feature
 
 struct P1Params {
   const uint8_t* xsplit;   // [num_tiles][hi 16 KB | lo 16 KB]  x~ 2^-a1, swizzled K-major
   const uint8_t* lgroups;  // [num_groups][hi 32 KB | lo 32 KB] L columns 2^-s_k, K-major
   const float* bvec;       // [Kpad][Dp]  b_k = (mu_k - c)^T L_k
-  const float2* kconst;    // [Kpad]  {const_k in log2 units, s_k}
+  const float2* kconst;    // [num_groups][16]  {const_k in log2 units, s_k} per group slot
   const int* amax;         // max|mu - c| (float bits) -> a1
   int64_t N;
   int K, Dp, G, num_groups, num_tiles;
@@ -80,6 +82,7 @@ struct P1Params {
 
 struct __align__(8) P1Ctl {
   uint64_t xfull[2], xempty[2];
+  uint64_t bfull[kP1BSlots], bempty[kP1BSlots];
   uint64_t lfull[kP1LStages], lempty[kP1LStages];
   uint64_t afull[2], aempty[2];
   uint64_t lse_bar;
@@ -179,8 +182,15 @@ __global__ void __launch_bounds__(64) full_prep_kernel(
       c = ((double)lpi[k] + s_logd[0] + s_logd[1] - 0.5 * D * kLog2Pi) * kLog2E;
       if (!(c > -1e30)) c = -1e30;
     }
-    kconst[k] = make_float2((float)c, (float)sk);
+    kconst[(size_t)(k / G) * 16 + (k % G)] = make_float2((float)c, (float)sk);
   }
+}
+
+// Row stride (floats) of the pass-2 x~ rows: D values, the constant 1, zeros,
+// even (8-byte aligned pairs) and covering every j-quad.
+__host__ __device__ __forceinline__ int xs2_stride(int D) {
+  const int need = D + 2 > 4 * ((D + 3) / 4) ? D + 2 : 4 * ((D + 3) / 4);
+  return (need + 1) & ~1;
 }
 
 // Split pass (any X strides), one warp per row, lane l carries features
@@ -205,8 +215,12 @@ __global__ void __launch_bounds__(256) full_split_kernel(
   }
   for (int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5); row < rows_pad;
        row += (int64_t)gridDim.x * 8) {
-    float* x2row = xs2 + row * (D + 1);
-    if (lane == 16) x2row[D] = 1.0f;
+    const int xs_stride = xs2_stride(D);
+    float* x2row = xs2 + row * xs_stride;
+    if (lane == 16) {  // constant slot D, zeros up to the stride
+      x2row[D] = 1.0f;
+      for (int d = D + 1; d < xs_stride; ++d) x2row[d] = 0.f;
+    }
     if (!active) continue;
     float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
     if (row < N) {
@@ -228,10 +242,15 @@ __global__ void __launch_bounds__(256) full_split_kernel(
       if (f + 2 >= D) x.z = 0.f;
       if (f + 3 >= D) x.w = 0.f;
     }
-    if (f + 0 < D) x2row[f + 0] = ldexpf(x.x, -a2);
-    if (f + 1 < D) x2row[f + 1] = ldexpf(x.y, -a2);
-    if (f + 2 < D) x2row[f + 2] = ldexpf(x.z, -a2);
-    if (f + 3 < D) x2row[f + 3] = ldexpf(x.w, -a2);
+    const float4 x2 = make_float4(ldexpf(x.x, -a2), ldexpf(x.y, -a2), ldexpf(x.z, -a2),
+                                  ldexpf(x.w, -a2));
+    if (f + 0 < D) x2row[f + 0] = x2.x;
+    if (f + 1 < D) x2row[f + 1] = x2.y;
+    if (f + 2 < D) x2row[f + 2] = x2.z;
+    if (f + 3 < D) x2row[f + 3] = x2.w;
+    // products of two such values must stay inside fp16's range in pass 2
+    if (!(fmaxf(fmaxf(fabsf(x2.x), fabsf(x2.y)), fmaxf(fabsf(x2.z), fabsf(x2.w))) < 255.f))
+      atomicOr(err, 0x20000);
     x = make_float4(ldexpf(x.x, -a1), ldexpf(x.y, -a1), ldexpf(x.z, -a1), ldexpf(x.w, -a1));
     const float mx = fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w)));
     if (!(mx < 65504.f)) atomicOr(err, 0x10000);  // outside fp16 range (or NaN)
@@ -253,8 +272,9 @@ __global__ void __launch_bounds__(kP1Threads, 1) full_ll_kernel(const P1Params p
   uint8_t* smem = align1024(smem_raw);
   uint8_t* xs = smem;                                         // [2][hi | lo] x~ tiles
   uint8_t* lsm = smem + 4 * kXTile;                           // [stages][hi | lo] L groups
-  float2* red = reinterpret_cast<float2*>(lsm + kP1LStages * 2 * kLGroup);  // [2][4][128]
-  P1Ctl* ctl = reinterpret_cast<P1Ctl*>(red + 8 * kP1Rows);
+  float2* red = reinterpret_cast<float2*>(lsm + kP1LStages * 2 * kLGroup);  // [2][2][4][128]
+  uint8_t* bst = reinterpret_cast<uint8_t*>(red + 16 * kP1Rows);            // [slots][kBSlot]
+  P1Ctl* ctl = reinterpret_cast<P1Ctl*>(bst + kP1BSlots * kBSlot);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ntiles = (p.num_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
@@ -272,6 +292,10 @@ __global__ void __launch_bounds__(kP1Threads, 1) full_ll_kernel(const P1Params p
       mbar_init(&ctl->lempty[i], 1);
     }
     mbar_init(&ctl->lse_bar, kP1EpiWarps);
+    for (int i = 0; i < kP1BSlots; ++i) {
+      mbar_init(&ctl->bfull[i], 1);
+      mbar_init(&ctl->bempty[i], kP1EpiWarps);
+    }
     ctl->abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -287,58 +311,74 @@ __global__ void __launch_bounds__(kP1Threads, 1) full_ll_kernel(const P1Params p
   const uint32_t tmem = ctl->tmem_base;
   const int xa = scale_exp_to(__int_as_float(*p.amax), 5);
 
+  // Tiles of this CTA: blockIdx.x + i * gridDim.x, processed in pairs (2q, 2q+1):
+  // each L group is loaded once per pair and multiplied with both x~ tiles,
+  // the two products alternating between the two TMEM accumulators.
+  const int npairs = (ntiles + 1) / 2;
+  auto pair_tiles = [&](int q) -> int { return 2 * q + 1 < ntiles ? 2 : 1; };
+  auto tile_of = [&](int q, int tt) -> int64_t {
+    return (int64_t)blockIdx.x + (int64_t)(2 * q + tt) * gridDim.x;
+  };
+
   if (warp == kP1MmaWarp) {
     if (lane == 0) {
       const uint32_t idesc = idesc_f16(p.G * p.Dp, false);
       const int ks = p.Dp / 16;
-      int gi = 0;
+      int gi = 0, li = 0;  // accumulator uses, L-group loads
       bool ok = true;
-      for (int t = 0; t < ntiles && ok; ++t) {
-        const int xb = t & 1;
-        if (!mbar_wait_flag(&ctl->xfull[xb], (t >> 1) & 1, abort_flag, p.err, 1)) break;
-        for (int g = 0; g < p.num_groups; ++g, ++gi) {
-          const int st = gi % kP1LStages, acc = gi & 1;
-          if (!mbar_wait_flag(&ctl->lfull[st], (gi / kP1LStages) & 1, abort_flag, p.err, 2) ||
-              !mbar_wait_flag(&ctl->aempty[acc], ((gi >> 1) & 1) ^ 1, abort_flag, p.err, 4)) {
+      for (int q = 0; q < npairs && ok; ++q) {
+        const int nt = pair_tiles(q);
+        for (int tt = 0; tt < nt && ok; ++tt)
+          ok = mbar_wait_flag(&ctl->xfull[tt], q & 1, abort_flag, p.err, 1);
+        for (int g = 0; g < p.num_groups && ok; ++g, ++li) {
+          const int st = li % kP1LStages;
+          if (!mbar_wait_flag(&ctl->lfull[st], (li / kP1LStages) & 1, abort_flag, p.err, 2)) {
             ok = false;
             break;
           }
-          tc_fence_after();
-          const uint32_t xhi = smem_u32(xs + xb * 2 * kXTile), xlo = xhi + kXTile;
           const uint32_t lhi = smem_u32(lsm + st * 2 * kLGroup), llo = lhi + kLGroup;
-          // terms x_lo*L_hi, x_hi*L_lo, x_hi*L_hi (smallest magnitudes first)
-          for (int term = 0; term < 3; ++term) {
-            const uint32_t a = term == 0 ? xlo : xhi;
-            const uint32_t b = term == 1 ? llo : lhi;
-            for (int s = 0; s < ks; ++s)
-              mma_ss(tmem + acc * 256, desc_kmajor(a + 32 * s), desc_kmajor(b + 32 * s), idesc,
-                     (term == 0 && s == 0) ? 0u : 1u);
+          for (int tt = 0; tt < nt; ++tt, ++gi) {
+            const int acc = gi & 1;
+            if (!mbar_wait_flag(&ctl->aempty[acc], ((gi >> 1) & 1) ^ 1, abort_flag, p.err, 4)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t xhi = smem_u32(xs + tt * 2 * kXTile), xlo = xhi + kXTile;
+            // terms x_lo*L_hi, x_hi*L_lo, x_hi*L_hi (smallest magnitudes first)
+            for (int term = 0; term < 3; ++term) {
+              const uint32_t a = term == 0 ? xlo : xhi;
+              const uint32_t b = term == 1 ? llo : lhi;
+              for (int s = 0; s < ks; ++s)
+                mma_ss(tmem + acc * 256, desc_kmajor(a + 32 * s), desc_kmajor(b + 32 * s), idesc,
+                       (term == 0 && s == 0) ? 0u : 1u);
+            }
+            tc_commit(&ctl->afull[acc]);
           }
-          tc_commit(&ctl->afull[acc]);
           tc_commit(&ctl->lempty[st]);
         }
-        tc_commit(&ctl->xempty[xb]);
+        for (int tt = 0; tt < nt; ++tt) tc_commit(&ctl->xempty[tt]);
       }
     }
     __syncwarp();
   } else if (warp == kP1LoadWarp) {
     if (lane == 0) {
-      auto load_x = [&](int t) -> bool {
-        const int xb = t & 1;
-        if (!mbar_wait_flag(&ctl->xempty[xb], ((t >> 1) & 1) ^ 1, abort_flag, p.err, 8))
-          return false;
-        const int64_t tile = (int64_t)blockIdx.x + (int64_t)t * gridDim.x;
-        mbar_arrive_expect_tx(&ctl->xfull[xb], 2 * kXTile);
-        bulk_g2s(smem_u32(xs + xb * 2 * kXTile), p.xsplit + tile * (2 * kXTile), 2 * kXTile,
-                 &ctl->xfull[xb]);
-        return true;
-      };
-      int gi = 0;
-      bool ok = ntiles > 0 ? load_x(0) : true;
-      for (int t = 0; t < ntiles && ok; ++t) {
-        for (int g = 0; g < p.num_groups; ++g, ++gi) {
-          const int st = gi % kP1LStages;
-          if (!mbar_wait_flag(&ctl->lempty[st], ((gi / kP1LStages) & 1) ^ 1, abort_flag, p.err,
+      int li = 0;
+      bool ok = true;
+      for (int q = 0; q < npairs && ok; ++q) {
+        const int nt = pair_tiles(q);
+        for (int tt = 0; tt < nt && ok; ++tt) {
+          if (!mbar_wait_flag(&ctl->xempty[tt], (q & 1) ^ 1, abort_flag, p.err, 8)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&ctl->xfull[tt], 2 * kXTile);
+          bulk_g2s(smem_u32(xs + tt * 2 * kXTile), p.xsplit + tile_of(q, tt) * (2 * kXTile),
+                   2 * kXTile, &ctl->xfull[tt]);
+        }
+        for (int g = 0; g < p.num_groups && ok; ++g, ++li) {
+          const int st = li % kP1LStages;
+          if (!mbar_wait_flag(&ctl->lempty[st], ((li / kP1LStages) & 1) ^ 1, abort_flag, p.err,
                               16)) {
             ok = false;
             break;
@@ -346,96 +386,121 @@ __global__ void __launch_bounds__(kP1Threads, 1) full_ll_kernel(const P1Params p
           mbar_arrive_expect_tx(&ctl->lfull[st], 2 * kLGroup);
           bulk_g2s(smem_u32(lsm + st * 2 * kLGroup), p.lgroups + (size_t)g * (2 * kLGroup),
                    2 * kLGroup, &ctl->lfull[st]);
-          if (g == 0 && t + 1 < ntiles && !load_x(t + 1)) {
+          const int bs = li % kP1BSlots;
+          if (!mbar_wait_flag(&ctl->bempty[bs], ((li / kP1BSlots) & 1) ^ 1, abort_flag, p.err,
+                              128)) {
             ok = false;
             break;
           }
+          const uint32_t bbytes = (uint32_t)(p.G * p.Dp * 4);
+          mbar_arrive_expect_tx(&ctl->bfull[bs], bbytes + 128u);
+          bulk_g2s(smem_u32(bst + bs * kBSlot), p.bvec + (size_t)g * p.G * p.Dp, bbytes,
+                   &ctl->bfull[bs]);
+          bulk_g2s(smem_u32(bst + bs * kBSlot + 1024), p.kconst + (size_t)g * 16, 128u,
+                   &ctl->bfull[bs]);
         }
       }
     }
     __syncwarp();
   } else if (warp < kP1EpiWarps) {
-    // thread = row (TMEM lane); warp quarter h takes components i = h, h+4, ...
-    const int q = warp & 3, h = warp >> 2;
-    const int row = q * 32 + lane;
-    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    // thread = row (TMEM lane) of tile tt; warp quarter h takes components
+    // i = h, h+4, ... of each group
+    const int q4 = warp & 3, h = warp >> 2;
+    const int row = q4 * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
     const float kHalfLog2E = 0.72134752044448170f;
-    int gi = 0;
-    for (int t = 0; t < ntiles; ++t) {
-      const int64_t n = ((int64_t)blockIdx.x + (int64_t)t * gridDim.x) * kP1Rows + row;
-      const bool live = n < p.N;
-      float m = -3.0e38f, l = 0.f;
+    int gi = 0, li = 0;
+    for (int q = 0; q < npairs; ++q) {
+      const int nt = pair_tiles(q);
+      float m[2] = {-3.0e38f, -3.0e38f}, l[2] = {0.f, 0.f};
       bool ok = true;
-      for (int g = 0; g < p.num_groups; ++g, ++gi) {
-        const int acc = gi & 1;
-        if (!mbar_wait_flag(&ctl->afull[acc], (gi >> 1) & 1, abort_flag, p.err, 32)) {
+      for (int g = 0; g < p.num_groups && ok; ++g, ++li) {
+        const int bs = li % kP1BSlots;
+        if (!mbar_wait_flag(&ctl->bfull[bs], (li / kP1BSlots) & 1, abort_flag, p.err, 256)) {
           ok = false;
           break;
         }
-        tc_fence_after();
-        for (int i = h; i < p.G; i += 4) {
-          const int k = g * p.G + i;
-          if (k >= p.K) break;
-          const float2 kc = p.kconst[k];
-          const float sc = ldexpf(1.0f, xa + (int)kc.y);  // V = V' 2^(a1 + s_k)
-          const float4* bk = reinterpret_cast<const float4*>(p.bvec + (size_t)k * p.Dp);
-          float mh[4] = {0.f, 0.f, 0.f, 0.f};  // independent partial sums of maha
-          for (int c = 0; c < p.Dp; c += 32) {
-            uint32_t v[32];
-            float bb[32];
-            const bool two = c + 16 < p.Dp;
-            tmem_ld16(tmem + lane_base + acc * 256 + i * p.Dp + c, v);
-            if (two) tmem_ld16(tmem + lane_base + acc * 256 + i * p.Dp + c + 16, v + 16);
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-              const float4 b4 = (u < 4 || two) ? __ldg(bk + c / 4 + u) : make_float4(0.f, 0.f, 0.f, 0.f);
-              bb[4 * u + 0] = b4.x;
-              bb[4 * u + 1] = b4.y;
-              bb[4 * u + 2] = b4.z;
-              bb[4 * u + 3] = b4.w;
-            }
-            tmem_wait_ld();
-            if (!two) {
-#pragma unroll
-              for (int u = 16; u < 32; ++u) v[u] = 0u;
-            }
-#pragma unroll
-            for (int u = 0; u < 32; ++u) {
-              const float dv = fmaf(__uint_as_float(v[u]), sc, -bb[u]);
-              mh[u & 3] = fmaf(dv, dv, mh[u & 3]);
-            }
+        const float* bgrp = reinterpret_cast<const float*>(bst + bs * kBSlot);
+        const float2* kgrp = reinterpret_cast<const float2*>(bst + bs * kBSlot + 1024);
+        for (int tt = 0; tt < nt; ++tt, ++gi) {
+          const int acc = gi & 1;
+          if (!mbar_wait_flag(&ctl->afull[acc], (gi >> 1) & 1, abort_flag, p.err, 32)) {
+            ok = false;
+            break;
           }
-          const float maha = (mh[0] + mh[1]) + (mh[2] + mh[3]);
-          const float ll2 = fmaf(-kHalfLog2E, maha, kc.x);
-          if (ll2 > m) {
-            l = fmaf(l, ex2(m - ll2), 1.0f);
-            m = ll2;
-          } else {
-            l += ex2(ll2 - m);
+          tc_fence_after();
+          const int64_t n = tile_of(q, tt) * kP1Rows + row;
+          const bool live = n < p.N;
+          for (int i = h; i < p.G; i += 4) {
+            const int k = g * p.G + i;
+            if (k >= p.K) break;
+            const float2 kc = kgrp[i];
+            const float sc = ldexpf(1.0f, xa + (int)kc.y);  // V = V' 2^(a1 + s_k)
+            const float4* bk = reinterpret_cast<const float4*>(bgrp + i * p.Dp);
+            float mh[4] = {0.f, 0.f, 0.f, 0.f};  // independent partial sums of maha
+            for (int c = 0; c < p.Dp; c += 32) {
+              uint32_t v[32];
+              float bb[32];
+              const bool two = c + 16 < p.Dp;
+              tmem_ld16(tmem + lane_base + acc * 256 + i * p.Dp + c, v);
+              if (two) tmem_ld16(tmem + lane_base + acc * 256 + i * p.Dp + c + 16, v + 16);
+#pragma unroll
+              for (int u = 0; u < 8; ++u) {
+                const float4 b4 = (u < 4 || two) ? bk[c / 4 + u] : make_float4(0.f, 0.f, 0.f, 0.f);
+                bb[4 * u + 0] = b4.x;
+                bb[4 * u + 1] = b4.y;
+                bb[4 * u + 2] = b4.z;
+                bb[4 * u + 3] = b4.w;
+              }
+              tmem_wait_ld();
+              if (!two) {
+#pragma unroll
+                for (int u = 16; u < 32; ++u) v[u] = 0u;
+              }
+#pragma unroll
+              for (int u = 0; u < 32; ++u) {
+                const float dv = fmaf(__uint_as_float(v[u]), sc, -bb[u]);
+                mh[u & 3] = fmaf(dv, dv, mh[u & 3]);
+              }
+            }
+            const float maha = (mh[0] + mh[1]) + (mh[2] + mh[3]);
+            const float ll2 = fmaf(-kHalfLog2E, maha, kc.x);
+            if (ll2 > m[tt]) {
+              l[tt] = fmaf(l[tt], ex2(m[tt] - ll2), 1.0f);
+              m[tt] = ll2;
+            } else {
+              l[tt] += ex2(ll2 - m[tt]);
+            }
+            if (live) p.ll2[(size_t)k * p.ld_ll + n] = ll2;
           }
-          if (live) p.ll2[(size_t)k * p.ld_ll + n] = ll2;
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&ctl->aempty[acc]);
         }
-        tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&ctl->aempty[acc]);
+        if (lane == 0) mbar_arrive(&ctl->bempty[bs]);
       }
       if (!ok) break;
-      // combine the four quarters of each row (red double-buffered by tile parity)
-      red[((t & 1) * 4 + h) * kP1Rows + row] = make_float2(m, l);
+      // combine the four quarters of each row; red double-buffered by pair parity
+      float2* rq = red + (q & 1) * 8 * kP1Rows;
+      for (int tt = 0; tt < nt; ++tt) rq[(tt * 4 + h) * kP1Rows + row] = make_float2(m[tt], l[tt]);
       __syncwarp();
       if (lane == 0) mbar_arrive(&ctl->lse_bar);
-      if (!mbar_wait_flag(&ctl->lse_bar, t & 1, abort_flag, p.err, 64)) break;
+      if (!mbar_wait_flag(&ctl->lse_bar, q & 1, abort_flag, p.err, 64)) break;
       if (h == 0) {
-        float2 o[4];
+        for (int tt = 0; tt < nt; ++tt) {
+          float2 o[4];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) o[u] = red[((t & 1) * 4 + u) * kP1Rows + row];
-        const float M = fmaxf(fmaxf(o[0].x, o[1].x), fmaxf(o[2].x, o[3].x));
-        const float Ls = (o[0].y * ex2(o[0].x - M) + o[1].y * ex2(o[1].x - M)) +
-                         (o[2].y * ex2(o[2].x - M) + o[3].y * ex2(o[3].x - M));
-        const float lz2 = M + lg2(Ls);
-        if (live) {
-          p.logZ[n] = lz2 * 0.6931471805599453f;
-          p.lz2[n] = lz2;
+          for (int u = 0; u < 4; ++u) o[u] = rq[(tt * 4 + u) * kP1Rows + row];
+          const float M = fmaxf(fmaxf(o[0].x, o[1].x), fmaxf(o[2].x, o[3].x));
+          const float Ls = (o[0].y * ex2(o[0].x - M) + o[1].y * ex2(o[1].x - M)) +
+                           (o[2].y * ex2(o[2].x - M) + o[3].y * ex2(o[3].x - M));
+          const float lz2 = M + lg2(Ls);
+          const int64_t n = tile_of(q, tt) * kP1Rows + row;
+          if (n < p.N) {
+            p.logZ[n] = lz2 * 0.6931471805599453f;
+            p.lz2[n] = lz2;
+          }
         }
       }
     }
@@ -449,30 +514,47 @@ __global__ void __launch_bounds__(kP1Threads, 1) full_ll_kernel(const P1Params p
   }
 }
 
-// Feature f of the pass-2 feature vector -> the two x~ slots it multiplies:
-// triangle features (i <= j) first, then x~_i (times the constant-1 slot D),
-// then 1 (slot D times slot D); past nf a zero feature.
-__device__ __forceinline__ uint32_t feature_slots(int f, int D, int nf) {
-  const int tri = D * (D + 1) / 2;
-  int i, j;
-  if (f < tri) {
-    i = 0;
-    int rem = f;
-    while (rem >= D - i) {
-      rem -= D - i;
-      ++i;
-    }
-    j = i + rem;
-  } else if (f < tri + D) {
-    i = f - tri;
-    j = D;
-  } else if (f < nf) {
-    i = D;
-    j = D;
-  } else {
-    return kPadFeature;
+// Pass-2 features come in quads of 4 consecutive columns:
+//   pair quad (i, q):  x~_i x~_j for j = 4q..4q+3, q >= floor(i/4)  (covers i <= j;
+//                      the few j < i columns are extra and ignored)
+//   x quad q:          x~_j for j = 4q..4q+3            (mu_acc)
+//   one quad:          [1, 0, 0, 0]                      (Nk)
+//   zero quads pad the last feature block.
+// With Dq = ceil(D/4), pair quads of row i start at pairbase(i) =
+// i*Dq - sum_{i'<i} floor(i'/4).  Columns for j >= D are never read back.
+__host__ __device__ __forceinline__ int quad_dq(int D) { return (D + 3) / 4; }
+__host__ __device__ __forceinline__ int pairbase(int i, int Dq) {
+  const int a = i >> 2, b = i & 3;
+  return i * Dq - (2 * a * (a - 1) + a * b);
+}
+__host__ __device__ __forceinline__ int pair_quads(int D) { return pairbase(D, quad_dq(D)); }
+__host__ __device__ __forceinline__ int num_features(int D) {
+  return 4 * (pair_quads(D) + quad_dq(D) + 1);
+}
+// Feature column of x_i x_j (i <= j), of x_i, and of the constant.
+__host__ __device__ __forceinline__ int pair_feature(int i, int j, int D) {
+  const int Dq = quad_dq(D);
+  return 4 * (pairbase(i, Dq) + (j >> 2) - (i >> 2)) + (j & 3);
+}
+__host__ __device__ __forceinline__ int x_feature(int i, int D) {
+  return 4 * (pair_quads(D) + (i >> 2)) + (i & 3);
+}
+__host__ __device__ __forceinline__ int one_feature(int D) {
+  return 4 * (pair_quads(D) + quad_dq(D));
+}
+// Kind of quad Q: 0 pair (i, q), 1 x quad (q), 2 one, 3 zero; packed as
+// kind | i << 8 | q << 16.
+__device__ __forceinline__ uint32_t quad_desc(int Q, int D) {
+  const int Dq = quad_dq(D), P = pair_quads(D);
+  if (Q < P) {
+    int i = 0;
+    while (i + 1 < D && pairbase(i + 1, Dq) <= Q) ++i;
+    const int q = (i >> 2) + (Q - pairbase(i, Dq));
+    return 0u | ((uint32_t)i << 8) | ((uint32_t)q << 16);
   }
-  return (uint32_t)i | ((uint32_t)j << 8);
+  if (Q < P + Dq) return 1u | ((uint32_t)(Q - P) << 16);
+  if (Q == P + Dq) return 2u;
+  return 3u;
 }
 
 // ---------------------------------------------------------------------------
@@ -533,13 +615,12 @@ __global__ void __launch_bounds__(kP2Comps) full_resp_kernel(const float* __rest
 __global__ void __launch_bounds__(kP2Threads, 1) full_stats_kernel(const P2Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
-  const int xs_stride = p.D + 1;
+  const int xs_stride = xs2_stride(p.D);
   const uint32_t xs_bytes = (uint32_t)(kP2Rows * xs_stride * 4);
   uint8_t* rst = smem;                                        // [2][hi | lo] R^T, 32 KB each
   uint8_t* zst = smem + 4 * kRBlock;                          // [2][hi | lo] z, 64 KB each
   float* xst = reinterpret_cast<float*>(zst + 2 * kZStage);   // [2][64][D+1]
-  uint32_t* ftab = reinterpret_cast<uint32_t*>(xst + 2 * kP2Rows * xs_stride);  // [256]
-  P2Ctl* ctl = reinterpret_cast<P2Ctl*>(ftab + kP2Feat);
+  P2Ctl* ctl = reinterpret_cast<P2Ctl*>(xst + 2 * kP2Rows * xs_stride);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int fb = (int)blockIdx.x % p.nfb;
@@ -562,8 +643,6 @@ __global__ void __launch_bounds__(kP2Threads, 1) full_stats_kernel(const P2Param
     ctl->abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  for (int f = threadIdx.x; f < kP2Feat; f += kP2Threads)
-    ftab[f] = feature_slots(fb * kP2Feat + f, p.D, p.nf);
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;" ::"r"(
                      smem_u32(&ctl->tmem_base))
@@ -616,8 +695,12 @@ __global__ void __launch_bounds__(kP2Threads, 1) full_stats_kernel(const P2Param
     }
     __syncwarp();
   } else {
-    // ---- z chunks: warp zw builds rows 4zw..4zw+3; lane l features 4l.. and 128+4l..
+    // ---- z chunks: warp zw builds rows 4zw..4zw+3; lane l owns the feature
+    // quads lane and 32 + lane of this CTA's 64 (features 4l.. and 128+4l..)
     const int zw = warp;
+    uint32_t qd[2];
+    qd[0] = quad_desc(fb * (kP2Feat / 4) + lane, p.D);
+    qd[1] = quad_desc(fb * (kP2Feat / 4) + 32 + lane, p.D);
     int c = 0;
     for (; c < nchunks; ++c) {
       const int b = c & 1;
@@ -626,30 +709,38 @@ __global__ void __launch_bounds__(kP2Threads, 1) full_stats_kernel(const P2Param
         break;
       const float* xsb = xst + b * kP2Rows * xs_stride;
       uint8_t* zs = zst + b * kZStage;
-      bool over = false;
 #pragma unroll 1
       for (int rr = 0; rr < 4; ++rr) {
         const int r = zw * 4 + rr;
         const float* xr = xsb + r * xs_stride;
 #pragma unroll
         for (int grp = 0; grp < 2; ++grp) {
-          const int f0 = grp * 128 + 4 * lane;
+          const uint32_t d = qd[grp];
+          const uint32_t kind = d & 0xffu;
           float z[4];
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const uint32_t ij = ftab[f0 + u];
-            z[u] = ij == kPadFeature ? 0.f : xr[ij & 0xffu] * xr[ij >> 8];
-            over |= !(fabsf(z[u]) < 65504.f);
+          if (kind <= 1u) {
+            const int j0 = 4 * (int)(d >> 16);
+            const float2 a01 = *reinterpret_cast<const float2*>(xr + j0);
+            const float2 a23 = *reinterpret_cast<const float2*>(xr + j0 + 2);
+            const float xi = kind == 0u ? xr[(d >> 8) & 0xffu] : 1.0f;
+            z[0] = xi * a01.x;
+            z[1] = xi * a01.y;
+            z[2] = xi * a23.x;
+            z[3] = xi * a23.y;
+          } else {
+            z[0] = kind == 2u ? 1.0f : 0.f;
+            z[1] = 0.f;
+            z[2] = 0.f;
+            z[3] = 0.f;
           }
           uint32_t h0, l0, h1, l1;
           split2(z[0], z[1], h0, l0);
           split2(z[2], z[3], h1, l1);
-          const uint32_t off = xoff(r, f0, kZChunk);
+          const uint32_t off = xoff(r, grp * 128 + 4 * lane, kZChunk);
           *reinterpret_cast<uint2*>(zs + off) = make_uint2(h0, h1);
           *reinterpret_cast<uint2*>(zs + 4 * kZChunk + off) = make_uint2(l0, l1);
         }
       }
-      if (over) atomicOr(p.err, 0x20000);
       fence_async_smem();
       __syncwarp();
       if (lane == 0) {
@@ -705,7 +796,6 @@ __global__ void full_reduce_kernel(const float* __restrict__ part, int slabs, in
   const double s1 = ldexp(1.0, a2), s2 = ldexp(1.0, 2 * a2);
   const bool bad = *err != 0;
   const float qnan = __int_as_float(0x7fc00000);
-  const int tri = D * (D + 1) / 2;
   const int per_k = D * D + D + 1;
   auto feat_sum = [&](int k, int f) -> double {
     double s = 0.0;
@@ -715,20 +805,20 @@ __global__ void full_reduce_kernel(const float* __restrict__ part, int slabs, in
   for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < (int64_t)K * per_k;
        e += (int64_t)gridDim.x * blockDim.x) {
     const int k = (int)(e / per_k), w = (int)(e % per_k);
-    const double n = feat_sum(k, tri + D);
+    const double n = feat_sum(k, one_feature(D));
     if (w == D * D + D) {
       const float v = bad ? qnan : (float)n;
       Nk[k] = accumulate ? Nk[k] + v : v;
     } else if (w >= D * D) {
       const int i = w - D * D;
-      const float v = bad ? qnan : (float)(feat_sum(k, tri + i) * s1 + (double)cvec[i] * n);
+      const float v = bad ? qnan : (float)(feat_sum(k, x_feature(i, D)) * s1 + (double)cvec[i] * n);
       float* dst = mu_acc + (size_t)k * D + i;
       *dst = accumulate ? *dst + v : v;
     } else {
       const int i = w / D, j = w % D;
       const int a = min(i, j), b = max(i, j);
-      const double sxx = feat_sum(k, a * D - a * (a - 1) / 2 + (b - a)) * s2;
-      const double mi = feat_sum(k, tri + i) * s1, mj = feat_sum(k, tri + j) * s1;
+      const double sxx = feat_sum(k, pair_feature(a, b, D)) * s2;
+      const double mi = feat_sum(k, x_feature(i, D)) * s1, mj = feat_sum(k, x_feature(j, D)) * s1;
       const double ci = cvec[i], cj = cvec[j];
       const float v = bad ? qnan : (float)(sxx + ci * mj + mi * cj + n * ci * cj);
       float* dst = sig + (size_t)k * D * D + w;
@@ -750,7 +840,7 @@ FullPlan plan_full(int64_t N, int K, int D) {
   pl.Kpad = pl.num_groups * pl.G;
   pl.num_tiles = (int)((N + kP1Rows - 1) / kP1Rows);
   pl.Npad = (int64_t)pl.num_tiles * kP1Rows;
-  pl.nf = D * (D + 1) / 2 + D + 1;
+  pl.nf = num_features(D);
   pl.nfb = (pl.nf + kP2Feat - 1) / kP2Feat;
   pl.ncb = (K + kP2Comps - 1) / kP2Comps;
   const int64_t nch_total = (N + kP2Rows - 1) / kP2Rows;
@@ -761,11 +851,11 @@ FullPlan plan_full(int64_t N, int K, int D) {
 
 size_t p1_smem_bytes() {
   return 1024 + (size_t)4 * kXTile + (size_t)kP1LStages * 2 * kLGroup +
-         (size_t)8 * kP1Rows * sizeof(float2) + sizeof(P1Ctl) + 64;
+         (size_t)16 * kP1Rows * sizeof(float2) + (size_t)kP1BSlots * kBSlot + sizeof(P1Ctl) + 64;
 }
 size_t p2_smem_bytes(int D) {
-  return 1024 + (size_t)4 * kRBlock + (size_t)2 * kZStage + (size_t)2 * kP2Rows * (D + 1) * 4 +
-         (size_t)kP2Feat * 4 + sizeof(P2Ctl) + 16;
+  return 1024 + (size_t)4 * kRBlock + (size_t)2 * kZStage +
+         (size_t)2 * kP2Rows * xs2_stride(D) * 4 + sizeof(P2Ctl) + 16;
 }
 
 struct FullWs {
@@ -790,9 +880,9 @@ FullWs carve_full(void* base, const FullPlan& pl, int D) {
   ws.cvec = w.take<float>(kFullMaxD);
   ws.lgroups = w.take<uint8_t>((size_t)pl.num_groups * 2 * kLGroup);
   ws.bvec = w.take<float>((size_t)pl.Kpad * pl.Dp);
-  ws.kconst = w.take<float2>(pl.Kpad);
+  ws.kconst = w.take<float2>((size_t)pl.num_groups * 16);
   ws.xsplit = w.take<uint8_t>((size_t)pl.num_tiles * 2 * kXTile);
-  ws.xs2 = w.take<float>((size_t)pl.Npad * (D + 1));
+  ws.xs2 = w.take<float>((size_t)pl.Npad * xs2_stride(D));
   ws.ll2 = w.take<float>((size_t)pl.Kpad * pl.Npad);
   ws.lz2 = w.take<float>((size_t)pl.Npad);
   ws.rt = w.take<uint8_t>((size_t)(pl.Npad / kP2Rows) * pl.ncb * 2 * kRBlock);
