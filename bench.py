@@ -59,18 +59,19 @@ SEED = 1234
 WORKLOADS = {
     "c2": dict(kind="iso", rows=1_000_000, K=1024, D=128, scaling="weak",
                title="C2 isotropic E-step N=1M K=1024 D=128 per GPU",
-               profile="tc_iso_kernel_c2.txt", kernel="tc_fused_kernel<iso> "
+               profile="tc_fused_iso_c2.txt", kernel="tc_fused_kernel<iso> "
                "(fused distance/LSE/statistics, tcgen05)"),
     "c3": dict(kind="diag", rows=1_000_000, K=1024, D=96, scaling="weak",
                title="C3 diagonal-covariance E-step N=1M K=1024 D=96 per GPU",
-               profile="tc_diag_kernel_c3.txt", kernel="tc_fused_kernel<diag> "
+               profile="tc_fused_diag_c3.txt", kernel="tc_fused_kernel<diag> "
                "(fused distance/LSE/statistics, tcgen05)"),
     "c4": dict(kind="full", rows=250_000, K=256, D=64, scaling="weak",
                title="C4 full-covariance E-step N=250K K=256 D=64 per GPU",
-               profile="full_kernel_c4.txt", kernel="full-covariance statistics pass"),
+               profile="full_passes_c4.txt", kernel="full_ll_kernel + full_resp_kernel + "
+               "full_stats_kernel (the two tensor-core passes and the responsibilities between)"),
     "c5": dict(kind="iso", rows=ROWS_C5, K=1024, D=128, scaling="strong",
                title="C5 streaming isotropic E-step N=100M K=1024 D=128 total",
-               profile="tc_iso_kernel_c2.txt", kernel="tc_fused_kernel<iso> "
+               profile="tc_fused_iso_c2.txt", kernel="tc_fused_kernel<iso> "
                "(fused distance/LSE/statistics, tcgen05), one 10M-row chunk"),
 }
 
