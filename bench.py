@@ -106,14 +106,17 @@ def profile_traffic(profile: str, name: str = "dram_bytes_per_launch"):
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    """nvidia-smi clocks / throttle reasons sampled during the timed region.
+
+    One sampler per job (rank 0) queries every GPU the job runs on: one
+    nvidia-smi per rank polling every few ms slowed 8-rank steps ~2x."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
+    def __init__(self, gpu_indices):
+        self.gpus = ",".join(str(g) for g in gpu_indices)
         self.proc = None
         self.tmp = None
         self.skip = 0
@@ -122,7 +125,7 @@ class ClockSampler:
         try:
             self.tmp = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
             self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                ["nvidia-smi", "-i", self.gpus, f"--query-gpu={self.FIELDS}",
                  "--format=csv,noheader,nounits", "-lms", "20"],
                 stdout=self.tmp, stderr=subprocess.DEVNULL)
             # the timed region starts once the sampler is producing lines
@@ -329,12 +332,20 @@ def main():
 
     # profiling events around the dominant kernel of each E-step call
     ev_pairs = []
-    sampler = ClockSampler(local)
+    # rank 0 samples the clocks of all of this job's GPUs (nvidia-smi indices)
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+    vis_ids = [v for v in vis.split(",") if v.strip() != ""]
+    gpu_ids = [vis_ids[i] if i < len(vis_ids) else str(i) for i in range(world)]
+    sampler = ClockSampler(gpu_ids) if rank == 0 else None
     launches0 = L.launch_count()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(dev)
-    sampler.start()
+    if sampler is not None:
+        sampler.start()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
     # X smaller than L2 (C4: 64 MB): each step is timed on its own and a
     # 256 MB buffer is rewritten between steps, outside the timed spans
     flush = None
@@ -360,7 +371,7 @@ def main():
     torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
-    clocks = sampler.stop()
+    clocks = sampler.stop() if sampler is not None else None
     launches = L.launch_count() - launches0
     ms_total = sum(t0.elapsed_time(t1) for t0, t1 in step_ev)
     kern_ms = [a.elapsed_time(b) for a, b in ev_pairs]
