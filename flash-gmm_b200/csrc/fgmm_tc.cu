@@ -844,6 +844,44 @@ TcPlan plan_tc(int variant, int64_t N, int K, int D, bool query_device) {
   return pl;
 }
 
+// Large calls run in kChunks row chunks so the split pass of chunk c+1
+// (low-priority stream) overlaps the fused kernel of chunk c (high-priority
+// stream, which the fused CTAs need to get their 120 SMs first); the split
+// pass then uses the SMs the 8-CTA clusters leave free.  Smaller calls (and
+// the whole path's workspace-free entry, which stays far below the
+// threshold) run on the caller's stream alone.
+constexpr int kChunks = 4;
+constexpr int kChunkMinTiles = 2048;
+
+int plan_chunks(const TcPlan& pl) { return pl.num_tiles >= kChunkMinTiles ? kChunks : 1; }
+
+struct SideStreams {
+  bool ready = false;
+  cudaStream_t hi = nullptr, lo = nullptr;
+  cudaEvent_t ev[kChunks + 3] = {};
+};
+// Per host thread and device: calls from different threads never share
+// streams or events.
+thread_local SideStreams t_side[16];
+
+SideStreams* side_streams() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 16) return nullptr;
+  SideStreams& ss = t_side[dev];
+  if (!ss.ready) {
+    int least = 0, greatest = 0;
+    if (cudaDeviceGetStreamPriorityRange(&least, &greatest) != cudaSuccess) return nullptr;
+    if (cudaStreamCreateWithPriority(&ss.hi, cudaStreamNonBlocking, greatest) != cudaSuccess)
+      return nullptr;
+    if (cudaStreamCreateWithPriority(&ss.lo, cudaStreamNonBlocking, least) != cudaSuccess)
+      return nullptr;
+    for (auto& e : ss.ev)
+      if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) return nullptr;
+    ss.ready = true;
+  }
+  return &ss;
+}
+
 template <class G>
 cudaError_t launch_fused(const TcPlan& pl, const TcParams& p, cudaStream_t stream) {
   cudaError_t e = cudaFuncSetAttribute(tc_fused_kernel<G>,
@@ -861,10 +899,7 @@ cudaError_t launch_fused(const TcPlan& pl, const TcParams& p, cudaStream_t strea
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  profile_mark(false, stream);
-  e = cudaLaunchKernelEx(&cfg, tc_fused_kernel<G>, p);
-  profile_mark(true, stream);
-  return e;
+  return cudaLaunchKernelEx(&cfg, tc_fused_kernel<G>, p);
 }
 
 }  // namespace
@@ -942,8 +977,9 @@ size_t tc_workspace_bytes(int variant, int64_t N, int K, int D) {
   w.take<__half>((size_t)pl.Kpad * pl.nfeat);
   w.take<__half>((size_t)pl.Kpad * pl.nfeat);
   w.take<float4>(pl.Kpad);
-  // partial rows for the largest cluster count a 148-SM device can run
-  w.take<float>((size_t)(kSms / pl.C) * pl.Kpad * pl.plen);
+  // partial rows for the largest cluster count a 148-SM device can run,
+  // per row chunk when the call is split into chunks
+  w.take<float>((size_t)plan_chunks(pl) * (kSms / pl.C) * pl.Kpad * pl.plen);
   w.take<uint8_t>((size_t)pl.num_tiles * pl.stage_bytes);             // split features
   if (!pl.diag) w.take<float>((size_t)pl.num_tiles * pl.rows);         // |x|^2
   return w.used + 256;
@@ -958,68 +994,124 @@ cudaError_t tc_estep(int variant, const EstepArgs& a) {
   __half* Whi = w.take<__half>((size_t)pl.Kpad * pl.nfeat);
   __half* Wlo = w.take<__half>((size_t)pl.Kpad * pl.nfeat);
   float4* consts = w.take<float4>(pl.Kpad);
-  float* part = w.take<float>((size_t)(kSms / pl.C) * pl.Kpad * pl.plen);
+  int nchunks = plan_chunks(pl);
+  float* part = w.take<float>((size_t)nchunks * (kSms / pl.C) * pl.Kpad * pl.plen);
   uint8_t* xsplit = w.take<uint8_t>((size_t)pl.num_tiles * pl.stage_bytes);
   float* xsq = pl.diag ? nullptr : w.take<float>((size_t)pl.num_tiles * pl.rows);
 
+  SideStreams* ss = nchunks > 1 ? side_streams() : nullptr;
+  if (ss == nullptr) nchunks = 1;
+  // hi: prep, fused kernels, reduce; lo: split passes (same stream when not chunked)
+  cudaStream_t hi = a.stream, lo = a.stream;
+  cudaError_t e;
+  if (nchunks > 1) {
+    hi = ss->hi;
+    lo = ss->lo;
+    if ((e = cudaEventRecord(ss->ev[0], a.stream)) != cudaSuccess) return e;
+    if ((e = cudaStreamWaitEvent(hi, ss->ev[0], 0)) != cudaSuccess) return e;
+    if ((e = cudaStreamWaitEvent(lo, ss->ev[0], 0)) != cudaSuccess) return e;
+  }
+
   // err[0]: device error word, err[1]: max|mu| (iso) or max|mu - c| (diag),
   // float bits, for the X scale
-  cudaError_t e = cudaMemsetAsync(err, 0, 2 * sizeof(int), a.stream);
+  e = cudaMemsetAsync(err, 0, 2 * sizeof(int), hi);
   if (e != cudaSuccess) return e;
-  const int64_t rows_pad = (int64_t)pl.num_tiles * pl.rows;
-  const int vec_ok = a.sxd == 1 && (reinterpret_cast<uintptr_t>(a.X) & 15) == 0 && a.sxn % 4 == 0;
-  const int sblocks = (int)std::min<int64_t>((rows_pad + 8 * kSplitRows - 1) / (8 * kSplitRows), 16 * kSms);
+  int launches = 0;
   if (pl.diag) {
-    centre_kernel<<<pl.Dp, 256, 0, a.stream>>>(a.mu, a.smk, a.smd, a.K, a.D, cvec,
-                                                       err + 1);
-    tc_prep_diag_kernel<<<pl.Kpad, 128, 0, a.stream>>>(a.mu, a.smk, a.smd, a.cov, a.lpi, cvec,
-                                                       err + 1, a.K, a.D, pl.Dp, Whi, Wlo,
-                                                       consts);
-    tc_split_kernel<DiagCfg::kRows, true><<<sblocks, 256, 0, a.stream>>>(
-        a.X, a.sxn, a.sxd, vec_ok, a.N, a.D, pl.Dp, pl.nch, rows_pad, err + 1, cvec, xsplit,
-        nullptr, err);
+    centre_kernel<<<pl.Dp, 256, 0, hi>>>(a.mu, a.smk, a.smd, a.K, a.D, cvec, err + 1);
+    tc_prep_diag_kernel<<<pl.Kpad, 128, 0, hi>>>(a.mu, a.smk, a.smd, a.cov, a.lpi, cvec, err + 1,
+                                                 a.K, a.D, pl.Dp, Whi, Wlo, consts);
+    launches += 2;
   } else {
-    tc_prep_kernel<<<pl.Kpad, 128, 0, a.stream>>>(a.mu, a.smk, a.smd, a.cov, a.lpi, a.K, a.D,
-                                                   pl.Dp, Whi, Wlo, consts, err + 1);
-    tc_split_kernel<IsoCfg::kRows, false><<<sblocks, 256, 0, a.stream>>>(
-        a.X, a.sxn, a.sxd, vec_ok, a.N, a.D, pl.Dp, pl.nch, rows_pad, err + 1, nullptr, xsplit,
-        xsq, err);
+    tc_prep_kernel<<<pl.Kpad, 128, 0, hi>>>(a.mu, a.smk, a.smd, a.cov, a.lpi, a.K, a.D, pl.Dp,
+                                            Whi, Wlo, consts, err + 1);
+    launches += 1;
   }
+  if (nchunks > 1) {
+    if ((e = cudaEventRecord(ss->ev[1], hi)) != cudaSuccess) return e;
+    if ((e = cudaStreamWaitEvent(lo, ss->ev[1], 0)) != cudaSuccess) return e;
+  }
+  const int vec_ok = a.sxd == 1 && (reinterpret_cast<uintptr_t>(a.X) & 15) == 0 && a.sxn % 4 == 0;
+  const int tiles_per_chunk = (pl.num_tiles + nchunks - 1) / nchunks;
+
+  // split passes (stream lo), one per chunk of tiles [t0, t1)
+  for (int c = 0; c < nchunks; ++c) {
+    const int t0 = c * tiles_per_chunk, t1 = std::min(pl.num_tiles, t0 + tiles_per_chunk);
+    if (t0 >= t1) break;
+    const int64_t row0 = (int64_t)t0 * pl.rows;
+    const int64_t rows = std::min<int64_t>(a.N, (int64_t)t1 * pl.rows) - row0;
+    const int64_t rows_pad = (int64_t)(t1 - t0) * pl.rows;
+    const int sblocks =
+        (int)std::min<int64_t>((rows_pad + 8 * kSplitRows - 1) / (8 * kSplitRows), 16 * kSms);
+    const float* Xc = a.X + row0 * a.sxn;
+    uint8_t* xs_c = xsplit + (size_t)t0 * pl.stage_bytes;
+    if (pl.diag)
+      tc_split_kernel<DiagCfg::kRows, true><<<sblocks, 256, 0, lo>>>(
+          Xc, a.sxn, a.sxd, vec_ok, rows, a.D, pl.Dp, pl.nch, rows_pad, err + 1, cvec, xs_c,
+          nullptr, err);
+    else
+      tc_split_kernel<IsoCfg::kRows, false><<<sblocks, 256, 0, lo>>>(
+          Xc, a.sxn, a.sxd, vec_ok, rows, a.D, pl.Dp, pl.nch, rows_pad, err + 1, nullptr, xs_c,
+          xsq + (size_t)t0 * pl.rows, err);
+    ++launches;
+    if (nchunks > 1 && (e = cudaEventRecord(ss->ev[2 + c], lo)) != cudaSuccess) return e;
+  }
+
+  // fused kernels (stream hi), each after its chunk's split; partials of
+  // chunk c follow those of chunks < c, so one reduction sums them in order
   TcParams p;
-  p.xsplit = xsplit;
-  p.xsq = xsq;
-  p.N = a.N;
   p.K = a.K;
   p.D = a.D;
   p.Dp = pl.Dp;
   p.nfeat = pl.nfeat;
   p.nch = pl.nch;
   p.C = pl.C;
-  p.num_tiles = pl.num_tiles;
   p.Whi = Whi;
   p.Wlo = Wlo;
   p.consts = consts;
   p.xscale = err + 1;
-  p.logZ = a.logZ;
-  p.part = part;
   p.plen = pl.plen;
   p.err = err;
-  e = pl.diag ? launch_fused<DiagCfg>(pl, p, a.stream) : launch_fused<IsoCfg>(pl, p, a.stream);
-  if (e != cudaSuccess) return e;
+  int part_clusters = 0;
+  for (int c = 0; c < nchunks; ++c) {
+    const int t0 = c * tiles_per_chunk, t1 = std::min(pl.num_tiles, t0 + tiles_per_chunk);
+    if (t0 >= t1) break;
+    if (nchunks > 1 && (e = cudaStreamWaitEvent(hi, ss->ev[2 + c], 0)) != cudaSuccess) return e;
+    if (c == 0) profile_mark(false, hi);  // the fused kernels of all chunks are bracketed
+    const int64_t row0 = (int64_t)t0 * pl.rows;
+    TcPlan pc = pl;
+    pc.num_tiles = t1 - t0;
+    pc.clusters = std::max(1, std::min(pl.clusters, pc.num_tiles));
+    p.xsplit = xsplit + (size_t)t0 * pl.stage_bytes;
+    p.xsq = pl.diag ? nullptr : xsq + (size_t)t0 * pl.rows;
+    p.N = std::min<int64_t>(a.N, (int64_t)t1 * pl.rows) - row0;
+    p.num_tiles = pc.num_tiles;
+    p.logZ = a.logZ + row0;
+    p.part = part + (size_t)part_clusters * pl.Kpad * pl.plen;
+    e = pl.diag ? launch_fused<DiagCfg>(pc, p, hi) : launch_fused<IsoCfg>(pc, p, hi);
+    if (e != cudaSuccess) return e;
+    part_clusters += pc.clusters;
+    ++launches;
+  }
+  profile_mark(true, hi);
   const int accumulate = (a.flags & 1u) ? 1 : 0;
   if (pl.diag) {
     const int64_t total = (int64_t)a.K * (a.D + 1);
     const int rblocks = (int)std::min<int64_t>((total + 255) / 256, 1024);
-    tc_reduce_diag_kernel<<<rblocks, 256, 0, a.stream>>>(part, pl.clusters, pl.Kpad, a.K, a.D,
-                                                         cvec, a.mu, a.smk, a.smd, err, a.Nk,
-                                                         a.mu_acc, a.sig, accumulate);
-    count_launches(5);
+    tc_reduce_diag_kernel<<<rblocks, 256, 0, hi>>>(part, part_clusters, pl.Kpad, a.K, a.D, cvec,
+                                                   a.mu, a.smk, a.smd, err, a.Nk, a.mu_acc,
+                                                   a.sig, accumulate);
   } else {
     const int64_t total = (int64_t)a.K * (a.D + 2);
     const int rblocks = (int)std::min<int64_t>((total + 255) / 256, 1024);
-    tc_reduce_kernel<<<rblocks, 256, 0, a.stream>>>(part, pl.clusters, pl.Kpad, a.K, a.D, err,
-                                                     a.Nk, a.mu_acc, a.sig, accumulate);
-    count_launches(4);
+    tc_reduce_kernel<<<rblocks, 256, 0, hi>>>(part, part_clusters, pl.Kpad, a.K, a.D, err, a.Nk,
+                                              a.mu_acc, a.sig, accumulate);
+  }
+  ++launches;
+  count_launches(launches);
+  if (nchunks > 1) {
+    if ((e = cudaEventRecord(ss->ev[2 + kChunks], hi)) != cudaSuccess) return e;
+    if ((e = cudaStreamWaitEvent(a.stream, ss->ev[2 + kChunks], 0)) != cudaSuccess) return e;
   }
   return cudaGetLastError();
 }

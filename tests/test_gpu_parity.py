@@ -122,3 +122,24 @@ def test_headline_config_full_size():
                                atol=1e-4 * np.abs(mu_acc).max() * 4)
     ref = O.estep_iso(X.cpu().numpy(), mu.cpu().numpy(), lss.cpu().numpy(), lpi.cpu().numpy())
     assert_parity((logZ, Nk, mu_acc, sig), ref, what="C2 full size")
+
+
+@pytest.mark.parametrize("cfg,n", [("c2", 300_000), ("c3", 140_000)])
+def test_chunked_calls_accumulate_and_repeat(cfg, n):
+    """Calls of >= 2048 row tiles run in row chunks on two internal streams
+    (split of chunk c+1 overlapping the fused kernel of chunk c): bitwise
+    run-to-run, accumulation over two such calls equals one call, and the
+    caller's stream sees the results (no explicit synchronisation between)."""
+    X, mu, cov, lpi = gmm_data.make_config(cfg, device=DEV, N=2 * n)
+    v = VARIANT[gmm_data.CONFIGS[cfg]["kind"]]
+    one = _np(L.estep(v, X, mu, cov, lpi))
+    again = _np(L.estep(v, X, mu, cov, lpi))
+    for a, b in zip(one, again):
+        np.testing.assert_array_equal(a, b)
+    out = L.estep(v, X[:n], mu, cov, lpi)
+    out = (torch.empty(n, device=DEV),) + out[1:]
+    L.estep(v, X[n:], mu, cov, lpi, out=out, accumulate=True)
+    acc = _np(out)
+    for u, w in zip(acc[1:], one[1:]):
+        assert np.max(np.abs(u - w)) <= 1e-5 * np.max(np.abs(w))
+    assert abs(one[1].astype(np.float64).sum() - 2 * n) <= 1e-5 * 2 * n
