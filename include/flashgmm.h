@@ -32,7 +32,11 @@
  *    kernel reduces in a fixed order: results are bitwise reproducible
  *    run-to-run (the reference's tl.atomic_add accumulation is not).
  *  - stream: a cudaStream_t passed as void*; NULL = legacy default stream.
- *    The call is asynchronous on that stream and never synchronises.
+ *    The call is asynchronous on that stream and never synchronises.  Large
+ *    isotropic / diagonal calls (>= 2048 row tiles) fork two library-owned
+ *    streams (one pair per host thread and device, created on first use) and
+ *    join back to `stream` with events: work the caller enqueues on `stream`
+ *    after the call sees all of its results.
  *  - Return value: FGMM_OK (0) or one of the FGMM_ERR_* codes; no C++
  *    exception crosses the ABI.  fgmm_last_error() gives a message for the
  *    last failing call on the calling thread.
