@@ -4,6 +4,7 @@
 #include <stdio.h>
 
 #include <atomic>
+#include <map>
 #include <mutex>
 #include <string>
 
@@ -169,16 +170,33 @@ void profile_mark(bool stop, cudaStream_t stream) {
   if (ev) cudaEventRecord(ev, stream);
 }
 
-static int g_num_sms = 0;
+static std::atomic<int> g_num_sms{0};
 int num_sms() {
-  if (g_num_sms == 0) {
-    int dev = 0, n = 0;
+  int n = g_num_sms.load(std::memory_order_relaxed);
+  if (n == 0) {
+    int dev = 0;
     cudaGetDevice(&dev);
     if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
       n = 148;
-    g_num_sms = n;
+    g_num_sms.store(n, std::memory_order_relaxed);
   }
-  return g_num_sms;
+  return n;
+}
+
+// The dynamic shared-memory limit of a kernel only ever grows (per kernel and
+// device), so a launch that needs less never races with one that raised it.
+cudaError_t ensure_dynamic_smem(const void* kernel, size_t bytes) {
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, size_t> limit;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lk(mu);
+  size_t& cur = limit[{kernel, dev}];
+  if (bytes <= cur) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  if (e == cudaSuccess) cur = bytes;
+  return e;
 }
 
 cudaError_t generate_iso_rows(float* X, const int64_t* row_ids, int64_t row0, int64_t nrows,

@@ -528,34 +528,30 @@ cudaError_t general_estep(int variant, const EstepArgs& a) {
     dim3 grid((K + BC - 1) / BC, p.slabs);
     profile_mark(false, st);
     if (diag) {
-      cudaFuncSetAttribute(stats_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)dyn);
+      ensure_dynamic_smem(reinterpret_cast<const void*>(stats_kernel<true>), dyn);
       stats_kernel<true><<<grid, kThreads, dyn, st>>>(a.X, a.sxn, a.sxd, a.mu, a.smk, a.smd,
                                                        inv, cst, N, K, D, a.logZ,
                                                        p.rows_per_slab, p.part_len, part);
     } else {
-      cudaFuncSetAttribute(stats_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)dyn);
+      ensure_dynamic_smem(reinterpret_cast<const void*>(stats_kernel<false>), dyn);
       stats_kernel<false><<<grid, kThreads, dyn, st>>>(a.X, a.sxn, a.sxd, a.mu, a.smk, a.smd,
                                                         inv, cst, N, K, D, a.logZ,
                                                         p.rows_per_slab, p.part_len, part);
     }
   } else {
     const size_t dyn = ((size_t)D * D + 2 * (size_t)BR * (D + 1)) * sizeof(float);
-    cudaFuncSetAttribute(full_lse_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn);
+    ensure_dynamic_smem(reinterpret_cast<const void*>(full_lse_kernel), dyn);
     full_lse_kernel<<<row_blocks, kThreads, dyn, st>>>(a.X, a.sxn, a.sxd, a.mu, a.smk, a.smd,
                                                         a.cov, cst, N, K, D, a.logZ);
     dim3 grid(K, p.slabs);
     profile_mark(false, st);
     if (D <= 64) {
-      cudaFuncSetAttribute(full_stats_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)dyn);
+      ensure_dynamic_smem(reinterpret_cast<const void*>(full_stats_kernel<4>), dyn);
       full_stats_kernel<4><<<grid, kThreads, dyn, st>>>(a.X, a.sxn, a.sxd, a.mu, a.smk, a.smd,
                                                          a.cov, cst, N, K, D, a.logZ,
                                                          p.rows_per_slab, p.part_len, part);
     } else {
-      cudaFuncSetAttribute(full_stats_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)dyn);
+      ensure_dynamic_smem(reinterpret_cast<const void*>(full_stats_kernel<8>), dyn);
       full_stats_kernel<8><<<grid, kThreads, dyn, st>>>(a.X, a.sxn, a.sxd, a.mu, a.smk, a.smd,
                                                          a.cov, cst, N, K, D, a.logZ,
                                                          p.rows_per_slab, p.part_len, part);

@@ -76,6 +76,10 @@ cudaError_t generate_iso_rows(float* X, const int64_t* row_ids, int64_t row0,
 
 int num_sms();
 
+// Raise (never lower) the dynamic shared-memory limit of `kernel` on the
+// current device to at least `bytes`; thread-safe.
+cudaError_t ensure_dynamic_smem(const void* kernel, size_t bytes);
+
 // Shared by the extern "C" entry points: record a failure message for
 // fgmm_last_error(), the sm_100 device check, and the validated E-step
 // dispatch (argument checks, workspace check, tensor-core or general path).

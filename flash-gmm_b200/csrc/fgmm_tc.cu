@@ -54,6 +54,7 @@
 #include <math.h>
 
 #include <algorithm>
+#include <atomic>
 
 #include "fgmm_internal.cuh"
 #include "fgmm_ptx.cuh"
@@ -796,11 +797,11 @@ size_t tc_smem_bytes(int nch) {
 
 template <class G>
 int max_active_clusters(int C) {
-  static int cache[kMaxCluster + 1] = {0};
-  if (cache[C] == 0) {
+  static std::atomic<int> cache[kMaxCluster + 1];
+  if (cache[C].load(std::memory_order_relaxed) == 0) {
     const int max_nch = (G::kMaxFeat + 63) / 64;
-    cudaFuncSetAttribute(tc_fused_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)tc_smem_bytes<G>(max_nch));
+    ensure_dynamic_smem(reinterpret_cast<const void*>(tc_fused_kernel<G>),
+                        tc_smem_bytes<G>(max_nch));
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -817,9 +818,9 @@ int max_active_clusters(int C) {
       cudaGetLastError();
       n = kSms / C;
     }
-    cache[C] = std::min(n, kSms / C);
+    cache[C].store(std::min(n, kSms / C), std::memory_order_relaxed);
   }
-  return cache[C];
+  return cache[C].load(std::memory_order_relaxed);
 }
 
 TcPlan plan_tc(int variant, int64_t N, int K, int D, bool query_device) {
@@ -884,8 +885,7 @@ SideStreams* side_streams() {
 
 template <class G>
 cudaError_t launch_fused(const TcPlan& pl, const TcParams& p, cudaStream_t stream) {
-  cudaError_t e = cudaFuncSetAttribute(tc_fused_kernel<G>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem);
+  cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(tc_fused_kernel<G>), pl.smem);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];

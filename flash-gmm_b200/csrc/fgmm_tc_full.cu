@@ -942,7 +942,7 @@ cudaError_t full_tc_estep(const EstepArgs& a) {
   p1.logZ = a.logZ;
   p1.err = ws.err;
   const size_t sm1 = p1_smem_bytes();
-  e = cudaFuncSetAttribute(full_ll_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm1);
+  e = ensure_dynamic_smem(reinterpret_cast<const void*>(full_ll_kernel), sm1);
   if (e != cudaSuccess) return e;
   profile_mark(false, st);
   full_ll_kernel<<<std::min(pl.num_tiles, kSmsFull), kP1Threads, sm1, st>>>(p1);
@@ -963,8 +963,7 @@ cudaError_t full_tc_estep(const EstepArgs& a) {
   p2.part = ws.part;
   p2.err = ws.err;
   const size_t sm2 = p2_smem_bytes(a.D);
-  e = cudaFuncSetAttribute(full_stats_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)sm2);
+  e = ensure_dynamic_smem(reinterpret_cast<const void*>(full_stats_kernel), sm2);
   if (e != cudaSuccess) return e;
   full_stats_kernel<<<pl.nfb * pl.ncb * pl.slabs, kP2Threads, sm2, st>>>(p2);
   profile_mark(true, st);
