@@ -8,15 +8,18 @@
 // chip.
 //
 // Both families are the same computation over a per-row feature vector F:
-//   isotropic:  F = x                     (nfeat = Dp)
-//               ll2[k,n] = c0'_k - ish_k |x_n|^2 + sum_d (2 ish_k mu_kd) x_nd
-//   diagonal:   F = [(x-c)^2, (x-c)]      (nfeat = 2 Dp; c = mean of the mu's)
+//   isotropic:  F = x - c                 (nfeat = Dp; c = mean of the mu's)
+//               ll2[k,n] = c0'_k - ish_k |x_n-c|^2 + sum_d 2 ish_k (mu_kd-c_d) F_nd
+//   diagonal:   F = [(x-c)^2, (x-c)]      (nfeat = 2 Dp)
 //               ll2[k,n] = c0'_k + sum_d (-A_kd (x-c)_d^2 + B_kd (x-c)_d)
 //               A = 1/2 e^{-lss} log2 e,  B = 2 A (mu - c)
 // (log2 units: the folding of flash_gmm_h100.py:286-291 / 137-138 and
 // flash_gmm_diag_h100.py:332-339 / 116-119).  The statistics GEMM
-// T = R^T F gives mu_acc (iso) or [sum r (x-c)^2, sum r (x-c)] (diag), from
-// which the reduction forms sig = rxsq - 2 m mu + m^2 Nk (diag:258-260).
+// T = R^T F gives sum r (x-c) (iso; mu_acc = T + c Nk) or
+// [sum r (x-c)^2, sum r (x-c)] (diag), from which the reduction forms
+// sig = rxsq - 2 m mu + m^2 Nk (diag:258-260).  Centring by one global vector
+// leaves every distance unchanged and shrinks the magnitudes that cancel in
+// the expanded form when the data sit away from the origin.
 //
 // Orientation ("components on TMEM lanes"):
 //   * a CTA owns a slice of 128 components = the 128 TMEM lanes; a cluster of
@@ -70,6 +73,8 @@ constexpr int kLoadWarp = kEpiWarps;                        // 16
 constexpr int kMmaWarp = kEpiWarps + 1;                     // 17
 constexpr int kThreads = (kEpiWarps + 4) * 32;              // 640: 5 warpgroups
 constexpr int kMaxCluster = 8;
+constexpr int kBlockComps = kComps * kMaxCluster;          // 1024 components per cluster
+constexpr int kMaxBlocks = 16;                              // K <= 16384 on the tensor cores
 constexpr int kMaxStages = 4;
 constexpr int kSplitRows = 4;                               // rows per warp step (split pass)
 constexpr int kSms = 148;                                   // B200
@@ -106,6 +111,11 @@ struct TcParams {
   const __half* Wlo;
   const float4* consts;      // [C*128] {c0', ish (iso), c0 (iso), s_k}
   const int* xscale;         // [0] = max|mu| (or max|mu - c|) bits -> a
+  // Mode 0 (single pass): logZ[row] out, natural log.  Component blocks of
+  // more than 1024 components (K > 1024) run in two phases: mode 1 writes
+  // each row's log-sum-exp over this launch's components to logZ[row] in
+  // log2 units; mode 2 reads the combined log2 normaliser from logZ[row] and
+  // forms r = 2^(ll - lz2) and the statistics without any exchange.
   float* logZ;
   float* part;               // [clusters][C*128][plen]
   int plen;
@@ -131,18 +141,18 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, SmemCtl*
 }
 
 // ---------------------------------------------------------------------------
-// Isotropic prep, one block per component (Kpad blocks of 128 threads):
+// Isotropic prep, one block per component (Kpad blocks of 128 threads), in
+// the centred form m = mu - c (c = mean of the mu's, as for diag):
 //   ish = 1/2 e^{-lss} log2 e,  c0 = (log pi - D/2 (log 2pi + lss)) log2 e,
-//   c0' = c0 - ish |mu|^2            (flash_gmm_h100.py:286-291)
-//   W = 2 ish mu, W' = W 2^-s (s from max|W_k|), split into fp16 hi/lo
-//   amax = max_k max_d |mu_kd| (atomic, for the X scale of the split pass).
+//   c0' = c0 - ish |m|^2             (flash_gmm_h100.py:286-291)
+//   W = 2 ish m, W' = W 2^-s (s from max|W_k|), split into fp16 hi/lo.
 // Components >= K get W = 0, ish = 0, c0' = c0 = -1e30 so they carry zero
 // responsibility; -inf log-weights are clamped to the same finite floor.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(128) tc_prep_kernel(
     const float* __restrict__ mu, int64_t smk, int64_t smd, const float* __restrict__ lss,
-    const float* __restrict__ lpi, int K, int D, int Dp, __half* __restrict__ Whi,
-    __half* __restrict__ Wlo, float4* __restrict__ consts, int* __restrict__ amax) {
+    const float* __restrict__ lpi, const float* __restrict__ cvec, int K, int D, int Dp,
+    __half* __restrict__ Whi, __half* __restrict__ Wlo, float4* __restrict__ consts) {
   const int k = blockIdx.x;
   const bool valid = k < K;
   double ish = 0.0, c0 = -1e30;
@@ -153,21 +163,19 @@ __global__ void __launch_bounds__(128) tc_prep_kernel(
   }
   const int d = threadIdx.x;  // Dp <= 128
   double m = 0.0;
-  if (valid && d < D) m = (double)mu[(int64_t)k * smk + (int64_t)d * smd];
+  if (valid && d < D) m = (double)mu[(int64_t)k * smk + (int64_t)d * smd] - (double)cvec[d];
   const float w = (float)(2.0 * ish * m);
   __shared__ double s_sq[4];
-  __shared__ float s_wmax[4], s_mmax[4];
+  __shared__ float s_wmax[4];
   double sq = m * m;
-  float wmax = fabsf(w), mmax = (float)fabs(m);
+  float wmax = fabsf(w);
   for (int o = 16; o > 0; o >>= 1) {
     sq += __shfl_xor_sync(0xffffffffu, sq, o);
     wmax = fmaxf(wmax, __shfl_xor_sync(0xffffffffu, wmax, o));
-    mmax = fmaxf(mmax, __shfl_xor_sync(0xffffffffu, mmax, o));
   }
   if ((threadIdx.x & 31) == 0) {
     s_sq[threadIdx.x >> 5] = sq;
     s_wmax[threadIdx.x >> 5] = wmax;
-    s_mmax[threadIdx.x >> 5] = mmax;
   }
   __syncthreads();
   const double musq = s_sq[0] + s_sq[1] + s_sq[2] + s_sq[3];
@@ -180,8 +188,6 @@ __global__ void __launch_bounds__(128) tc_prep_kernel(
     Wlo[(size_t)k * Dp + d] = __float2half_rn(ws - __half2float(h));
   }
   if (threadIdx.x == 0) {
-    const float mm = fmaxf(fmaxf(s_mmax[0], s_mmax[1]), fmaxf(s_mmax[2], s_mmax[3]));
-    if (valid) atomicMax(amax, __float_as_int(mm));  // non-negative floats order as ints
     double c0p = c0 - ish * musq;
     if (!(c0 > -1e30)) { c0 = -1e30; c0p = -1e30; }
     if (c0p < -1e30) c0p = -1e30;
@@ -259,7 +265,7 @@ __global__ void __launch_bounds__(128) tc_prep_diag_kernel(
 // ---------------------------------------------------------------------------
 // The fused kernel.
 // ---------------------------------------------------------------------------
-template <class G>
+template <class G, int MODE>
 __global__ void __launch_bounds__(kThreads, 1) tc_fused_kernel(const TcParams p) {
   constexpr int R = G::kRows, RB = G::kRB, NS = G::kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -273,7 +279,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fused_kernel(const TcParams p)
   float* scale_s = red_l + kEpiWarps * RB;           // [4 quadrants][R rows]
   float* fin = scale_s + 4 * R;                      // [8][128] end-of-kernel sums
   float2* xchg = reinterpret_cast<float2*>(fin + 8 * kComps);  // [2][kMaxCluster][R]
-  SmemCtl* ctl = reinterpret_cast<SmemCtl*>(xchg + 2 * kMaxCluster * R);
+  float* lzs = reinterpret_cast<float*>(xchg + 2 * kMaxCluster * R);  // mode 2: [NS][R]
+  SmemCtl* ctl = reinterpret_cast<SmemCtl*>(lzs + NS * R);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_rank();
@@ -384,13 +391,20 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fused_kernel(const TcParams p)
           }
         }
         tc_commit(&ctl->s_full);
+        if (MODE == 1) {
+          // LSE only: the stage is free once the epilogue has read this
+          // tile's distances and |x|^2 words (its s_empty arrival)
+          if (!mbar_wait(&ctl->s_empty, j & 1, ctl, p.err, 2)) break;
+          mbar_arrive(&ctl->xempty[b]);
+          continue;
+        }
         if (j >= 1) {
           if (!mbar_wait(&ctl->r_full, (j - 1) & 1, ctl, p.err, 4)) break;
           tc_fence_after();
           issue_stats(j - 1);
         }
       }
-      if (ntiles >= 1 && !ctl->abort_flag) {
+      if (MODE != 1 && ntiles >= 1 && !ctl->abort_flag) {
         if (mbar_wait(&ctl->r_full, (ntiles - 1) & 1, ctl, p.err, 4)) {
           tc_fence_after();
           issue_stats(ntiles - 1);
@@ -402,7 +416,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fused_kernel(const TcParams p)
   } else if (warp == kLoadWarp) {
     // ------------------------------------------------------------ F loader
     if (lane == 0) {
-      const uint32_t tx = (uint32_t)stage_bytes + (G::kDiag ? 0u : (uint32_t)R * 4u);
+      const uint32_t tx = (uint32_t)stage_bytes + (G::kDiag ? 0u : (uint32_t)R * 4u) +
+                          (MODE == 2 ? (uint32_t)R * 4u : 0u);
       for (int j = 0; j < ntiles; ++j) {
         const int b = j % NS;
         const int64_t tile = cluster_id + (int64_t)j * num_clusters;
@@ -412,6 +427,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fused_kernel(const TcParams p)
                  (uint32_t)stage_bytes, &ctl->xfull[b]);
         if (!G::kDiag)
           bulk_g2s(smem_u32(xsq + b * R), p.xsq + tile * R, (uint32_t)R * 4u, &ctl->xfull[b]);
+        if (MODE == 2)
+          bulk_g2s(smem_u32(lzs + b * R), p.logZ + tile * R, (uint32_t)R * 4u, &ctl->xfull[b]);
       }
     }
     __syncwarp();
@@ -451,7 +468,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fused_kernel(const TcParams p)
         tmem_wait_ld();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&ctl->s_empty);
+        if (MODE != 1 && lane == 0) mbar_arrive(&ctl->s_empty);
         if constexpr (G::kDiag) {
 #pragma unroll
           for (int i = 0; i < RB; ++i) ll[i] = fmaf(__uint_as_float(sv[i]), sck, c0p);
@@ -467,6 +484,17 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fused_kernel(const TcParams p)
           }
         }
       }
+      if (MODE == 1) {  // distances and |x|^2 read: the MMA warp frees the stage
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ctl->s_empty);
+      }
+      if constexpr (MODE == 2) {
+        // known log-normaliser: r = 2^(ll - lz2) directly (rows past N give 0)
+        const float* lzr = lzs + b * R + RB * cb;
+#pragma unroll
+        for (int i = 0; i < RB; ++i)
+          pv[i] = (row0 + RB * cb + i < p.N) ? ex2(ll[i] - lzr[i]) : 0.f;
+      } else {
       // Row maxima over this warp's 32 components (uniform across lanes),
       // p = 2^(ll - m), then the row sums by a transpose-reduce: log2(32)
       // shuffle rounds, each halving the rows a lane carries, leave the sum
@@ -544,12 +572,17 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fused_kernel(const TcParams p)
         GL += __shfl_xor_sync(0xffffffffu, GL, 16);
         const float lz2 = GM + lg2(GL);
         const bool valid = ok && (row0 + Rw < p.N);
-        if (valid && rank == 0 && g == 0) p.logZ[row0 + Rw] = lz2 * 0.6931471805599453f;
+        if (valid && rank == 0 && g == 0) {
+          if constexpr (MODE == 1) p.logZ[row0 + Rw] = lz2;
+          else p.logZ[row0 + Rw] = lz2 * 0.6931471805599453f;
+        }
         scale_s[g * R + Rw] = valid ? ex2(mg - lz2) : 0.f;
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&ctl->e_bar[1][grp]);
       if (!mbar_wait(&ctl->e_bar[1][grp], t & 1, ctl, p.err, 512)) break;
+      if constexpr (MODE == 1) continue;  // LSE only: no statistics
+      }
 
       // ---- D: r = p * scale, per-component sums, R^T into TMEM (16 rows at a time)
       const float* sc = scale_s + q * R + RB * cb;
@@ -561,7 +594,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fused_kernel(const TcParams p)
         uint32_t rh[8], rl[8];
 #pragma unroll
         for (int i = 0; i < 16; i += 4) {
-          const float4 s4 = *reinterpret_cast<const float4*>(sc + 16 * h + i);
+          float4 s4 = make_float4(1.f, 1.f, 1.f, 1.f);
+          if constexpr (MODE != 2) s4 = *reinterpret_cast<const float4*>(sc + 16 * h + i);
           const int o = 16 * h + i;
           const float r0 = pv[o + 0] * s4.x, r1 = pv[o + 1] * s4.y;
           const float r2 = pv[o + 2] * s4.z, r3 = pv[o + 3] * s4.w;
@@ -592,7 +626,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fused_kernel(const TcParams p)
     __syncwarp();
     if (lane == 0) mbar_arrive(&ctl->e_end);
     const bool ok = !ctl->abort_flag && ntiles >= 1 &&
-                    mbar_wait(&ctl->e_end, 0, ctl, p.err, 1024) &&
+                    mbar_wait(&ctl->e_end, 0, ctl, p.err, 1024) && MODE != 1 &&
                     mbar_wait(&ctl->t_done, 0, ctl, p.err, 128);
     float* out = p.part + ((size_t)cluster_id * p.C * kComps + kg) * p.plen;
     if (ok) {
@@ -642,7 +676,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fused_kernel(const TcParams p)
 // per-tile order of the fused kernel's stage buffers.  One warp per row; lane
 // l carries features 4l..4l+3 of x.  Rows past N and features past D are
 // zero.  v = hi + lo + O(2^-22 |v|).
-//   iso:  features x 2^-a, plus |x|^2 per row;
+//   iso:  features (x-c) 2^-a, plus |x-c|^2 per row;
 //   diag: features [((x-c) 2^-a)^2 | (x-c) 2^-a].
 // ---------------------------------------------------------------------------
 template <int ROWS, bool DIAG>
@@ -657,7 +691,7 @@ __global__ void __launch_bounds__(256) tc_split_kernel(
   const int nact = Dp / 4;
   const int f = 4 * lane;
   float4 cc = make_float4(0.f, 0.f, 0.f, 0.f);
-  if (DIAG && lane < nact) cc = *reinterpret_cast<const float4*>(cvec + f);
+  if (lane < nact) cc = *reinterpret_cast<const float4*>(cvec + f);
   // Each warp takes kSplitRows consecutive rows per step and issues all of
   // their loads before converting, to keep enough bytes in flight for HBM.
   for (int64_t row0 = ((int64_t)blockIdx.x * 8 + (threadIdx.x >> 5)) * kSplitRows; row0 < rows_pad;
@@ -677,17 +711,22 @@ __global__ void __launch_bounds__(256) tc_split_kernel(
           if (f + 2 < D) x.z = __ldg(src + (int64_t)(f + 2) * sxd);
           if (f + 3 < D) x.w = __ldg(src + (int64_t)(f + 3) * sxd);
         }
-        if (DIAG) {  // padding features have x = c = 0
-          x.x -= cc.x; x.y -= cc.y; x.z -= cc.z; x.w -= cc.w;
-        }
       }
       xr[u] = x;
     }
+    // all loads issued: centre and convert (padding features have x = c = 0;
+    // rows past N stay 0)
 #pragma unroll
     for (int u = 0; u < kSplitRows; ++u) {
       const int64_t row = row0 + u;
       if (row >= rows_pad) break;
-      const float4 x = xr[u];
+      float4 x = xr[u];
+      if (row < N) {
+        x.x -= cc.x;
+        x.y -= cc.y;
+        x.z -= cc.z;
+        x.w -= cc.w;
+      }
       if (lane < nact) {
         const float4 xs = make_float4(ldexpf(x.x, -a), ldexpf(x.y, -a), ldexpf(x.z, -a),
                                       ldexpf(x.w, -a));
@@ -723,22 +762,46 @@ __global__ void __launch_bounds__(256) tc_split_kernel(
   }
 }
 
-// Isotropic: sum the per-cluster partials {Nk, sig, mu_acc[D]} in cluster
-// order; NaN on a device-side error.
-__global__ void tc_reduce_kernel(const float* __restrict__ part, int clusters, int Kpad, int K,
-                                 int D, const int* __restrict__ err, float* __restrict__ Nk,
-                                 float* __restrict__ mu_acc, float* __restrict__ sig,
-                                 int accumulate) {
-  const int plen = D + 2;
-  const bool bad = *err != 0;
-  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < (int64_t)K * plen;
+// Chunked calls: partial slots [0, n) summed element-wise, in slot order, into
+// slot n - 1 (slot_elems floats per slot), while the last chunk's fused kernel
+// runs.  The reduction then starts from slot n - 1: the same fp32 summation
+// order as summing all slots in one pass.
+__global__ void __launch_bounds__(256) tc_part_presum_kernel(float* __restrict__ part, int n,
+                                                             int64_t slot_elems) {
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < slot_elems;
        e += (int64_t)gridDim.x * blockDim.x) {
-    const int k = (int)(e / plen), j = (int)(e % plen);
     float s = 0.f;
-    for (int c = 0; c < clusters; ++c) s += part[((size_t)c * Kpad + k) * plen + j];
-    if (bad) s = __int_as_float(0x7fc00000);
-    float* dst = j == 0 ? &Nk[k] : j == 1 ? &sig[k] : &mu_acc[(size_t)k * D + (j - 2)];
-    *dst = accumulate ? *dst + s : s;
+#pragma unroll 8
+    for (int c = 0; c < n; ++c) s += part[(size_t)c * slot_elems + e];
+    part[(size_t)(n - 1) * slot_elems + e] = s;
+  }
+}
+
+// Isotropic: sum the per-cluster partials {Nk, sig, sum r (x-c)} in cluster
+// order; mu_acc = sum r (x-c) + c Nk.  One block per component (thread j sums
+// partial column j < D + 2 <= 256); NaN on a device error.
+__global__ void __launch_bounds__(256) tc_reduce_kernel(
+    const float* __restrict__ part, int clusters, int Kpad, int K, int D,
+    const float* __restrict__ cvec, const int* __restrict__ err, float* __restrict__ Nk,
+    float* __restrict__ mu_acc, float* __restrict__ sig, int accumulate) {
+  const int plen = D + 2, j = threadIdx.x;
+  const bool bad = *err != 0;
+  __shared__ float s_n;
+  for (int k = blockIdx.x; k < K; k += gridDim.x) {
+    float s = 0.f;
+    if (j < plen) {
+#pragma unroll 16
+      for (int c = 0; c < clusters; ++c) s += part[((size_t)c * Kpad + k) * plen + j];
+    }
+    if (j == 0) s_n = s;
+    __syncthreads();
+    if (j >= 2 && j < plen) s = fmaf(cvec[j - 2], s_n, s);
+    __syncthreads();  // s_n is rewritten by the next component
+    if (j < plen) {
+      if (bad) s = __int_as_float(0x7fc00000);
+      float* dst = j == 0 ? &Nk[k] : j == 1 ? &sig[k] : &mu_acc[(size_t)k * D + (j - 2)];
+      *dst = accumulate ? *dst + s : s;
+    }
   }
 }
 
@@ -758,6 +821,7 @@ __global__ void tc_reduce_diag_kernel(const float* __restrict__ part, int cluste
        e += (int64_t)gridDim.x * blockDim.x) {
     const int k = (int)(e / (D + 1)), j = (int)(e % (D + 1));
     double n = 0.0;
+#pragma unroll 16
     for (int c = 0; c < clusters; ++c) n += part[((size_t)c * Kpad + k) * plen];
     if (j == 0) {
       const float v = bad ? qnan : (float)n;
@@ -766,6 +830,7 @@ __global__ void tc_reduce_diag_kernel(const float* __restrict__ part, int cluste
     }
     const int d = j - 1;
     double tx = 0.0, txx = 0.0;
+#pragma unroll 8
     for (int c = 0; c < clusters; ++c) {
       const float* pr = part + ((size_t)c * Kpad + k) * plen;
       tx += pr[1 + d];
@@ -782,6 +847,24 @@ __global__ void tc_reduce_diag_kernel(const float* __restrict__ part, int cluste
   }
 }
 
+// K > 1024: logZ of each row from the per-block log-sum-exps (log2 units),
+// lz2 = log2 sum_b 2^lse_b, written in log2 units for phase 2 and in natural
+// log for the caller (rows < N).
+__global__ void tc_lse_combine_kernel(const float* __restrict__ lse_part, int nb, int64_t npad,
+                                      int64_t N, float* __restrict__ lz2,
+                                      float* __restrict__ logZ) {
+  for (int64_t n = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; n < N;
+       n += (int64_t)gridDim.x * blockDim.x) {
+    float m = -3.0e38f;
+    for (int b = 0; b < nb; ++b) m = fmaxf(m, lse_part[(size_t)b * npad + n]);
+    float sum = 0.f;
+    for (int b = 0; b < nb; ++b) sum += ex2(lse_part[(size_t)b * npad + n] - m);
+    const float v = m + lg2(sum);
+    lz2[n] = v;
+    logZ[n] = v * 0.6931471805599453f;
+  }
+}
+
 struct TcPlan {
   bool diag;
   int rows, C, Kpad, Dp, nfeat, nch, num_tiles, clusters, plen;
@@ -792,7 +875,8 @@ template <class G>
 size_t tc_smem_bytes(int nch) {
   return 1024 + (size_t)G::kStages * 2 * nch * G::kChunk +
          ((size_t)G::kStages * G::kRows + 2 * kEpiWarps * G::kRB + 4 * G::kRows + 8 * kComps) * 4 +
-         (size_t)2 * kMaxCluster * G::kRows * 8 + sizeof(SmemCtl) + 64;
+         (size_t)2 * kMaxCluster * G::kRows * 8 + (size_t)G::kStages * G::kRows * 4 +
+         sizeof(SmemCtl) + 64;
 }
 
 template <class G>
@@ -800,7 +884,7 @@ int max_active_clusters(int C) {
   static std::atomic<int> cache[kMaxCluster + 1];
   if (cache[C].load(std::memory_order_relaxed) == 0) {
     const int max_nch = (G::kMaxFeat + 63) / 64;
-    ensure_dynamic_smem(reinterpret_cast<const void*>(tc_fused_kernel<G>),
+    ensure_dynamic_smem(reinterpret_cast<const void*>(tc_fused_kernel<G, 0>),
                         tc_smem_bytes<G>(max_nch));
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
@@ -814,7 +898,7 @@ int max_active_clusters(int C) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, tc_fused_kernel<G>, &cfg) != cudaSuccess || n <= 0) {
+    if (cudaOccupancyMaxActiveClusters(&n, tc_fused_kernel<G, 0>, &cfg) != cudaSuccess || n <= 0) {
       cudaGetLastError();
       n = kSms / C;
     }
@@ -859,7 +943,7 @@ int plan_chunks(const TcPlan& pl) { return pl.num_tiles >= kChunkMinTiles ? kChu
 struct SideStreams {
   bool ready = false;
   cudaStream_t hi = nullptr, lo = nullptr;
-  cudaEvent_t ev[kChunks + 3] = {};
+  cudaEvent_t ev[kChunks + 5] = {};
 };
 // Per host thread and device: calls from different threads never share
 // streams or events.
@@ -884,8 +968,10 @@ SideStreams* side_streams() {
 }
 
 template <class G>
-cudaError_t launch_fused(const TcPlan& pl, const TcParams& p, cudaStream_t stream) {
-  cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(tc_fused_kernel<G>), pl.smem);
+cudaError_t launch_fused(const TcPlan& pl, const TcParams& p, cudaStream_t stream, int mode = 0) {
+  auto kern = mode == 1 ? tc_fused_kernel<G, 1> : mode == 2 ? tc_fused_kernel<G, 2>
+                                                             : tc_fused_kernel<G, 0>;
+  cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), pl.smem);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
@@ -899,7 +985,148 @@ cudaError_t launch_fused(const TcPlan& pl, const TcParams& p, cudaStream_t strea
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, tc_fused_kernel<G>, p);
+  return cudaLaunchKernelEx(&cfg, kern, p);
+}
+
+// K > 1024 (iso / diag): the components run in blocks of 1024 (one 8-CTA
+// cluster each).  Phase 1 launches the fused kernel in LSE-only mode per
+// block, a small kernel combines the blocks' log-sum-exps into logZ, and
+// phase 2 launches it per block with that logZ (no exchange) to form the
+// statistics; the distance GEMM runs twice, the statistics once.
+struct MbWs {
+  int nb = 0;
+  int Kb[kMaxBlocks];
+  TcPlan pl[kMaxBlocks];
+  int* err = nullptr;
+  float* cvec = nullptr;
+  __half* Whi[kMaxBlocks];
+  __half* Wlo[kMaxBlocks];
+  float4* consts[kMaxBlocks];
+  float* part[kMaxBlocks];
+  uint8_t* xsplit = nullptr;
+  float* xsq = nullptr;
+  float* lse_part = nullptr;
+  float* lz2 = nullptr;
+  int64_t npad = 0;
+  size_t bytes = 0;
+};
+
+MbWs carve_mb(void* base, int variant, int64_t N, int K, int D, bool query_device) {
+  MbWs m;
+  m.nb = (K + kBlockComps - 1) / kBlockComps;
+  for (int b = 0; b < m.nb; ++b) {
+    m.Kb[b] = std::min(kBlockComps, K - b * kBlockComps);
+    m.pl[b] = plan_tc(variant, N, m.Kb[b], D, query_device);
+  }
+  const TcPlan& p0 = m.pl[0];
+  m.npad = (int64_t)p0.num_tiles * p0.rows;
+  WsCarve w(base);
+  m.err = w.take<int>(64);
+  m.cvec = w.take<float>(p0.Dp);
+  for (int b = 0; b < m.nb; ++b) {
+    m.Whi[b] = w.take<__half>((size_t)m.pl[b].Kpad * p0.nfeat);
+    m.Wlo[b] = w.take<__half>((size_t)m.pl[b].Kpad * p0.nfeat);
+    m.consts[b] = w.take<float4>(m.pl[b].Kpad);
+    m.part[b] = w.take<float>((size_t)(kSms / m.pl[b].C) * m.pl[b].Kpad * p0.plen);
+  }
+  m.xsplit = w.take<uint8_t>((size_t)p0.num_tiles * p0.stage_bytes);
+  if (!p0.diag) m.xsq = w.take<float>((size_t)p0.num_tiles * p0.rows);
+  m.lse_part = w.take<float>((size_t)m.nb * m.npad);
+  m.lz2 = w.take<float>((size_t)m.npad);
+  m.bytes = w.used + 256;
+  return m;
+}
+
+cudaError_t tc_estep_blocks(int variant, const EstepArgs& a) {
+  const MbWs m = carve_mb(a.ws, variant, a.N, a.K, a.D, true);
+  const TcPlan& p0 = m.pl[0];
+  cudaStream_t st = a.stream;
+  cudaError_t e = cudaMemsetAsync(m.err, 0, 2 * sizeof(int), st);
+  if (e != cudaSuccess) return e;
+  int launches = 0;
+  // one centre and X scale for all blocks
+  centre_kernel<<<p0.Dp, 256, 0, st>>>(a.mu, a.smk, a.smd, a.K, a.D, m.cvec, m.err + 1);
+  ++launches;
+  for (int b = 0; b < m.nb; ++b) {
+    const int64_t k0 = (int64_t)b * kBlockComps;
+    const float* mub = a.mu + k0 * a.smk;
+    if (p0.diag)
+      tc_prep_diag_kernel<<<m.pl[b].Kpad, 128, 0, st>>>(mub, a.smk, a.smd, a.cov + k0 * a.D,
+                                                        a.lpi + k0, m.cvec, m.err + 1, m.Kb[b],
+                                                        a.D, p0.Dp, m.Whi[b], m.Wlo[b],
+                                                        m.consts[b]);
+    else
+      tc_prep_kernel<<<m.pl[b].Kpad, 128, 0, st>>>(mub, a.smk, a.smd, a.cov + k0, a.lpi + k0,
+                                                   m.cvec, m.Kb[b], a.D, p0.Dp, m.Whi[b],
+                                                   m.Wlo[b], m.consts[b]);
+    ++launches;
+  }
+  const int vec_ok = a.sxd == 1 && (reinterpret_cast<uintptr_t>(a.X) & 15) == 0 && a.sxn % 4 == 0;
+  const int sblocks =
+      (int)std::min<int64_t>((m.npad + 8 * kSplitRows - 1) / (8 * kSplitRows), 16 * kSms);
+  if (p0.diag)
+    tc_split_kernel<DiagCfg::kRows, true><<<sblocks, 256, 0, st>>>(
+        a.X, a.sxn, a.sxd, vec_ok, a.N, a.D, p0.Dp, p0.nch, m.npad, m.err + 1, m.cvec, m.xsplit,
+        nullptr, m.err);
+  else
+    tc_split_kernel<IsoCfg::kRows, false><<<sblocks, 256, 0, st>>>(
+        a.X, a.sxn, a.sxd, vec_ok, a.N, a.D, p0.Dp, p0.nch, m.npad, m.err + 1, m.cvec, m.xsplit,
+        m.xsq, m.err);
+  ++launches;
+
+  TcParams p;
+  p.xsplit = m.xsplit;
+  p.xsq = m.xsq;
+  p.N = a.N;
+  p.D = a.D;
+  p.Dp = p0.Dp;
+  p.nfeat = p0.nfeat;
+  p.nch = p0.nch;
+  p.num_tiles = p0.num_tiles;
+  p.xscale = m.err + 1;
+  p.plen = p0.plen;
+  p.err = m.err;
+  profile_mark(false, st);
+  for (int phase = 1; phase <= 2; ++phase) {
+    for (int b = 0; b < m.nb; ++b) {
+      p.K = m.Kb[b];
+      p.C = m.pl[b].C;
+      p.Whi = m.Whi[b];
+      p.Wlo = m.Wlo[b];
+      p.consts = m.consts[b];
+      p.part = m.part[b];
+      p.logZ = phase == 1 ? m.lse_part + (size_t)b * m.npad : m.lz2;  // out / in, log2 units
+      e = p0.diag ? launch_fused<DiagCfg>(m.pl[b], p, st, phase)
+                  : launch_fused<IsoCfg>(m.pl[b], p, st, phase);
+      if (e != cudaSuccess) return e;
+      ++launches;
+    }
+    if (phase == 1) {
+      const int cblocks = (int)std::min<int64_t>((a.N + 255) / 256, 16 * kSms);
+      tc_lse_combine_kernel<<<cblocks, 256, 0, st>>>(m.lse_part, m.nb, m.npad, a.N, m.lz2,
+                                                     a.logZ);
+      ++launches;
+    }
+  }
+  profile_mark(true, st);
+  const int accumulate = (a.flags & 1u) ? 1 : 0;
+  for (int b = 0; b < m.nb; ++b) {
+    const int64_t k0 = (int64_t)b * kBlockComps;
+    if (p0.diag) {
+      const int64_t total = (int64_t)m.Kb[b] * (a.D + 1);
+      const int rblocks = (int)std::min<int64_t>((total + 255) / 256, 1024);
+      tc_reduce_diag_kernel<<<rblocks, 256, 0, st>>>(
+          m.part[b], m.pl[b].clusters, m.pl[b].Kpad, m.Kb[b], a.D, m.cvec, a.mu + k0 * a.smk,
+          a.smk, a.smd, m.err, a.Nk + k0, a.mu_acc + k0 * a.D, a.sig + k0 * a.D, accumulate);
+    } else {
+      tc_reduce_kernel<<<m.Kb[b], 256, 0, st>>>(m.part[b], m.pl[b].clusters, m.pl[b].Kpad,
+                                                 m.Kb[b], a.D, m.cvec, m.err, a.Nk + k0,
+                                                 a.mu_acc + k0 * a.D, a.sig + k0, accumulate);
+    }
+    ++launches;
+  }
+  count_launches(launches);
+  return cudaGetLastError();
 }
 
 }  // namespace
@@ -920,8 +1147,10 @@ __global__ void __launch_bounds__(256) centre_kernel(const float* __restrict__ m
   __shared__ float s_max[8];
   __shared__ float s_c;
   double sum = 0.0;
-  if (d < D)
+  if (d < D) {
+#pragma unroll 4
     for (int k = threadIdx.x; k < K; k += 256) sum += (double)mu[(int64_t)k * smk + (int64_t)d * smd];
+  }
   for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
   if ((threadIdx.x & 31) == 0) s_sum[threadIdx.x >> 5] = sum;
   __syncthreads();
@@ -934,9 +1163,11 @@ __global__ void __launch_bounds__(256) centre_kernel(const float* __restrict__ m
   __syncthreads();
   const float c = s_c;
   float mx = 0.f;
-  if (d < D)
+  if (d < D) {
+#pragma unroll 4
     for (int k = threadIdx.x; k < K; k += 256)
       mx = fmaxf(mx, fabsf(mu[(int64_t)k * smk + (int64_t)d * smd] - c));
+  }
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   if ((threadIdx.x & 31) == 0) s_max[threadIdx.x >> 5] = mx;
   __syncthreads();
@@ -960,7 +1191,7 @@ bool tc_supported(int variant, const EstepArgs& a, std::string* why) {
   } else {
     return full_tc_supported(a) ? true : no("full covariance: D > 64 or scratch too large");
   }
-  if ((a.K + kComps - 1) / kComps > kMaxCluster) return no("K > 1024");
+  if (a.K > kMaxBlocks * kBlockComps) return no("K > 16384");
   return true;
 }
 
@@ -970,10 +1201,11 @@ size_t tc_workspace_bytes(int variant, int64_t N, int K, int D) {
   probe.K = K;
   probe.D = D;
   if (!tc_supported(variant, probe, nullptr)) return 0;
+  if (K > kBlockComps) return carve_mb(nullptr, variant, N, K, D, false).bytes;
   TcPlan pl = plan_tc(variant, N, K, D, false);
   WsCarve w(nullptr);
   w.take<int>(64);
-  if (pl.diag) w.take<float>(pl.Dp);                                   // centre c
+  w.take<float>(pl.Dp);                                                // centre c
   w.take<__half>((size_t)pl.Kpad * pl.nfeat);
   w.take<__half>((size_t)pl.Kpad * pl.nfeat);
   w.take<float4>(pl.Kpad);
@@ -987,10 +1219,11 @@ size_t tc_workspace_bytes(int variant, int64_t N, int K, int D) {
 
 cudaError_t tc_estep(int variant, const EstepArgs& a) {
   if (variant == kFull) return full_tc_estep(a);
+  if (a.K > kBlockComps) return tc_estep_blocks(variant, a);
   TcPlan pl = plan_tc(variant, a.N, a.K, a.D, true);
   WsCarve w(a.ws);
   int* err = w.take<int>(64);
-  float* cvec = pl.diag ? w.take<float>(pl.Dp) : nullptr;
+  float* cvec = w.take<float>(pl.Dp);
   __half* Whi = w.take<__half>((size_t)pl.Kpad * pl.nfeat);
   __half* Wlo = w.take<__half>((size_t)pl.Kpad * pl.nfeat);
   float4* consts = w.take<float4>(pl.Kpad);
@@ -1012,25 +1245,23 @@ cudaError_t tc_estep(int variant, const EstepArgs& a) {
     if ((e = cudaStreamWaitEvent(lo, ss->ev[0], 0)) != cudaSuccess) return e;
   }
 
-  // err[0]: device error word, err[1]: max|mu| (iso) or max|mu - c| (diag),
-  // float bits, for the X scale
+  // err[0]: device error word, err[1]: max|mu - c| (float bits, for the X
+  // scale), written by the centre kernel
   e = cudaMemsetAsync(err, 0, 2 * sizeof(int), hi);
   if (e != cudaSuccess) return e;
   int launches = 0;
-  if (pl.diag) {
-    centre_kernel<<<pl.Dp, 256, 0, hi>>>(a.mu, a.smk, a.smd, a.K, a.D, cvec, err + 1);
-    tc_prep_diag_kernel<<<pl.Kpad, 128, 0, hi>>>(a.mu, a.smk, a.smd, a.cov, a.lpi, cvec, err + 1,
-                                                 a.K, a.D, pl.Dp, Whi, Wlo, consts);
-    launches += 2;
-  } else {
-    tc_prep_kernel<<<pl.Kpad, 128, 0, hi>>>(a.mu, a.smk, a.smd, a.cov, a.lpi, a.K, a.D, pl.Dp,
-                                            Whi, Wlo, consts, err + 1);
-    launches += 1;
-  }
-  if (nchunks > 1) {
+  centre_kernel<<<pl.Dp, 256, 0, hi>>>(a.mu, a.smk, a.smd, a.K, a.D, cvec, err + 1);
+  if (nchunks > 1) {  // the split passes need c and max|mu - c| only: they overlap the prep
     if ((e = cudaEventRecord(ss->ev[1], hi)) != cudaSuccess) return e;
     if ((e = cudaStreamWaitEvent(lo, ss->ev[1], 0)) != cudaSuccess) return e;
   }
+  if (pl.diag)
+    tc_prep_diag_kernel<<<pl.Kpad, 128, 0, hi>>>(a.mu, a.smk, a.smd, a.cov, a.lpi, cvec, err + 1,
+                                                 a.K, a.D, pl.Dp, Whi, Wlo, consts);
+  else
+    tc_prep_kernel<<<pl.Kpad, 128, 0, hi>>>(a.mu, a.smk, a.smd, a.cov, a.lpi, cvec, a.K, a.D,
+                                            pl.Dp, Whi, Wlo, consts);
+  launches += 2;
   const int vec_ok = a.sxd == 1 && (reinterpret_cast<uintptr_t>(a.X) & 15) == 0 && a.sxn % 4 == 0;
   const int tiles_per_chunk = (pl.num_tiles + nchunks - 1) / nchunks;
 
@@ -1051,7 +1282,7 @@ cudaError_t tc_estep(int variant, const EstepArgs& a) {
           nullptr, err);
     else
       tc_split_kernel<IsoCfg::kRows, false><<<sblocks, 256, 0, lo>>>(
-          Xc, a.sxn, a.sxd, vec_ok, rows, a.D, pl.Dp, pl.nch, rows_pad, err + 1, nullptr, xs_c,
+          Xc, a.sxn, a.sxd, vec_ok, rows, a.D, pl.Dp, pl.nch, rows_pad, err + 1, cvec, xs_c,
           xsq + (size_t)t0 * pl.rows, err);
     ++launches;
     if (nchunks > 1 && (e = cudaEventRecord(ss->ev[2 + c], lo)) != cudaSuccess) return e;
@@ -1072,7 +1303,7 @@ cudaError_t tc_estep(int variant, const EstepArgs& a) {
   p.xscale = err + 1;
   p.plen = pl.plen;
   p.err = err;
-  int part_clusters = 0;
+  int part_clusters = 0, presummed = 0;
   for (int c = 0; c < nchunks; ++c) {
     const int t0 = c * tiles_per_chunk, t1 = std::min(pl.num_tiles, t0 + tiles_per_chunk);
     if (t0 >= t1) break;
@@ -1092,8 +1323,24 @@ cudaError_t tc_estep(int variant, const EstepArgs& a) {
     if (e != cudaSuccess) return e;
     part_clusters += pc.clusters;
     ++launches;
+    if (nchunks > 1 && c == nchunks - 2) {
+      // pre-sum the partials so far on the side stream, behind the last chunk
+      const int64_t slot = (int64_t)pl.Kpad * pl.plen;
+      if ((e = cudaEventRecord(ss->ev[3 + kChunks], hi)) != cudaSuccess) return e;
+      if ((e = cudaStreamWaitEvent(lo, ss->ev[3 + kChunks], 0)) != cudaSuccess) return e;
+      tc_part_presum_kernel<<<(int)std::min<int64_t>((slot + 255) / 256, 4 * kSms), 256, 0, lo>>>(
+          part, part_clusters, slot);
+      ++launches;
+      if ((e = cudaEventRecord(ss->ev[4 + kChunks], lo)) != cudaSuccess) return e;
+      presummed = part_clusters - 1;
+    }
   }
   profile_mark(true, hi);
+  if (presummed > 0) {
+    if ((e = cudaStreamWaitEvent(hi, ss->ev[4 + kChunks], 0)) != cudaSuccess) return e;
+    part += (size_t)presummed * pl.Kpad * pl.plen;
+    part_clusters -= presummed;
+  }
   const int accumulate = (a.flags & 1u) ? 1 : 0;
   if (pl.diag) {
     const int64_t total = (int64_t)a.K * (a.D + 1);
@@ -1102,10 +1349,8 @@ cudaError_t tc_estep(int variant, const EstepArgs& a) {
                                                    a.mu, a.smk, a.smd, err, a.Nk, a.mu_acc,
                                                    a.sig, accumulate);
   } else {
-    const int64_t total = (int64_t)a.K * (a.D + 2);
-    const int rblocks = (int)std::min<int64_t>((total + 255) / 256, 1024);
-    tc_reduce_kernel<<<rblocks, 256, 0, hi>>>(part, part_clusters, pl.Kpad, a.K, a.D, err, a.Nk,
-                                              a.mu_acc, a.sig, accumulate);
+    tc_reduce_kernel<<<a.K, 256, 0, hi>>>(part, part_clusters, pl.Kpad, a.K, a.D, cvec, err, a.Nk,
+                                          a.mu_acc, a.sig, accumulate);
   }
   ++launches;
   count_launches(launches);

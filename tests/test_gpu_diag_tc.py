@@ -68,6 +68,32 @@ def test_tc_diag_offset_data_and_strided_inputs():
     assert_parity(out, ref, what="offset diag, strided")
 
 
+@pytest.mark.parametrize("kind,N,K,D", [("iso", 600_000, 2048, 128), ("diag", 300_000, 1500, 96)])
+def test_tc_more_than_1024_components_many_tiles(kind, N, K, D):
+    """K > 1024 with many row tiles per cluster, so every stage buffer is
+    reused many times in both passes: against the general kernels, plus
+    sum_k Nk = N and sum_k mu_acc = sum_n x_n."""
+    X, mu, cov, lpi = (t.to(DEV) for t in _many_components(kind, N, K, D, 0.0))
+    v = L.FGMM_VARIANT_ISO if kind == "iso" else L.FGMM_VARIANT_DIAG
+    tc = _np(L.estep(v, X, mu, cov, lpi))
+    gen = _np(L.estep(v, X, mu, cov, lpi, force_general=True))
+    assert np.isfinite(tc[0]).all() and np.isfinite(tc[1]).all()
+    assert abs(tc[1].astype(np.float64).sum() - N) <= 1e-5 * N
+    xs = X.double().sum(0).cpu().numpy()
+    np.testing.assert_allclose(tc[2].astype(np.float64).sum(0), xs,
+                               atol=1e-4 * np.abs(tc[2]).max() * 4)
+    assert_parity(tc, gen, what=f"{kind} K={K} N={N} vs general")
+
+
+def test_tc_iso_offset_data():
+    """Isotropic data far from the origin (every feature near +60): the
+    centred features keep the expanded distance at fp32-level accuracy."""
+    X, mu, lss, lpi = _many_components("iso", 8000, 700, 128, 60.0)
+    ref = O.estep_iso(X.numpy(), mu.numpy(), lss.numpy(), lpi.numpy())
+    out = _np(L.estep(L.FGMM_VARIANT_ISO, *(t.to(DEV) for t in (X, mu, lss, lpi))))
+    assert_parity(out, ref, what="offset iso")
+
+
 def test_tc_diag_neg_inf_weight():
     N, K, D = 2000, 40, 16
     X, mu, lss, lpi = _case(N, K, D, seed=3)
@@ -92,3 +118,39 @@ def test_c3_full_size():
                                atol=1e-4 * np.abs(mu_acc).max() * 4)
     ref = O.estep_diag(X.cpu().numpy(), mu.cpu().numpy(), lss.cpu().numpy(), lpi.cpu().numpy())
     assert_parity(out, ref, what="C3 full size")
+
+
+def _many_components(kind, N, K, D, offset):
+    """The C2 / C3 recipes (gmm_data) with means moved off the data rows,
+    varied variances and weights, all shifted by `offset`."""
+    make = gmm_data.iso_mixture if kind == "iso" else gmm_data.diag_mixture
+    X, mu, cov, _ = make(N, K, D, seed=K + D)
+    g = torch.Generator().manual_seed(D)
+    X, mu = X + offset, mu + offset + 0.3 * torch.randn(K, D, generator=g)
+    if kind == "iso":
+        cov = 0.4 * torch.rand(K, generator=g) - 0.2
+    lpi = torch.log_softmax(torch.randn(K, generator=g), 0)
+    return X, mu, cov, lpi
+
+
+@pytest.mark.parametrize("kind,N,K,D,offset", [("iso", 4000, 1500, 64, 0.0),
+                                               ("iso", 3000, 2048, 128, 0.0),
+                                               ("iso", 4000, 3100, 32, 0.0),
+                                               ("iso", 3000, 2048, 128, 40.0),
+                                               ("diag", 3000, 1500, 48, 0.0),
+                                               ("diag", 2400, 2300, 96, 0.0)])
+def test_tc_more_than_1024_components(kind, N, K, D, offset):
+    """K > 1024: blocks of 1024 components, LSE-only pass per block, combined
+    logZ, then the statistics pass per block with that logZ."""
+    X, mu, cov, lpi = _many_components(kind, N, K, D, offset)
+    v = L.FGMM_VARIANT_ISO if kind == "iso" else L.FGMM_VARIANT_DIAG
+    ref = (O.estep_iso if kind == "iso" else O.estep_diag)(X.numpy(), mu.numpy(), cov.numpy(),
+                                                            lpi.numpy())
+    Xd, mud, covd, lpid = (t.to(DEV) for t in (X, mu, cov, lpi))
+    tc = _np(L.estep(v, Xd, mud, covd, lpid))
+    gen = _np(L.estep(v, Xd, mud, covd, lpid, force_general=True))
+    assert_parity(tc, ref, what=f"{kind} K={K} vs oracle")
+    assert_parity(tc, gen, what=f"{kind} K={K} vs general")
+    again = _np(L.estep(v, Xd, mud, covd, lpid))
+    for a, b in zip(tc, again):
+        np.testing.assert_array_equal(a, b)
