@@ -7,10 +7,12 @@
 // kernels:
 //
 // Pass 1 (full_ll_kernel, rows on TMEM lanes): for a 128-row tile of
-//   x~ = x - c (c = mean of the means), V = x~ [L_G1 | L_G2 | ...] is one
-//   M=128, N=G*Dp (256 for D=64: 4 components), K=Dp GEMM per group of G
-//   components, A = the x~ tile and B = the group's L columns, both fp16 hi/lo
-//   in shared memory (three passes lo*hi + hi*lo + hi*hi, 22-bit operands).
+//   x~ = x - c (c = mean of the means), V = x~ L_k is evaluated per region of
+//   16 components x 16 columns j of their L's: one M=128, N=256 GEMM with
+//   A = the x~ tile and B = those L columns, both fp16 hi/lo in shared memory
+//   (three passes lo*hi + hi*lo + hi*hi, 22-bit operands).  L_k is lower
+//   triangular, so columns j in block jb only meet rows d >= 16 jb: region jb
+//   runs the K-steps s = jb .. Dp/16-1 (at D = 64: 10 of 16 K-steps).
 //   The epilogue (thread = row) forms v = V - b_k (b_k = (mu_k - c)^T L_k),
 //   maha = |v|^2, ll2 = const_k - maha/2 * log2 e (full:124-129, 289-296, log2
 //   units), keeps an online log-sum-exp per row and writes ll2 for pass 2.
@@ -49,9 +51,11 @@ constexpr int kP1MmaWarp = 17;
 constexpr int kP1Threads = 18 * 32;
 constexpr int kP1LStages = 2;
 constexpr int kXTile = kP1Rows * 128;        // 16 KB: one hi (or lo) x~ tile, 64 features
-constexpr int kLGroup = 256 * 128;           // 32 KB: one hi (or lo) group of L columns
-constexpr int kP1BSlots = 4;                 // ring of per-group b vectors + constants
-constexpr int kBSlot = 256 * 4 + 16 * 8;     // bytes: b (G*Dp <= 256 floats) + 16 float2
+constexpr int kCG = 16;                      // components per group (16 x 16 columns = MMA N)
+constexpr int kLGroup = 256 * 128;           // 32 KB: one hi (or lo) region of L columns
+constexpr int kP1BSlots = 2;                 // ring of per-group b vectors + constants
+constexpr int kBOff = kCG * kFullMaxD * 4;   // 4 KB: b of 16 components, then 16 float2
+constexpr int kBSlot = kBOff + kCG * 8;
 
 // ---- pass 2
 constexpr int kP2Rows = 64;                  // rows per chunk (MMA K extent)
@@ -67,12 +71,14 @@ constexpr int kRBlock = kP2Comps * 128;      // 16 KB: R^T hi (or lo), 128 compo
 
 struct P1Params {
   const uint8_t* xsplit;   // [num_tiles][hi 16 KB | lo 16 KB]  x~ 2^-a1, swizzled K-major
-  const uint8_t* lgroups;  // [num_groups][hi 32 KB | lo 32 KB] L columns 2^-s_k, K-major
+  const uint8_t* lgroups;  // [num_groups][Dp/16 regions][hi 32 KB | lo 32 KB] L columns
+                           // 2^-s_k, K-major; region row i*16 + jj = column 16 jb + jj of
+                           // component 16 g + i
   const float* bvec;       // [Kpad][Dp]  b_k = (mu_k - c)^T L_k
-  const float2* kconst;    // [num_groups][16]  {const_k in log2 units, s_k} per group slot
+  const float2* kconst;    // [num_groups][16]  {const_k in log2 units, s_k}
   const int* amax;         // max|mu - c| (float bits) -> a1
   int64_t N;
-  int K, Dp, G, num_groups, num_tiles;
+  int K, Dp, num_groups, num_tiles;
   int64_t ld_ll;           // row stride of ll2 (= num_tiles * 128)
   float* ll2;              // [Kpad][ld_ll]
   float* lz2;              // [ld_ll]  logZ in log2 units (for pass 2)
@@ -122,15 +128,16 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
 
 // ---------------------------------------------------------------------------
 // Prep, one block per component k < Kpad (64 threads; thread e = output index):
-//   s_k from max|L_k| (exact power of two), group layout of the L columns
-//   (row (k % G)*Dp + e of group k/G holds L_k[:, e] 2^-s_k, fp16 hi/lo),
+//   s_k from max|L_k| (exact power of two), region layout of the L columns
+//   (row (k % 16)*16 + e % 16 of region e/16 of group k/16 holds L_k[:, e]
+//   2^-s_k, fp16 hi/lo),
 //   b_k[e] = sum_d (mu_kd - c_d) L_k[d, e],
 //   const_k = (log pi_k + sum_d log(|L_kdd| + 1e-30) - D/2 log 2pi) log2 e.
 // Components >= K get zero columns and const = -1e30.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(64) full_prep_kernel(
     const float* __restrict__ mu, int64_t smk, int64_t smd, const float* __restrict__ L,
-    const float* __restrict__ lpi, const float* __restrict__ cvec, int K, int D, int Dp, int G,
+    const float* __restrict__ lpi, const float* __restrict__ cvec, int K, int D, int Dp,
     uint8_t* __restrict__ lgroups, float* __restrict__ bvec, float2* __restrict__ kconst) {
   const int k = blockIdx.x;
   const int e = threadIdx.x;
@@ -160,8 +167,8 @@ __global__ void __launch_bounds__(64) full_prep_kernel(
   __syncthreads();
   const int sk = scale_exp_to(fmaxf(s_max[0], s_max[1]), 5);
   if (e < Dp) {
-    uint8_t* grp = lgroups + (size_t)(k / G) * 2 * kLGroup;
-    const int rr = (k % G) * Dp + e;
+    uint8_t* grp = lgroups + ((size_t)(k / kCG) * (Dp / 16) + e / 16) * 2 * kLGroup;
+    const int rr = (k % kCG) * 16 + e % 16;
     for (int d0 = 0; d0 < 64; d0 += 8) {
       uint32_t hi[4], lo[4];
       for (int u = 0; u < 8; u += 2) {
@@ -182,7 +189,7 @@ __global__ void __launch_bounds__(64) full_prep_kernel(
       c = ((double)lpi[k] + s_logd[0] + s_logd[1] - 0.5 * D * kLog2Pi) * kLog2E;
       if (!(c > -1e30)) c = -1e30;
     }
-    kconst[(size_t)(k / G) * 16 + (k % G)] = make_float2((float)c, (float)sk);
+    kconst[k] = make_float2((float)c, (float)sk);
   }
 }
 
@@ -320,42 +327,45 @@ __global__ void __launch_bounds__(kP1Threads, 1) full_ll_kernel(const P1Params p
     return (int64_t)blockIdx.x + (int64_t)(2 * q + tt) * gridDim.x;
   };
 
+  const int nreg = p.Dp / 16;  // regions (column blocks) per component group
   if (warp == kP1MmaWarp) {
     if (lane == 0) {
-      const uint32_t idesc = idesc_f16(p.G * p.Dp, false);
-      const int ks = p.Dp / 16;
-      int gi = 0, li = 0;  // accumulator uses, L-group loads
+      const uint32_t idesc = idesc_f16(256, false);
+      int gi = 0, li = 0;  // accumulator uses, region loads
       bool ok = true;
       for (int q = 0; q < npairs && ok; ++q) {
         const int nt = pair_tiles(q);
         for (int tt = 0; tt < nt && ok; ++tt)
           ok = mbar_wait_flag(&ctl->xfull[tt], q & 1, abort_flag, p.err, 1);
-        for (int g = 0; g < p.num_groups && ok; ++g, ++li) {
-          const int st = li % kP1LStages;
-          if (!mbar_wait_flag(&ctl->lfull[st], (li / kP1LStages) & 1, abort_flag, p.err, 2)) {
-            ok = false;
-            break;
-          }
-          const uint32_t lhi = smem_u32(lsm + st * 2 * kLGroup), llo = lhi + kLGroup;
-          for (int tt = 0; tt < nt; ++tt, ++gi) {
-            const int acc = gi & 1;
-            if (!mbar_wait_flag(&ctl->aempty[acc], ((gi >> 1) & 1) ^ 1, abort_flag, p.err, 4)) {
+        for (int g = 0; g < p.num_groups && ok; ++g) {
+          for (int jb = 0; jb < nreg && ok; ++jb, ++li) {
+            const int st = li % kP1LStages;
+            if (!mbar_wait_flag(&ctl->lfull[st], (li / kP1LStages) & 1, abort_flag, p.err, 2)) {
               ok = false;
               break;
             }
-            tc_fence_after();
-            const uint32_t xhi = smem_u32(xs + tt * 2 * kXTile), xlo = xhi + kXTile;
-            // terms x_lo*L_hi, x_hi*L_lo, x_hi*L_hi (smallest magnitudes first)
-            for (int term = 0; term < 3; ++term) {
-              const uint32_t a = term == 0 ? xlo : xhi;
-              const uint32_t b = term == 1 ? llo : lhi;
-              for (int s = 0; s < ks; ++s)
-                mma_ss(tmem + acc * 256, desc_kmajor(a + 32 * s), desc_kmajor(b + 32 * s), idesc,
-                       (term == 0 && s == 0) ? 0u : 1u);
+            const uint32_t lhi = smem_u32(lsm + st * 2 * kLGroup), llo = lhi + kLGroup;
+            for (int tt = 0; tt < nt; ++tt, ++gi) {
+              const int acc = gi & 1;
+              if (!mbar_wait_flag(&ctl->aempty[acc], ((gi >> 1) & 1) ^ 1, abort_flag, p.err, 4)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              const uint32_t xhi = smem_u32(xs + tt * 2 * kXTile), xlo = xhi + kXTile;
+              // terms x_lo*L_hi, x_hi*L_lo, x_hi*L_hi (smallest magnitudes first);
+              // K-steps below jb meet the zero upper triangle of L and are skipped
+              for (int term = 0; term < 3; ++term) {
+                const uint32_t a = term == 0 ? xlo : xhi;
+                const uint32_t b = term == 1 ? llo : lhi;
+                for (int ks = jb; ks < nreg; ++ks)
+                  mma_ss(tmem + acc * 256, desc_kmajor(a + 32 * ks), desc_kmajor(b + 32 * ks),
+                         idesc, (term == 0 && ks == jb) ? 0u : 1u);
+              }
+              tc_commit(&ctl->afull[acc]);
             }
-            tc_commit(&ctl->afull[acc]);
+            tc_commit(&ctl->lempty[st]);
           }
-          tc_commit(&ctl->lempty[st]);
         }
         for (int tt = 0; tt < nt; ++tt) tc_commit(&ctl->xempty[tt]);
       }
@@ -363,8 +373,9 @@ __global__ void __launch_bounds__(kP1Threads, 1) full_ll_kernel(const P1Params p
     __syncwarp();
   } else if (warp == kP1LoadWarp) {
     if (lane == 0) {
-      int li = 0;
+      int li = 0, bi = 0;
       bool ok = true;
+      const uint32_t bbytes = (uint32_t)(kCG * p.Dp * 4);
       for (int q = 0; q < npairs && ok; ++q) {
         const int nt = pair_tiles(q);
         for (int tt = 0; tt < nt && ok; ++tt) {
@@ -376,95 +387,120 @@ __global__ void __launch_bounds__(kP1Threads, 1) full_ll_kernel(const P1Params p
           bulk_g2s(smem_u32(xs + tt * 2 * kXTile), p.xsplit + tile_of(q, tt) * (2 * kXTile),
                    2 * kXTile, &ctl->xfull[tt]);
         }
-        for (int g = 0; g < p.num_groups && ok; ++g, ++li) {
-          const int st = li % kP1LStages;
-          if (!mbar_wait_flag(&ctl->lempty[st], ((li / kP1LStages) & 1) ^ 1, abort_flag, p.err,
-                              16)) {
-            ok = false;
-            break;
-          }
-          mbar_arrive_expect_tx(&ctl->lfull[st], 2 * kLGroup);
-          bulk_g2s(smem_u32(lsm + st * 2 * kLGroup), p.lgroups + (size_t)g * (2 * kLGroup),
-                   2 * kLGroup, &ctl->lfull[st]);
-          const int bs = li % kP1BSlots;
-          if (!mbar_wait_flag(&ctl->bempty[bs], ((li / kP1BSlots) & 1) ^ 1, abort_flag, p.err,
+        for (int g = 0; g < p.num_groups && ok; ++g, ++bi) {
+          const int bs = bi % kP1BSlots;
+          if (!mbar_wait_flag(&ctl->bempty[bs], ((bi / kP1BSlots) & 1) ^ 1, abort_flag, p.err,
                               128)) {
             ok = false;
             break;
           }
-          const uint32_t bbytes = (uint32_t)(p.G * p.Dp * 4);
-          mbar_arrive_expect_tx(&ctl->bfull[bs], bbytes + 128u);
-          bulk_g2s(smem_u32(bst + bs * kBSlot), p.bvec + (size_t)g * p.G * p.Dp, bbytes,
+          mbar_arrive_expect_tx(&ctl->bfull[bs], bbytes + (uint32_t)(kCG * 8));
+          bulk_g2s(smem_u32(bst + bs * kBSlot), p.bvec + (size_t)g * kCG * p.Dp, bbytes,
                    &ctl->bfull[bs]);
-          bulk_g2s(smem_u32(bst + bs * kBSlot + 1024), p.kconst + (size_t)g * 16, 128u,
-                   &ctl->bfull[bs]);
+          bulk_g2s(smem_u32(bst + bs * kBSlot + kBOff), p.kconst + (size_t)g * kCG,
+                   (uint32_t)(kCG * 8), &ctl->bfull[bs]);
+          for (int jb = 0; jb < nreg; ++jb, ++li) {
+            const int st = li % kP1LStages;
+            if (!mbar_wait_flag(&ctl->lempty[st], ((li / kP1LStages) & 1) ^ 1, abort_flag, p.err,
+                                16)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&ctl->lfull[st], 2 * kLGroup);
+            bulk_g2s(smem_u32(lsm + st * 2 * kLGroup),
+                     p.lgroups + ((size_t)g * nreg + jb) * (2 * kLGroup), 2 * kLGroup,
+                     &ctl->lfull[st]);
+          }
         }
       }
     }
     __syncwarp();
   } else if (warp < kP1EpiWarps) {
     // thread = row (TMEM lane) of tile tt; warp quarter h takes components
-    // i = h, h+4, ... of each group
+    // i = h, h+4, h+8, h+12 of each group (16 columns of each per region) and
+    // keeps their partial |v|^2 over the regions
     const int q4 = warp & 3, h = warp >> 2;
     const int row = q4 * 32 + lane;
     const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
     const float kHalfLog2E = 0.72134752044448170f;
-    int gi = 0, li = 0;
+    int gi = 0, bi = 0;
     for (int q = 0; q < npairs; ++q) {
       const int nt = pair_tiles(q);
       float m[2] = {-3.0e38f, -3.0e38f}, l[2] = {0.f, 0.f};
       bool ok = true;
-      for (int g = 0; g < p.num_groups && ok; ++g, ++li) {
-        const int bs = li % kP1BSlots;
-        if (!mbar_wait_flag(&ctl->bfull[bs], (li / kP1BSlots) & 1, abort_flag, p.err, 256)) {
+      for (int g = 0; g < p.num_groups && ok; ++g, ++bi) {
+        const int bs = bi % kP1BSlots;
+        if (!mbar_wait_flag(&ctl->bfull[bs], (bi / kP1BSlots) & 1, abort_flag, p.err, 256)) {
           ok = false;
           break;
         }
         const float* bgrp = reinterpret_cast<const float*>(bst + bs * kBSlot);
-        const float2* kgrp = reinterpret_cast<const float2*>(bst + bs * kBSlot + 1024);
-        for (int tt = 0; tt < nt; ++tt, ++gi) {
-          const int acc = gi & 1;
-          if (!mbar_wait_flag(&ctl->afull[acc], (gi >> 1) & 1, abort_flag, p.err, 32)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const int64_t n = tile_of(q, tt) * kP1Rows + row;
-          const bool live = n < p.N;
-          for (int i = h; i < p.G; i += 4) {
-            const int k = g * p.G + i;
-            if (k >= p.K) break;
-            const float2 kc = kgrp[i];
-            const float sc = ldexpf(1.0f, xa + (int)kc.y);  // V = V' 2^(a1 + s_k)
-            const float4* bk = reinterpret_cast<const float4*>(bgrp + i * p.Dp);
-            float mh[4] = {0.f, 0.f, 0.f, 0.f};  // independent partial sums of maha
-            for (int c = 0; c < p.Dp; c += 32) {
-              uint32_t v[32];
-              float bb[32];
-              const bool two = c + 16 < p.Dp;
-              tmem_ld16(tmem + lane_base + acc * 256 + i * p.Dp + c, v);
-              if (two) tmem_ld16(tmem + lane_base + acc * 256 + i * p.Dp + c + 16, v + 16);
+        const float2* kgrp = reinterpret_cast<const float2*>(bst + bs * kBSlot + kBOff);
+        float sc[4];  // V = V' 2^(a1 + s_k)
 #pragma unroll
-              for (int u = 0; u < 8; ++u) {
-                const float4 b4 = (u < 4 || two) ? bk[c / 4 + u] : make_float4(0.f, 0.f, 0.f, 0.f);
-                bb[4 * u + 0] = b4.x;
-                bb[4 * u + 1] = b4.y;
-                bb[4 * u + 2] = b4.z;
-                bb[4 * u + 3] = b4.w;
+        for (int u = 0; u < 4; ++u) sc[u] = ldexpf(1.0f, xa + (int)kgrp[h + 4 * u].y);
+        float mp[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};  // partial |v|^2
+        for (int jb = 0; jb < nreg && ok; ++jb) {
+#pragma unroll
+          for (int tt = 0; tt < 2; ++tt) {
+            if (tt >= nt) break;
+            const int acc = gi & 1;
+            if (!mbar_wait_flag(&ctl->afull[acc], (gi >> 1) & 1, abort_flag, p.err, 32)) {
+              ok = false;
+              break;
+            }
+            ++gi;
+            tc_fence_after();
+#pragma unroll
+            for (int u0 = 0; u0 < 4; u0 += 2) {
+              uint32_t v[32];
+              tmem_ld16(tmem + lane_base + acc * 256 + (h + 4 * u0) * 16, v);
+              tmem_ld16(tmem + lane_base + acc * 256 + (h + 4 * u0 + 4) * 16, v + 16);
+              float bb[32];
+#pragma unroll
+              for (int w = 0; w < 2; ++w) {
+                const float4* bk =
+                    reinterpret_cast<const float4*>(bgrp + (h + 4 * (u0 + w)) * p.Dp + 16 * jb);
+#pragma unroll
+                for (int z = 0; z < 4; ++z) {
+                  const float4 b4 = bk[z];
+                  bb[16 * w + 4 * z + 0] = b4.x;
+                  bb[16 * w + 4 * z + 1] = b4.y;
+                  bb[16 * w + 4 * z + 2] = b4.z;
+                  bb[16 * w + 4 * z + 3] = b4.w;
+                }
               }
               tmem_wait_ld();
-              if (!two) {
 #pragma unroll
-                for (int u = 16; u < 32; ++u) v[u] = 0u;
-              }
+              for (int w = 0; w < 2; ++w) {
+                float s0 = 0.f, s1 = 0.f;
 #pragma unroll
-              for (int u = 0; u < 32; ++u) {
-                const float dv = fmaf(__uint_as_float(v[u]), sc, -bb[u]);
-                mh[u & 3] = fmaf(dv, dv, mh[u & 3]);
+                for (int z = 0; z < 16; z += 2) {
+                  const float d0 = fmaf(__uint_as_float(v[16 * w + z]), sc[u0 + w], -bb[16 * w + z]);
+                  const float d1 =
+                      fmaf(__uint_as_float(v[16 * w + z + 1]), sc[u0 + w], -bb[16 * w + z + 1]);
+                  s0 = fmaf(d0, d0, s0);
+                  s1 = fmaf(d1, d1, s1);
+                }
+                mp[tt][u0 + w] += s0 + s1;
               }
             }
-            const float maha = (mh[0] + mh[1]) + (mh[2] + mh[3]);
-            const float ll2 = fmaf(-kHalfLog2E, maha, kc.x);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&ctl->aempty[acc]);
+          }
+        }
+        if (!ok) break;
+#pragma unroll
+        for (int tt = 0; tt < 2; ++tt) {
+          if (tt >= nt) break;
+          const int64_t n = tile_of(q, tt) * kP1Rows + row;
+          const bool live = n < p.N;
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int k = g * kCG + h + 4 * u;
+            if (k >= p.K) break;
+            const float ll2 = fmaf(-kHalfLog2E, mp[tt][u], kgrp[h + 4 * u].x);
             if (ll2 > m[tt]) {
               l[tt] = fmaf(l[tt], ex2(m[tt] - ll2), 1.0f);
               m[tt] = ll2;
@@ -473,9 +509,6 @@ __global__ void __launch_bounds__(kP1Threads, 1) full_ll_kernel(const P1Params p
             }
             if (live) p.ll2[(size_t)k * p.ld_ll + n] = ll2;
           }
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&ctl->aempty[acc]);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&ctl->bempty[bs]);
@@ -828,16 +861,15 @@ __global__ void full_reduce_kernel(const float* __restrict__ part, int slabs, in
 }
 
 struct FullPlan {
-  int Dp, G, num_groups, Kpad, num_tiles, nf, nfb, ncb, slabs;
+  int Dp, num_groups, Kpad, num_tiles, nf, nfb, ncb, slabs;
   int64_t Npad, rows_per_slab;
 };
 
 FullPlan plan_full(int64_t N, int K, int D) {
   FullPlan pl;
   pl.Dp = (D + 15) / 16 * 16;
-  pl.G = 256 / pl.Dp;
-  pl.num_groups = (K + pl.G - 1) / pl.G;
-  pl.Kpad = pl.num_groups * pl.G;
+  pl.num_groups = (K + kCG - 1) / kCG;
+  pl.Kpad = pl.num_groups * kCG;
   pl.num_tiles = (int)((N + kP1Rows - 1) / kP1Rows);
   pl.Npad = (int64_t)pl.num_tiles * kP1Rows;
   pl.nf = num_features(D);
@@ -878,7 +910,7 @@ FullWs carve_full(void* base, const FullPlan& pl, int D) {
   FullWs ws;
   ws.err = w.take<int>(64);
   ws.cvec = w.take<float>(kFullMaxD);
-  ws.lgroups = w.take<uint8_t>((size_t)pl.num_groups * 2 * kLGroup);
+  ws.lgroups = w.take<uint8_t>((size_t)pl.num_groups * (pl.Dp / 16) * 2 * kLGroup);
   ws.bvec = w.take<float>((size_t)pl.Kpad * pl.Dp);
   ws.kconst = w.take<float2>((size_t)pl.num_groups * 16);
   ws.xsplit = w.take<uint8_t>((size_t)pl.num_tiles * 2 * kXTile);
@@ -918,7 +950,7 @@ cudaError_t full_tc_estep(const EstepArgs& a) {
   int* amax = ws.err + 1;
   centre_kernel<<<pl.Dp, 256, 0, st>>>(a.mu, a.smk, a.smd, a.K, a.D, ws.cvec, amax);
   full_prep_kernel<<<pl.Kpad, 64, 0, st>>>(a.mu, a.smk, a.smd, a.cov, a.lpi, ws.cvec, a.K, a.D,
-                                           pl.Dp, pl.G, ws.lgroups, ws.bvec, ws.kconst);
+                                           pl.Dp, ws.lgroups, ws.bvec, ws.kconst);
   const int vec_ok = a.sxd == 1 && (reinterpret_cast<uintptr_t>(a.X) & 15) == 0 && a.sxn % 4 == 0;
   const int sblocks = (int)std::min<int64_t>((pl.Npad + 7) / 8, 16 * kSmsFull);
   full_split_kernel<<<sblocks, 256, 0, st>>>(a.X, a.sxn, a.sxd, vec_ok, a.N, a.D, pl.Npad,
@@ -933,7 +965,6 @@ cudaError_t full_tc_estep(const EstepArgs& a) {
   p1.N = a.N;
   p1.K = a.K;
   p1.Dp = pl.Dp;
-  p1.G = pl.G;
   p1.num_groups = pl.num_groups;
   p1.num_tiles = pl.num_tiles;
   p1.ld_ll = pl.Npad;
