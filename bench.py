@@ -72,7 +72,7 @@ WORKLOADS = {
     "c5": dict(kind="iso", rows=ROWS_C5, K=1024, D=128, scaling="strong",
                title="C5 streaming isotropic E-step N=100M K=1024 D=128 total",
                profile="tc_fused_iso_c2.txt", kernel="tc_fused_kernel<iso> "
-               "(fused distance/LSE/statistics, tcgen05), one 10M-row chunk"),
+               "(fused distance/LSE/statistics, tcgen05), the last row chunk of a step"),
 }
 
 
@@ -436,9 +436,10 @@ def main():
     # ---- roofline of the dominant kernel
     peaks = load_peaks()
     fpp = flops_per_pair(kind, D)
-    flops_launch = fpp * chunk * K
-    # the events bracket the last dominant-kernel launch of each step (one
-    # E-step call per step, except c5: the last chunk's call)
+    # the events bracket the dominant kernels of the last E-step call of each
+    # step (one call per step, except c5: the call on the last row chunk)
+    last_rows = n_local - ((n_local - 1) // chunk) * chunk
+    flops_launch = fpp * last_rows * K
     kern_launch_ms = kern_avg
     achieved = flops_launch / (kern_launch_ms * 1e-3) / 1e12
     traffic = profile_traffic(w["profile"])
@@ -447,7 +448,7 @@ def main():
                 "traffic": traffic, "peak_source": peaks["source"] + " bf16 burst",
                 "kernel": w["kernel"],
                 "algorithmic_flops_per_launch": flops_launch,
-                "kernel_ms_per_launch": kern_launch_ms}
+                "kernel_ms_per_launch": kern_launch_ms, "rows_per_launch": last_rows}
     # north-star roofline: max(tensor time at TF32 peak = bf16/2, exp time at MUFU peak)
     p_tf32 = peaks["bf16_tflops"] / 2
     p_mufu = 148 * 16 * 1.965e9
