@@ -407,20 +407,20 @@ def main():
             for h, r in zip(out_host, res):
                 h.copy_(r.reshape(-1), non_blocking=True)
 
-        for _ in range(2):
+        for _ in range(max(3, args.warmup)):
             e2e_step()
         torch.cuda.synchronize(dev)
         if world > 1:
             dist.barrier()
-        a = torch.cuda.Event(enable_timing=True)
-        b = torch.cuda.Event(enable_timing=True)
         n_e2e = max(3, min(args.steps, 10))
-        a.record(stream)
-        for _ in range(n_e2e):
+        e2e_ev = [torch.cuda.Event(enable_timing=True) for _ in range(n_e2e + 1)]
+        e2e_ev[0].record(stream)
+        for i in range(n_e2e):
             e2e_step()
-        b.record(stream)
+            e2e_ev[i + 1].record(stream)
         torch.cuda.synchronize(dev)
-        ms_e2e = a.elapsed_time(b) / n_e2e
+        e2e_ms_each = [e2e_ev[i].elapsed_time(e2e_ev[i + 1]) for i in range(n_e2e)]
+        ms_e2e = sum(e2e_ms_each) / n_e2e
         if world > 1:
             t = torch.tensor([ms_e2e], device=dev)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -429,6 +429,7 @@ def main():
         d2h = (n_local + K + K * D + n_sig) * 4
         e2e = {"value": pairs_step / (ms_e2e * 1e-3), "unit": UNIT, "h2d_bytes_per_step": h2d,
                "d2h_bytes_per_step": d2h, "ms_per_step": ms_e2e,
+               "ms_per_step_min_max": [min(e2e_ms_each), max(e2e_ms_each)],
                "path": f"pinned host X in {E2E_CHUNK}-row pieces -> device (copy stream, "
                        "overlapped) -> gmm_stream.stream_estep (the library E-step per piece, "
                        "statistics accumulated) -> logZ and statistics -> host"}
