@@ -412,7 +412,7 @@ def main():
         torch.cuda.synchronize(dev)
         if world > 1:
             dist.barrier()
-        n_e2e = max(3, min(args.steps, 10))
+        n_e2e = max(10, min(args.steps, 30))  # host-driven: more steps dilute a scheduling hiccup
         e2e_ev = [torch.cuda.Event(enable_timing=True) for _ in range(n_e2e + 1)]
         e2e_ev[0].record(stream)
         for i in range(n_e2e):
