@@ -12,6 +12,12 @@ which has no distributed code of its own.
 staging buffers on a copy stream, overlapped with the E-step of the previous
 chunk, and the statistics are accumulated in place (FGMM_FLAG_ACCUMULATE).
 
+``resumable_stream_estep``: the same pass over rows [0, n_rows) read by a
+callable, with its progress ``(next_row, Nk, mu_acc, sig, sum logZ)`` saved
+to a checkpoint file every few chunks, so a pass that stops (a crash, a
+pre-empted job) continues from the last checkpoint and ends with the
+statistics an uninterrupted pass would have produced, bit for bit.
+
 ``generate_rows``: rows of the streaming configuration made on the device by
 the library's counter-based generator, keyed by global row index, so every
 sharding of the same global row range sees the same data.
@@ -19,7 +25,9 @@ sharding of the same global row range sees the same data.
 
 from __future__ import annotations
 
+import dataclasses
 import math
+import os
 from typing import Callable, Iterable, Optional
 
 import torch
@@ -91,11 +99,13 @@ class ShardedEStep:
 
 def stream_estep(chunks: Iterable[torch.Tensor], mu: torch.Tensor, cov: torch.Tensor,
                  log_pi: torch.Tensor, variant: str = "iso", device=None,
-                 keep_logZ: bool = False):
+                 keep_logZ: bool = False, init=None):
     """E-step over host chunks (each (n_i, D) float32, ideally pinned).
 
     Copies chunk i+1 on a side stream while chunk i is processed; statistics
-    are accumulated on the device.  Returns (logZ or None, Nk, mu_acc, sig).
+    are accumulated on the device, starting from ``init = (Nk, mu_acc, sig)``
+    when given (a resumed pass) and from zero otherwise.  Returns
+    (logZ or None, Nk, mu_acc, sig).
     """
     device = torch.device(device or "cuda")
     K, D = mu.shape
@@ -103,6 +113,9 @@ def stream_estep(chunks: Iterable[torch.Tensor], mu: torch.Tensor, cov: torch.Te
     cov = cov.to(device)
     log_pi = log_pi.to(device)
     _, (Nk, mu_acc, sig) = packed_stats(variant, K, D, device)
+    if init is not None:
+        for dst, src in zip((Nk, mu_acc, sig), init):
+            dst.copy_(src.reshape(dst.shape))
     copy_stream = torch.cuda.Stream(device)
     compute = torch.cuda.current_stream(device)
     logZ_parts = []
@@ -131,17 +144,107 @@ def stream_estep(chunks: Iterable[torch.Tensor], mu: torch.Tensor, cov: torch.Te
         Xd = staged[cur_slot]
         logZ = torch.empty(Xd.shape[0], device=device, dtype=torch.float32)
         L.estep(VARIANTS[variant], Xd, mu, cov, log_pi, out=(logZ, Nk, mu_acc, sig),
-                accumulate=not first)
+                accumulate=init is not None or not first)
         Xd.record_stream(compute)
         first = False
         if keep_logZ:
             logZ_parts.append(logZ)
-    if first:  # no chunk at all
+    if first and init is None:  # no chunk at all
         Nk.zero_()
         mu_acc.zero_()
         sig.zero_()
     logZ = torch.cat(logZ_parts) if keep_logZ and logZ_parts else None
     return logZ, Nk, mu_acc, sig
+
+
+@dataclasses.dataclass
+class StreamState:
+    """Progress of a resumable streamed E-step: rows [0, next_row) are in the
+    statistics (host fp32 tensors) and in sum_logZ (float64 on the host)."""
+    variant: str
+    n_rows: int
+    chunk_rows: int
+    next_row: int
+    Nk: torch.Tensor
+    mu_acc: torch.Tensor
+    sig: torch.Tensor
+    sum_logZ: float = 0.0
+
+    @classmethod
+    def start(cls, variant: str, n_rows: int, chunk_rows: int, K: int, D: int) -> "StreamState":
+        shape = sig_shape(variant, K, D)
+        return cls(variant, n_rows, chunk_rows, 0, torch.zeros(K), torch.zeros(K, D),
+                   torch.zeros(shape))
+
+    @property
+    def done(self) -> bool:
+        return self.next_row >= self.n_rows
+
+    def save(self, path: str) -> None:
+        """Atomic: written to a temporary file, then renamed over ``path``."""
+        tmp = f"{path}.tmp"
+        torch.save({"variant": self.variant, "n_rows": self.n_rows,
+                    "chunk_rows": self.chunk_rows, "next_row": self.next_row,
+                    "Nk": self.Nk, "mu_acc": self.mu_acc, "sig": self.sig,
+                    "sum_logZ": self.sum_logZ}, tmp)
+        os.replace(tmp, path)
+
+    @classmethod
+    def load(cls, path: str) -> "StreamState":
+        d = torch.load(path, map_location="cpu", weights_only=True)
+        return cls(d["variant"], int(d["n_rows"]), int(d["chunk_rows"]), int(d["next_row"]),
+                   d["Nk"], d["mu_acc"], d["sig"], float(d["sum_logZ"]))
+
+
+def resumable_stream_estep(read_rows: Callable[[int, int], torch.Tensor], n_rows: int,
+                           mu: torch.Tensor, cov: torch.Tensor, log_pi: torch.Tensor,
+                           variant: str = "iso", chunk_rows: int = 1 << 20,
+                           checkpoint_path: Optional[str] = None, checkpoint_every: int = 8,
+                           state: Optional[StreamState] = None,
+                           logz_sink: Optional[Callable[[int, torch.Tensor], None]] = None,
+                           device=None, window_fn: Optional[Callable] = None) -> StreamState:
+    """Streamed E-step over rows [0, n_rows) with checkpoints (N larger than
+    device memory, README.md:81-103, plus resume).
+
+    read_rows(row0, n) returns host rows [row0, row0+n) as an (n, D) float32
+    tensor (pinned for overlap).  Rows go through ``stream_estep`` in windows
+    of ``checkpoint_every`` chunks of ``chunk_rows``; after each window the
+    statistics come back to the host and, with ``checkpoint_path``, the state
+    is saved.  ``state`` (or an existing checkpoint file) resumes a pass: the
+    chunking must be the one the state was made with.  logz_sink(row0, logZ)
+    receives each window's logZ.  ``window_fn(chunks, mu, cov, log_pi, init)``
+    replaces the device E-step (CPU tests only; default ``stream_estep``).
+    Returns the final state."""
+    K, D = mu.shape
+    if state is None and checkpoint_path is not None and os.path.exists(checkpoint_path):
+        state = StreamState.load(checkpoint_path)
+    if state is None:
+        state = StreamState.start(variant, n_rows, chunk_rows, K, D)
+    if (state.variant, state.n_rows, state.chunk_rows) != (variant, n_rows, chunk_rows):
+        raise ValueError("resume state was made for another pass: "
+                         f"{(state.variant, state.n_rows, state.chunk_rows)} != "
+                         f"{(variant, n_rows, chunk_rows)}")
+    if state.next_row % chunk_rows != 0 and state.next_row < n_rows:
+        raise ValueError("resume state is not on a chunk boundary")
+    if window_fn is None:
+        def window_fn(chunks, mu_, cov_, lpi_, init):
+            return stream_estep(chunks, mu_, cov_, lpi_, variant=variant, device=device,
+                                keep_logZ=True, init=init)
+    while not state.done:
+        row0 = state.next_row
+        starts = range(row0, min(n_rows, row0 + checkpoint_every * chunk_rows), chunk_rows)
+        chunks = [read_rows(r, min(chunk_rows, n_rows - r)) for r in starts]
+        logZ, Nk, mu_acc, sig = window_fn(chunks, mu, cov, log_pi,
+                                          (state.Nk, state.mu_acc, state.sig))
+        logZ_h = logZ.double().cpu()
+        state.Nk, state.mu_acc, state.sig = Nk.cpu(), mu_acc.cpu(), sig.cpu()
+        state.sum_logZ += float(logZ_h.sum())
+        state.next_row = min(n_rows, starts[-1] + chunk_rows)
+        if logz_sink is not None:
+            logz_sink(row0, logZ.cpu())
+        if checkpoint_path is not None:
+            state.save(checkpoint_path)
+    return state
 
 
 def mixture_centres(K: int, D: int, seed: int, device) -> torch.Tensor:
