@@ -80,20 +80,35 @@ constexpr int kSplitRows = 4;                               // rows per warp ste
 constexpr int kSms = 148;                                   // B200
 
 // Compile-time shape of one fused-kernel instantiation.
+//
+// Stage layout (one row tile, fp16 hi/lo feature words, K-major 128B swizzle):
+//   iso:  [hi chunk 0 | hi chunk 1 | ... | lo chunk 0 | ...]
+//   diag: [hi chunk 0 | lo chunk 0 | hi chunk 1 | lo chunk 1 | ...], so that the
+//         hi and lo rows of one 64-feature chunk form a single 128-row B operand:
+//         one N=128 MMA gives W_hi F_hi and W_hi F_lo side by side (an N=64 MMA
+//         costs as much as an N=128 one), W_lo F_hi is a second, N=64 MMA.
+//         W_hi then lives in shared memory (A operand of the N=128 MMA) and
+//         only W_lo in TMEM.
 template <int ROWS, bool DIAG>
 struct Cfg {
   static constexpr int kRows = ROWS;                  // rows per tile (distance MMA N)
   static constexpr bool kDiag = DIAG;
-  static constexpr int kStages = DIAG ? 4 : 3;        // F tile buffers
+  static constexpr int kStages = 3;                   // F tile buffers
   static constexpr int kMaxFeat = DIAG ? 2 * kMaxDDiag : kMaxDIso;
   static constexpr int kChunk = ROWS * 128;           // bytes of one 64-feature chunk
+  static constexpr int kFStride = DIAG ? 2 * kChunk : kChunk;  // chunk stride in a stage
   static constexpr int kRB = ROWS / 4;                // rows per epilogue warp (phase A)
+  static constexpr int kSCols = DIAG ? 2 * ROWS : ROWS;        // diag: [hh + lh | hl]
+  static constexpr int kWCols = DIAG ? kMaxFeat / 2 : kMaxFeat;  // diag: W lo only
+  static constexpr int kWSmem = DIAG ? kComps * 2 * kMaxFeat : 0;  // diag: W hi, bytes
   // TMEM column map (512 columns allocated)
   static constexpr uint32_t kColT = 0;                // statistics accumulator
   static constexpr uint32_t kColS = kMaxFeat;         // distance accumulator
-  static constexpr uint32_t kColR = kColS + ROWS;     // R^T hi (ROWS/2) + lo (ROWS/2)
-  static constexpr uint32_t kColW = kColR + ROWS;     // W hi (nfeat/2) + lo (nfeat/2)
-  static_assert(kColW + kMaxFeat <= 512, "TMEM budget");
+  static constexpr uint32_t kColR = kColS + kSCols;   // R^T hi (ROWS/2) + lo (ROWS/2)
+  static constexpr uint32_t kColW = kColR + ROWS;     // iso: W hi + lo; diag: W lo
+  static_assert(kColW + kWCols <= 512, "TMEM budget");
+  // byte offset of the lo half of a stage
+  __host__ __device__ static constexpr int lo_offset(int nch) { return DIAG ? kChunk : nch * kChunk; }
   static_assert(kStages <= kMaxStages, "stage count");
   static_assert(kRB == 16 || kRB == 32, "epilogue row block");
   static constexpr int kGroups = ROWS == 128 ? 4 : 1;  // independent epilogue row groups
@@ -272,8 +287,9 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fused_kernel(const TcParams p)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   const int stage_bytes = 2 * p.nch * G::kChunk;    // hi + lo
-  uint8_t* xs = smem;                                // [NS][hi | lo]
-  float* xsq = reinterpret_cast<float*>(smem + NS * stage_bytes);  // iso: [NS][R]
+  uint8_t* xs = smem;                                // [NS][stage]
+  uint8_t* whs = smem + NS * stage_bytes;            // diag: W hi, 16 KB per 64 features
+  float* xsq = reinterpret_cast<float*>(whs + G::kWSmem);  // iso: [NS][R]
   float* red_m = xsq + NS * R;                       // [16 warps][RB]
   float* red_l = red_m + kEpiWarps * RB;             // [16 warps][RB]
   float* scale_s = red_l + kEpiWarps * RB;           // [4 quadrants][R rows]
@@ -331,21 +347,32 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fused_kernel(const TcParams p)
   const uint32_t tmem = ctl->tmem_base;
   const uint32_t wcols = (uint32_t)(p.nfeat / 2);
 
-  // W rows into TMEM (A operand of the distance GEMM): lane = component.
+  // W rows (A operand of the distance GEMM), lane = component: iso hi and lo
+  // into TMEM; diag lo into TMEM and hi into shared memory (K-major swizzled).
   if (warp < 4) {
     const uint4* wh = reinterpret_cast<const uint4*>(p.Whi + (size_t)kg * p.nfeat);
     const uint4* wl = reinterpret_cast<const uint4*>(p.Wlo + (size_t)kg * p.nfeat);
     for (int s = 0; s < p.nfeat / 16; ++s) {
       uint32_t v[8];
-      uint4 a = wh[2 * s], b = wh[2 * s + 1];
-      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-      tmem_st8(tmem + ((uint32_t)(q * 32) << 16) + G::kColW + 8 * s, v);
+      uint4 a, b;
+      if constexpr (G::kDiag) {
+        a = wh[2 * s];
+        b = wh[2 * s + 1];
+        *reinterpret_cast<uint4*>(whs + xoff(kl, 16 * s, kComps * 128)) = a;
+        *reinterpret_cast<uint4*>(whs + xoff(kl, 16 * s + 8, kComps * 128)) = b;
+      } else {
+        a = wh[2 * s];
+        b = wh[2 * s + 1];
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+        tmem_st8(tmem + ((uint32_t)(q * 32) << 16) + G::kColW + 8 * s, v);
+      }
       a = wl[2 * s]; b = wl[2 * s + 1];
       v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-      tmem_st8(tmem + ((uint32_t)(q * 32) << 16) + G::kColW + wcols + 8 * s, v);
+      tmem_st8(tmem + ((uint32_t)(q * 32) << 16) + G::kColW + (G::kDiag ? 0u : wcols) + 8 * s, v);
     }
     tmem_wait_st();
   }
+  if constexpr (G::kDiag) fence_async_smem();  // W hi: generic stores -> tensor-core reads
   tc_fence_before();
   __syncthreads();
   cluster_sync_all();  // peers' barriers are initialised before any remote arrive
@@ -355,18 +382,20 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fused_kernel(const TcParams p)
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t id_dist = idesc_f16(R, false);
+      const uint32_t id_dist2 = idesc_f16(2 * R, false);  // diag: [F_hi; F_lo] rows
       const uint32_t id_stat = idesc_f16(64 * p.nch, true);
       const int ksd = p.nfeat / 16;
+      const uint32_t lo_off = (uint32_t)G::lo_offset(p.nch);
       bool first_stats = true;
       auto issue_stats = [&](int jj) -> void {
         const uint8_t* st = xs + (jj % NS) * stage_bytes;
-        const uint32_t xhi = smem_u32(st), xlo = smem_u32(st + p.nch * G::kChunk);
+        const uint32_t xhi = smem_u32(st), xlo = xhi + lo_off;
         // terms lo*hi, hi*lo, then hi*hi (smallest magnitudes first)
         for (int t = 0; t < 3; ++t) {
           const uint32_t acol = G::kColR + (t == 0 ? (uint32_t)(R / 2) : 0u);
           const uint32_t b = t == 1 ? xlo : xhi;
           for (int s = 0; s < R / 16; ++s) {
-            mma_ts(tmem + G::kColT, tmem + acol + 8 * s, desc_mnmajor(b + s * 2048, G::kChunk),
+            mma_ts(tmem + G::kColT, tmem + acol + 8 * s, desc_mnmajor(b + s * 2048, G::kFStride),
                    id_stat, (first_stats && t == 0 && s == 0) ? 0u : 1u);
           }
         }
@@ -380,14 +409,26 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fused_kernel(const TcParams p)
         if (j >= 1 && !mbar_wait(&ctl->s_empty, (j - 1) & 1, ctl, p.err, 2)) break;
         tc_fence_after();
         const uint8_t* st = xs + b * stage_bytes;
-        const uint32_t xhi = smem_u32(st), xlo = smem_u32(st + p.nch * G::kChunk);
-        for (int t = 0; t < 3; ++t) {
-          const uint32_t acol = G::kColW + (t == 0 ? wcols : 0u);
-          const uint32_t bb = t == 1 ? xlo : xhi;
+        const uint32_t xhi = smem_u32(st), xlo = xhi + lo_off;
+        if constexpr (G::kDiag) {
+          // per K-step: W_hi [F_hi; F_lo] (N = 2R: columns [hh | hl]), then
+          // W_lo F_hi (N = R) into the hh columns
+          const uint32_t wsm = smem_u32(whs);
           for (int s = 0; s < ksd; ++s) {
-            const uint32_t baddr = bb + (s >> 2) * G::kChunk + (s & 3) * 32;
-            mma_ts(tmem + G::kColS, tmem + acol + 8 * s, desc_kmajor(baddr), id_dist,
-                   (t == 0 && s == 0) ? 0u : 1u);
+            const uint32_t fa = xhi + (s >> 2) * G::kFStride + (s & 3) * 32;
+            const uint32_t wa = wsm + (s >> 2) * (kComps * 128) + (s & 3) * 32;
+            mma_ss(tmem + G::kColS, desc_kmajor(wa), desc_kmajor(fa), id_dist2, s == 0 ? 0u : 1u);
+            mma_ts(tmem + G::kColS, tmem + G::kColW + 8 * s, desc_kmajor(fa), id_dist, 1u);
+          }
+        } else {
+          for (int t = 0; t < 3; ++t) {
+            const uint32_t acol = G::kColW + (t == 0 ? wcols : 0u);
+            const uint32_t bb = t == 1 ? xlo : xhi;
+            for (int s = 0; s < ksd; ++s) {
+              const uint32_t baddr = bb + (s >> 2) * G::kChunk + (s & 3) * 32;
+              mma_ts(tmem + G::kColS, tmem + acol + 8 * s, desc_kmajor(baddr), id_dist,
+                     (t == 0 && s == 0) ? 0u : 1u);
+            }
           }
         }
         tc_commit(&ctl->s_full);
@@ -463,9 +504,21 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fused_kernel(const TcParams p)
       float ll[RB], pv[RB];
       {
         uint32_t sv[RB];
-        if constexpr (RB == 32) tmem_ld32(tmem + lane_base + G::kColS + RB * cb, sv);
-        else tmem_ld16(tmem + lane_base + G::kColS + RB * cb, sv);
-        tmem_wait_ld();
+        if constexpr (RB == 32) {
+          tmem_ld32(tmem + lane_base + G::kColS + RB * cb, sv);
+          tmem_wait_ld();
+        } else if constexpr (G::kDiag) {
+          uint32_t sl[RB];  // the W_hi F_lo columns
+          tmem_ld16(tmem + lane_base + G::kColS + RB * cb, sv);
+          tmem_ld16(tmem + lane_base + G::kColS + R + RB * cb, sl);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < RB; ++i)
+            sv[i] = __float_as_uint(__uint_as_float(sv[i]) + __uint_as_float(sl[i]));
+        } else {
+          tmem_ld16(tmem + lane_base + G::kColS + RB * cb, sv);
+          tmem_wait_ld();
+        }
         tc_fence_before();
         __syncwarp();
         if (MODE != 1 && lane == 0) mbar_arrive(&ctl->s_empty);
@@ -735,18 +788,21 @@ __global__ void __launch_bounds__(256) tc_split_kernel(
         if (!(mx < 65504.f)) atomicOr(err, 0x10000);  // outside fp16 range (or NaN)
         uint8_t* tile = xsplit + (row / ROWS) * stage_bytes;
         const int r = (int)(row % ROWS);
+        // iso: [hi chunks | lo chunks]; diag: [hi | lo] per chunk (see Cfg)
+        constexpr int kFS = DIAG ? 2 * kChunk : kChunk;
+        const int64_t lo = DIAG ? kChunk : (int64_t)nch * kChunk;
         uint32_t h0, l0, h1, l1;
         split2(xs.x, xs.y, h0, l0);
         split2(xs.z, xs.w, h1, l1);
-        const uint32_t off = xoff(r, DIAG ? Dp + f : f, kChunk);
+        const uint32_t off = xoff(r, DIAG ? Dp + f : f, kFS);
         *reinterpret_cast<uint2*>(tile + off) = make_uint2(h0, h1);
-        *reinterpret_cast<uint2*>(tile + nch * kChunk + off) = make_uint2(l0, l1);
+        *reinterpret_cast<uint2*>(tile + lo + off) = make_uint2(l0, l1);
         if (DIAG) {
           split2(xs.x * xs.x, xs.y * xs.y, h0, l0);
           split2(xs.z * xs.z, xs.w * xs.w, h1, l1);
-          const uint32_t off2 = xoff(r, f, kChunk);
+          const uint32_t off2 = xoff(r, f, kFS);
           *reinterpret_cast<uint2*>(tile + off2) = make_uint2(h0, h1);
-          *reinterpret_cast<uint2*>(tile + nch * kChunk + off2) = make_uint2(l0, l1);
+          *reinterpret_cast<uint2*>(tile + lo + off2) = make_uint2(l0, l1);
         }
       }
       if (!DIAG) {
@@ -873,7 +929,7 @@ struct TcPlan {
 
 template <class G>
 size_t tc_smem_bytes(int nch) {
-  return 1024 + (size_t)G::kStages * 2 * nch * G::kChunk +
+  return 1024 + (size_t)G::kStages * 2 * nch * G::kChunk + (size_t)G::kWSmem +
          ((size_t)G::kStages * G::kRows + 2 * kEpiWarps * G::kRB + 4 * G::kRows + 8 * kComps) * 4 +
          (size_t)2 * kMaxCluster * G::kRows * 8 + (size_t)G::kStages * G::kRows * 4 +
          sizeof(SmemCtl) + 64;

@@ -154,3 +154,32 @@ def test_tc_more_than_1024_components(kind, N, K, D, offset):
     again = _np(L.estep(v, Xd, mud, covd, lpid))
     for a, b in zip(tc, again):
         np.testing.assert_array_equal(a, b)
+
+
+@pytest.mark.parametrize("kind", ["iso", "diag"])
+def test_tc_more_than_1024_components_edge_cases(kind):
+    """K > 1024: -inf log-weights in several blocks (their Nk stays 0), a
+    ragged last block, a transposed X, a single row, and the accumulate flag
+    adding a second call's statistics."""
+    N, K, D = 2500, 2100, 40
+    X, mu, cov, lpi = _many_components(kind, N, K, D, 0.0)
+    dead = [3, 1030, 2099]
+    lpi[dead] = -math.inf
+    v = L.FGMM_VARIANT_ISO if kind == "iso" else L.FGMM_VARIANT_DIAG
+    oracle = O.estep_iso if kind == "iso" else O.estep_diag
+    ref = oracle(X.numpy(), mu.numpy(), cov.numpy(), lpi.numpy())
+    Xt = X.t().contiguous().to(DEV).t()
+    mud, covd, lpid = mu.to(DEV), cov.to(DEV), lpi.to(DEV)
+    out = _np(L.estep(v, Xt, mud, covd, lpid))
+    assert_parity(out, ref, what=f"{kind} K={K} -inf weights, transposed X")
+    assert all(out[1][k] == 0.0 for k in dead)
+
+    one = _np(L.estep(v, Xt[:1], mud, covd, lpid))
+    assert_parity(one, oracle(X[:1].numpy(), mu.numpy(), cov.numpy(), lpi.numpy()),
+                  what=f"{kind} K={K} one row")
+
+    first = L.estep(v, Xt[:1200], mud, covd, lpid)
+    second = (torch.empty(N - 1200, device=DEV),) + tuple(t.clone() for t in first[1:])
+    L.estep(v, Xt[1200:], mud, covd, lpid, out=second, accumulate=True)
+    acc = (np.concatenate([_np(first)[0], _np(second)[0]]),) + _np(second)[1:]
+    assert_parity(acc, ref, what=f"{kind} K={K} accumulated over two calls")
