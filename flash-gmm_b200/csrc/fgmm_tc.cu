@@ -87,8 +87,8 @@ constexpr int kSms = 148;                                   // B200
 //         hi and lo rows of one 64-feature chunk form a single 128-row B operand:
 //         one N=128 MMA gives W_hi F_hi and W_hi F_lo side by side (an N=64 MMA
 //         costs as much as an N=128 one), W_lo F_hi is a second, N=64 MMA.
-//         W_hi then lives in shared memory (A operand of the N=128 MMA) and
-//         only W_lo in TMEM.
+//         W_hi stays in TMEM (A of the N=128 MMA) and W_lo moves to shared
+//         memory (A of the N=64 MMA, whose B is half as wide).
 template <int ROWS, bool DIAG>
 struct Cfg {
   static constexpr int kRows = ROWS;                  // rows per tile (distance MMA N)
@@ -99,13 +99,13 @@ struct Cfg {
   static constexpr int kFStride = DIAG ? 2 * kChunk : kChunk;  // chunk stride in a stage
   static constexpr int kRB = ROWS / 4;                // rows per epilogue warp (phase A)
   static constexpr int kSCols = DIAG ? 2 * ROWS : ROWS;        // diag: [hh + lh | hl]
-  static constexpr int kWCols = DIAG ? kMaxFeat / 2 : kMaxFeat;  // diag: W lo only
-  static constexpr int kWSmem = DIAG ? kComps * 2 * kMaxFeat : 0;  // diag: W hi, bytes
+  static constexpr int kWCols = DIAG ? kMaxFeat / 2 : kMaxFeat;  // diag: W hi only
+  static constexpr int kWSmem = DIAG ? kComps * 2 * kMaxFeat : 0;  // diag: W lo, bytes
   // TMEM column map (512 columns allocated)
   static constexpr uint32_t kColT = 0;                // statistics accumulator
   static constexpr uint32_t kColS = kMaxFeat;         // distance accumulator
   static constexpr uint32_t kColR = kColS + kSCols;   // R^T hi (ROWS/2) + lo (ROWS/2)
-  static constexpr uint32_t kColW = kColR + ROWS;     // iso: W hi + lo; diag: W lo
+  static constexpr uint32_t kColW = kColR + ROWS;     // iso: W hi + lo; diag: W hi
   static_assert(kColW + kWCols <= 512, "TMEM budget");
   // byte offset of the lo half of a stage
   __host__ __device__ static constexpr int lo_offset(int nch) { return DIAG ? kChunk : nch * kChunk; }
@@ -288,7 +288,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fused_kernel(const TcParams p)
                                              ~uintptr_t(1023));
   const int stage_bytes = 2 * p.nch * G::kChunk;    // hi + lo
   uint8_t* xs = smem;                                // [NS][stage]
-  uint8_t* whs = smem + NS * stage_bytes;            // diag: W hi, 16 KB per 64 features
+  uint8_t* whs = smem + NS * stage_bytes;            // diag: W lo, 16 KB per 64 features
   float* xsq = reinterpret_cast<float*>(whs + G::kWSmem);  // iso: [NS][R]
   float* red_m = xsq + NS * R;                       // [16 warps][RB]
   float* red_l = red_m + kEpiWarps * RB;             // [16 warps][RB]
@@ -348,31 +348,28 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fused_kernel(const TcParams p)
   const uint32_t wcols = (uint32_t)(p.nfeat / 2);
 
   // W rows (A operand of the distance GEMM), lane = component: iso hi and lo
-  // into TMEM; diag lo into TMEM and hi into shared memory (K-major swizzled).
+  // into TMEM; diag hi into TMEM and lo into shared memory (K-major swizzled).
   if (warp < 4) {
     const uint4* wh = reinterpret_cast<const uint4*>(p.Whi + (size_t)kg * p.nfeat);
     const uint4* wl = reinterpret_cast<const uint4*>(p.Wlo + (size_t)kg * p.nfeat);
     for (int s = 0; s < p.nfeat / 16; ++s) {
       uint32_t v[8];
-      uint4 a, b;
+      uint4 a = wh[2 * s], b = wh[2 * s + 1];
+      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+      tmem_st8(tmem + ((uint32_t)(q * 32) << 16) + G::kColW + 8 * s, v);
+      a = wl[2 * s];
+      b = wl[2 * s + 1];
       if constexpr (G::kDiag) {
-        a = wh[2 * s];
-        b = wh[2 * s + 1];
         *reinterpret_cast<uint4*>(whs + xoff(kl, 16 * s, kComps * 128)) = a;
         *reinterpret_cast<uint4*>(whs + xoff(kl, 16 * s + 8, kComps * 128)) = b;
       } else {
-        a = wh[2 * s];
-        b = wh[2 * s + 1];
         v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-        tmem_st8(tmem + ((uint32_t)(q * 32) << 16) + G::kColW + 8 * s, v);
+        tmem_st8(tmem + ((uint32_t)(q * 32) << 16) + G::kColW + wcols + 8 * s, v);
       }
-      a = wl[2 * s]; b = wl[2 * s + 1];
-      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-      tmem_st8(tmem + ((uint32_t)(q * 32) << 16) + G::kColW + (G::kDiag ? 0u : wcols) + 8 * s, v);
     }
     tmem_wait_st();
   }
-  if constexpr (G::kDiag) fence_async_smem();  // W hi: generic stores -> tensor-core reads
+  if constexpr (G::kDiag) fence_async_smem();  // W lo: generic stores -> tensor-core reads
   tc_fence_before();
   __syncthreads();
   cluster_sync_all();  // peers' barriers are initialised before any remote arrive
@@ -417,8 +414,9 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fused_kernel(const TcParams p)
           for (int s = 0; s < ksd; ++s) {
             const uint32_t fa = xhi + (s >> 2) * G::kFStride + (s & 3) * 32;
             const uint32_t wa = wsm + (s >> 2) * (kComps * 128) + (s & 3) * 32;
-            mma_ss(tmem + G::kColS, desc_kmajor(wa), desc_kmajor(fa), id_dist2, s == 0 ? 0u : 1u);
-            mma_ts(tmem + G::kColS, tmem + G::kColW + 8 * s, desc_kmajor(fa), id_dist, 1u);
+            mma_ts(tmem + G::kColS, tmem + G::kColW + 8 * s, desc_kmajor(fa), id_dist2,
+                   s == 0 ? 0u : 1u);
+            mma_ss(tmem + G::kColS, desc_kmajor(wa), desc_kmajor(fa), id_dist, 1u);
           }
         } else {
           for (int t = 0; t < 3; ++t) {
