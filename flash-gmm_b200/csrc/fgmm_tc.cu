@@ -66,7 +66,8 @@ namespace fgmm {
 namespace {
 
 constexpr int kComps = 128;          // components per CTA (TMEM lanes, MMA M)
-constexpr int kMaxDIso = 128;        // largest D of the isotropic tensor-core path
+constexpr int kMaxDIso = 128;        // largest D of the 128-row isotropic kernel
+constexpr int kMaxDIsoWide = 256;    // largest D of the isotropic tensor-core path
 constexpr int kMaxDDiag = 96;        // largest D of the diagonal tensor-core path
 constexpr int kEpiWarps = 16;
 constexpr int kLoadWarp = kEpiWarps;                        // 16
@@ -89,32 +90,55 @@ constexpr int kSms = 148;                                   // B200
 //         costs as much as an N=128 one), W_lo F_hi is a second, N=64 MMA.
 //         W_hi stays in TMEM (A of the N=128 MMA) and W_lo moves to shared
 //         memory (A of the N=64 MMA, whose B is half as wide).
-template <int ROWS, bool DIAG>
+//
+// The wide isotropic kernel (128 < D <= 256) uses 64-row tiles with the iso
+// stage layout, W_hi in TMEM and W_lo in shared memory: TMEM T 256 | S 64 |
+// R^T 64 | W_hi 128.
+template <int ROWS, bool DIAG, int MAXFEAT, int STAGES, bool WLO_SMEM, bool STACK>
 struct Cfg {
   static constexpr int kRows = ROWS;                  // rows per tile (distance MMA N)
   static constexpr bool kDiag = DIAG;
-  static constexpr int kStages = 3;                   // F tile buffers
-  static constexpr int kMaxFeat = DIAG ? 2 * kMaxDDiag : kMaxDIso;
+  static constexpr bool kStack = STACK;               // [hi | lo] rows per chunk (diag)
+  static constexpr bool kWloSmem = WLO_SMEM;          // W_lo in shared memory
+  static constexpr int kStages = STAGES;              // F tile buffers
+  static constexpr int kMaxFeat = MAXFEAT;
+  static constexpr int kMaxD = DIAG ? MAXFEAT / 2 : MAXFEAT;
   static constexpr int kChunk = ROWS * 128;           // bytes of one 64-feature chunk
-  static constexpr int kFStride = DIAG ? 2 * kChunk : kChunk;  // chunk stride in a stage
+  static constexpr int kFStride = STACK ? 2 * kChunk : kChunk;  // chunk stride in a stage
   static constexpr int kRB = ROWS / 4;                // rows per epilogue warp (phase A)
-  static constexpr int kSCols = DIAG ? 2 * ROWS : ROWS;        // diag: [hh + lh | hl]
-  static constexpr int kWCols = DIAG ? kMaxFeat / 2 : kMaxFeat;  // diag: W hi only
-  static constexpr int kWSmem = DIAG ? kComps * 2 * kMaxFeat : 0;  // diag: W lo, bytes
+  static constexpr int kSCols = STACK ? 2 * ROWS : ROWS;        // stacked: [hh + lh | hl]
+  static constexpr int kWCols = WLO_SMEM ? kMaxFeat / 2 : kMaxFeat;  // W hi (+ lo)
+  static constexpr int kWSmem = WLO_SMEM ? kComps * 2 * kMaxFeat : 0;  // W lo, bytes
+  static constexpr int kNV = (kMaxD + 127) / 128;     // float4 of x per lane (split pass)
+  // Distance passes per tile: the wide kernel evaluates S over features
+  // [0, 128) and [128, nfeat) separately and adds the halves in fp32
+  // registers, so no accumulator chain runs over more than 8 K-steps.
+  static constexpr int kHalves = (!STACK && MAXFEAT > 128) ? 2 : 1;
   // TMEM column map (512 columns allocated)
   static constexpr uint32_t kColT = 0;                // statistics accumulator
   static constexpr uint32_t kColS = kMaxFeat;         // distance accumulator
   static constexpr uint32_t kColR = kColS + kSCols;   // R^T hi (ROWS/2) + lo (ROWS/2)
-  static constexpr uint32_t kColW = kColR + ROWS;     // iso: W hi + lo; diag: W hi
+  static constexpr uint32_t kColW = kColR + ROWS;     // W hi (+ W lo when in TMEM)
   static_assert(kColW + kWCols <= 512, "TMEM budget");
   // byte offset of the lo half of a stage
-  __host__ __device__ static constexpr int lo_offset(int nch) { return DIAG ? kChunk : nch * kChunk; }
+  __host__ __device__ static constexpr int lo_offset(int nch) {
+    return STACK ? kChunk : nch * kChunk;
+  }
   static_assert(kStages <= kMaxStages, "stage count");
   static_assert(kRB == 16 || kRB == 32, "epilogue row block");
   static constexpr int kGroups = ROWS == 128 ? 4 : 1;  // independent epilogue row groups
 };
-using IsoCfg = Cfg<128, false>;
-using DiagCfg = Cfg<64, true>;
+using IsoCfg = Cfg<128, false, kMaxDIso, 3, false, false>;
+using DiagCfg = Cfg<64, true, 2 * kMaxDDiag, 3, true, true>;
+using WideCfg = Cfg<64, false, kMaxDIsoWide, 2, true, false>;
+enum CfgId { kCfgIso = 0, kCfgDiag = 1, kCfgWide = 2 };
+// Calls f with a value of the configuration type (an empty struct).
+template <class F>
+decltype(auto) with_cfg(int id, F&& f) {
+  if (id == kCfgDiag) return f(DiagCfg{});
+  if (id == kCfgWide) return f(WideCfg{});
+  return f(IsoCfg{});
+}
 
 struct TcParams {
   const uint8_t* xsplit;     // [num_tiles][stage bytes] swizzled fp16 hi/lo features
@@ -164,7 +188,10 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, SmemCtl*
 // Components >= K get W = 0, ish = 0, c0' = c0 = -1e30 so they carry zero
 // responsibility; -inf log-weights are clamped to the same finite floor.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(128) tc_prep_kernel(
+// Threads of the isotropic prep block: one per padded feature, 4 or 8 warps.
+inline int prep_threads(int Dp) { return Dp > 128 ? 256 : 128; }
+
+__global__ void __launch_bounds__(256) tc_prep_kernel(
     const float* __restrict__ mu, int64_t smk, int64_t smd, const float* __restrict__ lss,
     const float* __restrict__ lpi, const float* __restrict__ cvec, int K, int D, int Dp,
     __half* __restrict__ Whi, __half* __restrict__ Wlo, float4* __restrict__ consts) {
@@ -176,12 +203,13 @@ __global__ void __launch_bounds__(128) tc_prep_kernel(
     ish = 0.5 * exp(-l) * kLog2E;
     c0 = ((double)lpi[k] - 0.5 * D * (kLog2Pi + l)) * kLog2E;
   }
-  const int d = threadIdx.x;  // Dp <= 128
+  const int d = threadIdx.x;  // Dp <= blockDim.x
+  const int nw = blockDim.x >> 5;
   double m = 0.0;
   if (valid && d < D) m = (double)mu[(int64_t)k * smk + (int64_t)d * smd] - (double)cvec[d];
   const float w = (float)(2.0 * ish * m);
-  __shared__ double s_sq[4];
-  __shared__ float s_wmax[4];
+  __shared__ double s_sq[8];
+  __shared__ float s_wmax[8];
   double sq = m * m;
   float wmax = fabsf(w);
   for (int o = 16; o > 0; o >>= 1) {
@@ -193,8 +221,12 @@ __global__ void __launch_bounds__(128) tc_prep_kernel(
     s_wmax[threadIdx.x >> 5] = wmax;
   }
   __syncthreads();
-  const double musq = s_sq[0] + s_sq[1] + s_sq[2] + s_sq[3];
-  const float wm = fmaxf(fmaxf(s_wmax[0], s_wmax[1]), fmaxf(s_wmax[2], s_wmax[3]));
+  double musq = 0.0;
+  float wm = 0.f;
+  for (int i = 0; i < nw; ++i) {
+    musq += s_sq[i];
+    wm = fmaxf(wm, s_wmax[i]);
+  }
   const int sk = scale_exp(wm);
   if (d < Dp) {
     const float ws = ldexpf(w, -sk);
@@ -359,7 +391,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fused_kernel(const TcParams p)
       tmem_st8(tmem + ((uint32_t)(q * 32) << 16) + G::kColW + 8 * s, v);
       a = wl[2 * s];
       b = wl[2 * s + 1];
-      if constexpr (G::kDiag) {
+      if constexpr (G::kWloSmem) {
         *reinterpret_cast<uint4*>(whs + xoff(kl, 16 * s, kComps * 128)) = a;
         *reinterpret_cast<uint4*>(whs + xoff(kl, 16 * s + 8, kComps * 128)) = b;
       } else {
@@ -369,7 +401,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fused_kernel(const TcParams p)
     }
     tmem_wait_st();
   }
-  if constexpr (G::kDiag) fence_async_smem();  // W lo: generic stores -> tensor-core reads
+  if constexpr (G::kWloSmem) fence_async_smem();  // W lo: generic stores -> tensor-core reads
   tc_fence_before();
   __syncthreads();
   cluster_sync_all();  // peers' barriers are initialised before any remote arrive
@@ -400,14 +432,16 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fused_kernel(const TcParams p)
         tc_commit(&ctl->r_empty);
         tc_commit(&ctl->xempty[jj % NS]);
       };
-      for (int j = 0; j < ntiles; ++j) {
+      constexpr int H = G::kHalves;
+      bool ok = true;
+      for (int j = 0; j < ntiles && ok; ++j) {
         const int b = j % NS;
         if (!mbar_wait(&ctl->xfull[b], (j / NS) & 1, ctl, p.err, 1)) break;
-        if (j >= 1 && !mbar_wait(&ctl->s_empty, (j - 1) & 1, ctl, p.err, 2)) break;
-        tc_fence_after();
         const uint8_t* st = xs + b * stage_bytes;
         const uint32_t xhi = smem_u32(st), xlo = xhi + lo_off;
-        if constexpr (G::kDiag) {
+        if constexpr (G::kStack) {
+          if (j >= 1 && !mbar_wait(&ctl->s_empty, (j - 1) & 1, ctl, p.err, 2)) break;
+          tc_fence_after();
           // per K-step: W_hi [F_hi; F_lo] (N = 2R: columns [hh | hl]), then
           // W_lo F_hi (N = R) into the hh columns
           const uint32_t wsm = smem_u32(whs);
@@ -418,22 +452,44 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fused_kernel(const TcParams p)
                    s == 0 ? 0u : 1u);
             mma_ss(tmem + G::kColS, desc_kmajor(wa), desc_kmajor(fa), id_dist, 1u);
           }
+          tc_commit(&ctl->s_full);
         } else {
-          for (int t = 0; t < 3; ++t) {
-            const uint32_t acol = G::kColW + (t == 0 ? wcols : 0u);
-            const uint32_t bb = t == 1 ? xlo : xhi;
-            for (int s = 0; s < ksd; ++s) {
-              const uint32_t baddr = bb + (s >> 2) * G::kChunk + (s & 3) * 32;
-              mma_ts(tmem + G::kColS, tmem + acol + 8 * s, desc_kmajor(baddr), id_dist,
-                     (t == 0 && s == 0) ? 0u : 1u);
+          // terms W_lo x_hi, W_hi x_lo, W_hi x_hi (smallest magnitudes first),
+          // per pass h over K-steps [8h, 8h + 8); W_lo from shared memory in
+          // the wide kernel.  Pass (j, h) is s_full / s_empty phase j H + h.
+          const uint32_t wsm = smem_u32(whs);
+          for (int h = 0; h < H; ++h) {
+            const int ph = j * H + h;
+            if (ph >= 1 && !mbar_wait(&ctl->s_empty, (ph - 1) & 1, ctl, p.err, 2)) {
+              ok = false;
+              break;
             }
+            tc_fence_after();
+            const int s0 = H == 1 ? 0 : 8 * h;
+            const int s1 = H == 1 ? ksd : (ksd < 8 * h + 8 ? ksd : 8 * h + 8);
+            for (int t = 0; t < 3; ++t) {
+              const uint32_t acol = G::kColW + (t == 0 ? wcols : 0u);
+              const uint32_t bb = t == 1 ? xlo : xhi;
+              for (int s = s0; s < s1; ++s) {
+                const uint32_t baddr = bb + (s >> 2) * G::kChunk + (s & 3) * 32;
+                const uint32_t acc = (t == 0 && s == s0) ? 0u : 1u;
+                if (G::kWloSmem && t == 0)
+                  mma_ss(tmem + G::kColS,
+                         desc_kmajor(wsm + (s >> 2) * (kComps * 128) + (s & 3) * 32),
+                         desc_kmajor(baddr), id_dist, acc);
+                else
+                  mma_ts(tmem + G::kColS, tmem + acol + 8 * s, desc_kmajor(baddr), id_dist,
+                         acc);
+              }
+            }
+            tc_commit(&ctl->s_full);
           }
+          if (!ok) break;
         }
-        tc_commit(&ctl->s_full);
         if (MODE == 1) {
           // LSE only: the stage is free once the epilogue has read this
-          // tile's distances and |x|^2 words (its s_empty arrival)
-          if (!mbar_wait(&ctl->s_empty, j & 1, ctl, p.err, 2)) break;
+          // tile's distances and |x|^2 words (its last s_empty arrival)
+          if (!mbar_wait(&ctl->s_empty, (j * H + H - 1) & 1, ctl, p.err, 2)) break;
           mbar_arrive(&ctl->xempty[b]);
           continue;
         }
@@ -496,16 +552,32 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fused_kernel(const TcParams p)
       const int b = t % NS;
       const int64_t row0 = (int64_t)(cluster_id + (int64_t)t * num_clusters) * R;
       // ---- A
-      if (!mbar_wait(&ctl->s_full, t & 1, ctl, p.err, 16)) break;
+      constexpr int H = G::kHalves;
+      if (!mbar_wait(&ctl->s_full, (t * H) & 1, ctl, p.err, 16)) break;
       if (!mbar_wait(&ctl->xfull[b], (t / NS) & 1, ctl, p.err, 4096)) break;
       tc_fence_after();
       float ll[RB], pv[RB];
       {
         uint32_t sv[RB];
-        if constexpr (RB == 32) {
+        if constexpr (H == 2) {
+          // first distance pass into registers, then the second one added
+          tmem_ld16(tmem + lane_base + G::kColS + RB * cb, sv);
+          tmem_wait_ld();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&ctl->s_empty);
+          if (!mbar_wait(&ctl->s_full, (t * H + 1) & 1, ctl, p.err, 16)) break;
+          tc_fence_after();
+          uint32_t s2[RB];
+          tmem_ld16(tmem + lane_base + G::kColS + RB * cb, s2);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < RB; ++i)
+            sv[i] = __float_as_uint(__uint_as_float(sv[i]) + __uint_as_float(s2[i]));
+        } else if constexpr (RB == 32) {
           tmem_ld32(tmem + lane_base + G::kColS + RB * cb, sv);
           tmem_wait_ld();
-        } else if constexpr (G::kDiag) {
+        } else if constexpr (G::kStack) {
           uint32_t sl[RB];  // the W_hi F_lo columns
           tmem_ld16(tmem + lane_base + G::kColS + RB * cb, sv);
           tmem_ld16(tmem + lane_base + G::kColS + R + RB * cb, sl);
@@ -730,40 +802,51 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fused_kernel(const TcParams p)
 //   iso:  features (x-c) 2^-a, plus |x-c|^2 per row;
 //   diag: features [((x-c) 2^-a)^2 | (x-c) 2^-a].
 // ---------------------------------------------------------------------------
-template <int ROWS, bool DIAG>
+template <class G>
 __global__ void __launch_bounds__(256) tc_split_kernel(
     const float* __restrict__ X, int64_t sxn, int64_t sxd, int vec_ok, int64_t N, int D, int Dp,
     int nch, int64_t rows_pad, const int* __restrict__ amax, const float* __restrict__ cvec,
     uint8_t* __restrict__ xsplit, float* __restrict__ xsq, int* __restrict__ err) {
+  constexpr int ROWS = G::kRows, NV = G::kNV;
+  constexpr bool DIAG = G::kDiag;
   constexpr int kChunk = ROWS * 128;
+  // stage layout: [hi chunks | lo chunks], or [hi | lo] per chunk when stacked
+  constexpr int kFS = G::kFStride;
+  const int64_t lo = G::lo_offset(nch);
   const int lane = threadIdx.x & 31;
   const int a = x_scale_exp<DIAG>(__int_as_float(*amax));
   const int64_t stage_bytes = (int64_t)2 * nch * kChunk;
-  const int nact = Dp / 4;
-  const int f = 4 * lane;
-  float4 cc = make_float4(0.f, 0.f, 0.f, 0.f);
-  if (lane < nact) cc = *reinterpret_cast<const float4*>(cvec + f);
+  float4 cc[NV];
+#pragma unroll
+  for (int v = 0; v < NV; ++v) {
+    const int f = 128 * v + 4 * lane;
+    cc[v] = f < Dp ? *reinterpret_cast<const float4*>(cvec + f) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
   // Each warp takes kSplitRows consecutive rows per step and issues all of
   // their loads before converting, to keep enough bytes in flight for HBM.
   for (int64_t row0 = ((int64_t)blockIdx.x * 8 + (threadIdx.x >> 5)) * kSplitRows; row0 < rows_pad;
        row0 += (int64_t)gridDim.x * 8 * kSplitRows) {
-    float4 xr[kSplitRows];
+    float4 xr[kSplitRows][NV];
 #pragma unroll
     for (int u = 0; u < kSplitRows; ++u) {
       const int64_t row = row0 + u;
-      float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (lane < nact && row < N) {
-        const float* src = X + row * sxn;
-        if (vec_ok && f + 3 < D) {
-          x = __ldg(reinterpret_cast<const float4*>(src + f));
-        } else {
-          if (f + 0 < D) x.x = __ldg(src + (int64_t)(f + 0) * sxd);
-          if (f + 1 < D) x.y = __ldg(src + (int64_t)(f + 1) * sxd);
-          if (f + 2 < D) x.z = __ldg(src + (int64_t)(f + 2) * sxd);
-          if (f + 3 < D) x.w = __ldg(src + (int64_t)(f + 3) * sxd);
+#pragma unroll
+      for (int v = 0; v < NV; ++v) {
+        const int f = 128 * v + 4 * lane;
+        float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (f < Dp && row < N) {
+          const float* src = X + row * sxn;
+          if (vec_ok && f + 3 < D) {
+            x = __ldg(reinterpret_cast<const float4*>(src + f));
+          } else {
+            if (f + 0 < D) x.x = __ldg(src + (int64_t)(f + 0) * sxd);
+            if (f + 1 < D) x.y = __ldg(src + (int64_t)(f + 1) * sxd);
+            if (f + 2 < D) x.z = __ldg(src + (int64_t)(f + 2) * sxd);
+            if (f + 3 < D) x.w = __ldg(src + (int64_t)(f + 3) * sxd);
+          }
         }
+        xr[u][v] = x;
       }
-      xr[u] = x;
     }
     // all loads issued: centre and convert (padding features have x = c = 0;
     // rows past N stay 0)
@@ -771,43 +854,47 @@ __global__ void __launch_bounds__(256) tc_split_kernel(
     for (int u = 0; u < kSplitRows; ++u) {
       const int64_t row = row0 + u;
       if (row >= rows_pad) break;
-      float4 x = xr[u];
-      if (row < N) {
-        x.x -= cc.x;
-        x.y -= cc.y;
-        x.z -= cc.z;
-        x.w -= cc.w;
-      }
-      if (lane < nact) {
-        const float4 xs = make_float4(ldexpf(x.x, -a), ldexpf(x.y, -a), ldexpf(x.z, -a),
-                                      ldexpf(x.w, -a));
-        float mx = fmaxf(fmaxf(fabsf(xs.x), fabsf(xs.y)), fmaxf(fabsf(xs.z), fabsf(xs.w)));
-        if (DIAG) mx = fmaxf(mx, mx * mx);
-        if (!(mx < 65504.f)) atomicOr(err, 0x10000);  // outside fp16 range (or NaN)
-        uint8_t* tile = xsplit + (row / ROWS) * stage_bytes;
-        const int r = (int)(row % ROWS);
-        // iso: [hi chunks | lo chunks]; diag: [hi | lo] per chunk (see Cfg)
-        constexpr int kFS = DIAG ? 2 * kChunk : kChunk;
-        const int64_t lo = DIAG ? kChunk : (int64_t)nch * kChunk;
-        uint32_t h0, l0, h1, l1;
-        split2(xs.x, xs.y, h0, l0);
-        split2(xs.z, xs.w, h1, l1);
-        const uint32_t off = xoff(r, DIAG ? Dp + f : f, kFS);
-        *reinterpret_cast<uint2*>(tile + off) = make_uint2(h0, h1);
-        *reinterpret_cast<uint2*>(tile + lo + off) = make_uint2(l0, l1);
-        if (DIAG) {
-          split2(xs.x * xs.x, xs.y * xs.y, h0, l0);
-          split2(xs.z * xs.z, xs.w * xs.w, h1, l1);
-          const uint32_t off2 = xoff(r, f, kFS);
-          *reinterpret_cast<uint2*>(tile + off2) = make_uint2(h0, h1);
-          *reinterpret_cast<uint2*>(tile + lo + off2) = make_uint2(l0, l1);
+      uint8_t* tile = xsplit + (row / ROWS) * stage_bytes;
+      const int r = (int)(row % ROWS);
+      float sq = 0.f;
+#pragma unroll
+      for (int v = 0; v < NV; ++v) {
+        const int f = 128 * v + 4 * lane;
+        float4 x = xr[u][v];
+        if (row < N) {
+          x.x -= cc[v].x;
+          x.y -= cc[v].y;
+          x.z -= cc[v].z;
+          x.w -= cc[v].w;
+        }
+        if (f < Dp) {
+          const float4 xs = make_float4(ldexpf(x.x, -a), ldexpf(x.y, -a), ldexpf(x.z, -a),
+                                        ldexpf(x.w, -a));
+          float mx = fmaxf(fmaxf(fabsf(xs.x), fabsf(xs.y)), fmaxf(fabsf(xs.z), fabsf(xs.w)));
+          if (DIAG) mx = fmaxf(mx, mx * mx);
+          if (!(mx < 65504.f)) atomicOr(err, 0x10000);  // outside fp16 range (or NaN)
+          uint32_t h0, l0, h1, l1;
+          split2(xs.x, xs.y, h0, l0);
+          split2(xs.z, xs.w, h1, l1);
+          const uint32_t off = xoff(r, DIAG ? Dp + f : f, kFS);
+          *reinterpret_cast<uint2*>(tile + off) = make_uint2(h0, h1);
+          *reinterpret_cast<uint2*>(tile + lo + off) = make_uint2(l0, l1);
+          if (DIAG) {
+            split2(xs.x * xs.x, xs.y * xs.y, h0, l0);
+            split2(xs.z * xs.z, xs.w * xs.w, h1, l1);
+            const uint32_t off2 = xoff(r, f, kFS);
+            *reinterpret_cast<uint2*>(tile + off2) = make_uint2(h0, h1);
+            *reinterpret_cast<uint2*>(tile + lo + off2) = make_uint2(l0, l1);
+          }
+        }
+        if (!DIAG) {
+          sq = fmaf(x.x, x.x, sq);
+          sq = fmaf(x.y, x.y, sq);
+          sq = fmaf(x.z, x.z, sq);
+          sq = fmaf(x.w, x.w, sq);
         }
       }
       if (!DIAG) {
-        float sq = x.x * x.x;
-        sq = fmaf(x.y, x.y, sq);
-        sq = fmaf(x.z, x.z, sq);
-        sq = fmaf(x.w, x.w, sq);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
         if (lane == 0) xsq[row] = sq;
@@ -833,8 +920,10 @@ __global__ void __launch_bounds__(256) tc_part_presum_kernel(float* __restrict__
 
 // Isotropic: sum the per-cluster partials {Nk, sig, sum r (x-c)} in cluster
 // order; mu_acc = sum r (x-c) + c Nk.  One block per component (thread j sums
-// partial column j < D + 2 <= 256); NaN on a device error.
-__global__ void __launch_bounds__(256) tc_reduce_kernel(
+// partial column j < D + 2 <= blockDim.x); NaN on a device error.
+inline int reduce_threads(int D) { return D + 2 > 256 ? 288 : 256; }
+
+__global__ void __launch_bounds__(288) tc_reduce_kernel(
     const float* __restrict__ part, int clusters, int Kpad, int K, int D,
     const float* __restrict__ cvec, const int* __restrict__ err, float* __restrict__ Nk,
     float* __restrict__ mu_acc, float* __restrict__ sig, int accumulate) {
@@ -921,7 +1010,7 @@ __global__ void tc_lse_combine_kernel(const float* __restrict__ lse_part, int nb
 
 struct TcPlan {
   bool diag;
-  int rows, C, Kpad, Dp, nfeat, nch, num_tiles, clusters, plen;
+  int cfg, rows, C, Kpad, Dp, nfeat, nch, num_tiles, clusters, plen;
   size_t stage_bytes, smem;
 };
 
@@ -964,7 +1053,8 @@ int max_active_clusters(int C) {
 TcPlan plan_tc(int variant, int64_t N, int K, int D, bool query_device) {
   TcPlan pl;
   pl.diag = variant == kDiag;
-  pl.rows = pl.diag ? DiagCfg::kRows : IsoCfg::kRows;
+  pl.cfg = pl.diag ? kCfgDiag : (D > kMaxDIso ? kCfgWide : kCfgIso);
+  pl.rows = with_cfg(pl.cfg, [](auto g) { return decltype(g)::kRows; });
   // cluster size: a power of two
   pl.C = 1;
   while (pl.C * kComps < K) pl.C *= 2;
@@ -975,10 +1065,11 @@ TcPlan plan_tc(int variant, int64_t N, int K, int D, bool query_device) {
   pl.num_tiles = (int)((N + pl.rows - 1) / pl.rows);
   pl.plen = pl.diag ? 1 + 2 * D : D + 2;
   pl.stage_bytes = (size_t)2 * pl.nch * pl.rows * 128;
-  pl.smem = pl.diag ? tc_smem_bytes<DiagCfg>(pl.nch) : tc_smem_bytes<IsoCfg>(pl.nch);
+  const int nch = pl.nch, C = pl.C;
+  pl.smem = with_cfg(pl.cfg, [nch](auto g) { return tc_smem_bytes<decltype(g)>(nch); });
   int maxc = kSms / pl.C;
   if (query_device && pl.C <= kMaxCluster)
-    maxc = pl.diag ? max_active_clusters<DiagCfg>(pl.C) : max_active_clusters<IsoCfg>(pl.C);
+    maxc = with_cfg(pl.cfg, [C](auto g) { return max_active_clusters<decltype(g)>(C); });
   pl.clusters = std::max(1, std::min(maxc, pl.num_tiles));
   return pl;
 }
@@ -1110,22 +1201,20 @@ cudaError_t tc_estep_blocks(int variant, const EstepArgs& a) {
                                                         a.D, p0.Dp, m.Whi[b], m.Wlo[b],
                                                         m.consts[b]);
     else
-      tc_prep_kernel<<<m.pl[b].Kpad, 128, 0, st>>>(mub, a.smk, a.smd, a.cov + k0, a.lpi + k0,
-                                                   m.cvec, m.Kb[b], a.D, p0.Dp, m.Whi[b],
-                                                   m.Wlo[b], m.consts[b]);
+      tc_prep_kernel<<<m.pl[b].Kpad, prep_threads(p0.Dp), 0, st>>>(
+          mub, a.smk, a.smd, a.cov + k0, a.lpi + k0, m.cvec, m.Kb[b], a.D, p0.Dp, m.Whi[b],
+          m.Wlo[b], m.consts[b]);
     ++launches;
   }
   const int vec_ok = a.sxd == 1 && (reinterpret_cast<uintptr_t>(a.X) & 15) == 0 && a.sxn % 4 == 0;
   const int sblocks =
       (int)std::min<int64_t>((m.npad + 8 * kSplitRows - 1) / (8 * kSplitRows), 16 * kSms);
-  if (p0.diag)
-    tc_split_kernel<DiagCfg::kRows, true><<<sblocks, 256, 0, st>>>(
-        a.X, a.sxn, a.sxd, vec_ok, a.N, a.D, p0.Dp, p0.nch, m.npad, m.err + 1, m.cvec, m.xsplit,
-        nullptr, m.err);
-  else
-    tc_split_kernel<IsoCfg::kRows, false><<<sblocks, 256, 0, st>>>(
+  with_cfg(p0.cfg, [&](auto g) {
+    tc_split_kernel<decltype(g)><<<sblocks, 256, 0, st>>>(
         a.X, a.sxn, a.sxd, vec_ok, a.N, a.D, p0.Dp, p0.nch, m.npad, m.err + 1, m.cvec, m.xsplit,
         m.xsq, m.err);
+    return 0;
+  });
   ++launches;
 
   TcParams p;
@@ -1150,8 +1239,8 @@ cudaError_t tc_estep_blocks(int variant, const EstepArgs& a) {
       p.consts = m.consts[b];
       p.part = m.part[b];
       p.logZ = phase == 1 ? m.lse_part + (size_t)b * m.npad : m.lz2;  // out / in, log2 units
-      e = p0.diag ? launch_fused<DiagCfg>(m.pl[b], p, st, phase)
-                  : launch_fused<IsoCfg>(m.pl[b], p, st, phase);
+      const TcPlan& pb = m.pl[b];
+      e = with_cfg(p0.cfg, [&](auto g) { return launch_fused<decltype(g)>(pb, p, st, phase); });
       if (e != cudaSuccess) return e;
       ++launches;
     }
@@ -1173,7 +1262,7 @@ cudaError_t tc_estep_blocks(int variant, const EstepArgs& a) {
           m.part[b], m.pl[b].clusters, m.pl[b].Kpad, m.Kb[b], a.D, m.cvec, a.mu + k0 * a.smk,
           a.smk, a.smd, m.err, a.Nk + k0, a.mu_acc + k0 * a.D, a.sig + k0 * a.D, accumulate);
     } else {
-      tc_reduce_kernel<<<m.Kb[b], 256, 0, st>>>(m.part[b], m.pl[b].clusters, m.pl[b].Kpad,
+      tc_reduce_kernel<<<m.Kb[b], reduce_threads(a.D), 0, st>>>(m.part[b], m.pl[b].clusters, m.pl[b].Kpad,
                                                  m.Kb[b], a.D, m.cvec, m.err, a.Nk + k0,
                                                  a.mu_acc + k0 * a.D, a.sig + k0, accumulate);
     }
@@ -1239,7 +1328,7 @@ bool tc_supported(int variant, const EstepArgs& a, std::string* why) {
     return false;
   };
   if (variant == kIso) {
-    if (a.D > kMaxDIso) return no("D > 128");
+    if (a.D > kMaxDIsoWide) return no("D > 256");
   } else if (variant == kDiag) {
     if (a.D > kMaxDDiag) return no("D > 96");
   } else {
@@ -1313,7 +1402,7 @@ cudaError_t tc_estep(int variant, const EstepArgs& a) {
     tc_prep_diag_kernel<<<pl.Kpad, 128, 0, hi>>>(a.mu, a.smk, a.smd, a.cov, a.lpi, cvec, err + 1,
                                                  a.K, a.D, pl.Dp, Whi, Wlo, consts);
   else
-    tc_prep_kernel<<<pl.Kpad, 128, 0, hi>>>(a.mu, a.smk, a.smd, a.cov, a.lpi, cvec, a.K, a.D,
+    tc_prep_kernel<<<pl.Kpad, prep_threads(pl.Dp), 0, hi>>>(a.mu, a.smk, a.smd, a.cov, a.lpi, cvec, a.K, a.D,
                                             pl.Dp, Whi, Wlo, consts);
   launches += 2;
   const int vec_ok = a.sxd == 1 && (reinterpret_cast<uintptr_t>(a.X) & 15) == 0 && a.sxn % 4 == 0;
@@ -1330,14 +1419,13 @@ cudaError_t tc_estep(int variant, const EstepArgs& a) {
         (int)std::min<int64_t>((rows_pad + 8 * kSplitRows - 1) / (8 * kSplitRows), 16 * kSms);
     const float* Xc = a.X + row0 * a.sxn;
     uint8_t* xs_c = xsplit + (size_t)t0 * pl.stage_bytes;
-    if (pl.diag)
-      tc_split_kernel<DiagCfg::kRows, true><<<sblocks, 256, 0, lo>>>(
-          Xc, a.sxn, a.sxd, vec_ok, rows, a.D, pl.Dp, pl.nch, rows_pad, err + 1, cvec, xs_c,
-          nullptr, err);
-    else
-      tc_split_kernel<IsoCfg::kRows, false><<<sblocks, 256, 0, lo>>>(
-          Xc, a.sxn, a.sxd, vec_ok, rows, a.D, pl.Dp, pl.nch, rows_pad, err + 1, cvec, xs_c,
-          xsq + (size_t)t0 * pl.rows, err);
+    float* xsq_c = pl.diag ? nullptr : xsq + (size_t)t0 * pl.rows;
+    with_cfg(pl.cfg, [&](auto g) {
+      tc_split_kernel<decltype(g)><<<sblocks, 256, 0, lo>>>(Xc, a.sxn, a.sxd, vec_ok, rows, a.D,
+                                                            pl.Dp, pl.nch, rows_pad, err + 1,
+                                                            cvec, xs_c, xsq_c, err);
+      return 0;
+    });
     ++launches;
     if (nchunks > 1 && (e = cudaEventRecord(ss->ev[2 + c], lo)) != cudaSuccess) return e;
   }
@@ -1373,7 +1461,7 @@ cudaError_t tc_estep(int variant, const EstepArgs& a) {
     p.num_tiles = pc.num_tiles;
     p.logZ = a.logZ + row0;
     p.part = part + (size_t)part_clusters * pl.Kpad * pl.plen;
-    e = pl.diag ? launch_fused<DiagCfg>(pc, p, hi) : launch_fused<IsoCfg>(pc, p, hi);
+    e = with_cfg(pl.cfg, [&](auto g) { return launch_fused<decltype(g)>(pc, p, hi); });
     if (e != cudaSuccess) return e;
     part_clusters += pc.clusters;
     ++launches;
@@ -1403,7 +1491,7 @@ cudaError_t tc_estep(int variant, const EstepArgs& a) {
                                                    a.mu, a.smk, a.smd, err, a.Nk, a.mu_acc,
                                                    a.sig, accumulate);
   } else {
-    tc_reduce_kernel<<<a.K, 256, 0, hi>>>(part, part_clusters, pl.Kpad, a.K, a.D, cvec, err, a.Nk,
+    tc_reduce_kernel<<<a.K, reduce_threads(a.D), 0, hi>>>(part, part_clusters, pl.Kpad, a.K, a.D, cvec, err, a.Nk,
                                           a.mu_acc, a.sig, accumulate);
   }
   ++launches;
