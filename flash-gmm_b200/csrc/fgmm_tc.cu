@@ -68,7 +68,8 @@ namespace {
 constexpr int kComps = 128;          // components per CTA (TMEM lanes, MMA M)
 constexpr int kMaxDIso = 128;        // largest D of the 128-row isotropic kernel
 constexpr int kMaxDIsoWide = 256;    // largest D of the isotropic tensor-core path
-constexpr int kMaxDDiag = 96;        // largest D of the diagonal tensor-core path
+constexpr int kMaxDDiag = 96;        // largest D of the stacked diagonal kernel
+constexpr int kMaxDDiagWide = 128;   // largest D of the diagonal tensor-core path
 constexpr int kEpiWarps = 16;
 constexpr int kLoadWarp = kEpiWarps;                        // 16
 constexpr int kMmaWarp = kEpiWarps + 1;                     // 17
@@ -91,9 +92,9 @@ constexpr int kSms = 148;                                   // B200
 //         W_hi stays in TMEM (A of the N=128 MMA) and W_lo moves to shared
 //         memory (A of the N=64 MMA, whose B is half as wide).
 //
-// The wide isotropic kernel (128 < D <= 256) uses 64-row tiles with the iso
-// stage layout, W_hi in TMEM and W_lo in shared memory: TMEM T 256 | S 64 |
-// R^T 64 | W_hi 128.
+// The wide kernels (isotropic 128 < D <= 256, diagonal 96 < D <= 128: up to
+// 256 features) use 64-row tiles with the iso stage layout, W_hi in TMEM and
+// W_lo in shared memory: TMEM T 256 | S 64 | R^T 64 | W_hi 128.
 template <int ROWS, bool DIAG, int MAXFEAT, int STAGES, bool WLO_SMEM, bool STACK>
 struct Cfg {
   static constexpr int kRows = ROWS;                  // rows per tile (distance MMA N)
@@ -131,12 +132,14 @@ struct Cfg {
 using IsoCfg = Cfg<128, false, kMaxDIso, 3, false, false>;
 using DiagCfg = Cfg<64, true, 2 * kMaxDDiag, 3, true, true>;
 using WideCfg = Cfg<64, false, kMaxDIsoWide, 2, true, false>;
-enum CfgId { kCfgIso = 0, kCfgDiag = 1, kCfgWide = 2 };
+using DiagWideCfg = Cfg<64, true, 2 * kMaxDDiagWide, 2, true, false>;
+enum CfgId { kCfgIso = 0, kCfgDiag = 1, kCfgWide = 2, kCfgDiagWide = 3 };
 // Calls f with a value of the configuration type (an empty struct).
 template <class F>
 decltype(auto) with_cfg(int id, F&& f) {
   if (id == kCfgDiag) return f(DiagCfg{});
   if (id == kCfgWide) return f(WideCfg{});
+  if (id == kCfgDiagWide) return f(DiagWideCfg{});
   return f(IsoCfg{});
 }
 
@@ -1053,7 +1056,8 @@ int max_active_clusters(int C) {
 TcPlan plan_tc(int variant, int64_t N, int K, int D, bool query_device) {
   TcPlan pl;
   pl.diag = variant == kDiag;
-  pl.cfg = pl.diag ? kCfgDiag : (D > kMaxDIso ? kCfgWide : kCfgIso);
+  pl.cfg = pl.diag ? (D > kMaxDDiag ? kCfgDiagWide : kCfgDiag)
+                  : (D > kMaxDIso ? kCfgWide : kCfgIso);
   pl.rows = with_cfg(pl.cfg, [](auto g) { return decltype(g)::kRows; });
   // cluster size: a power of two
   pl.C = 1;
@@ -1330,7 +1334,7 @@ bool tc_supported(int variant, const EstepArgs& a, std::string* why) {
   if (variant == kIso) {
     if (a.D > kMaxDIsoWide) return no("D > 256");
   } else if (variant == kDiag) {
-    if (a.D > kMaxDDiag) return no("D > 96");
+    if (a.D > kMaxDDiagWide) return no("D > 128");
   } else {
     return full_tc_supported(a) ? true : no("full covariance: D > 64 or scratch too large");
   }

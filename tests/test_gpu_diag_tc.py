@@ -183,3 +183,17 @@ def test_tc_more_than_1024_components_edge_cases(kind):
     L.estep(v, Xt[1200:], mud, covd, lpid, out=second, accumulate=True)
     acc = (np.concatenate([_np(first)[0], _np(second)[0]]),) + _np(second)[1:]
     assert_parity(acc, ref, what=f"{kind} K={K} accumulated over two calls")
+
+
+@pytest.mark.parametrize("N,K,D", [(3000, 300, 100), (4000, 1024, 128), (257, 5, 112),
+                                   (2500, 1500, 120)])
+def test_tc_diag_wide_features(N, K, D):
+    """96 < D <= 128: 256 features on 64-row tiles (W_lo in shared memory,
+    two distance passes added in registers), incl. K > 1024."""
+    X, mu, lss, lpi = _case(N, K, D, seed=N + D)
+    ref = O.estep_diag(X.numpy(), mu.numpy(), lss.numpy(), lpi.numpy())
+    Xd, mud, lssd, lpid = (t.to(DEV) for t in (X, mu, lss, lpi))
+    tc = _np(flash_gmm_diag_h100.flash_gmm_estep_diag(Xd, mud, lssd, lpid))
+    gen = _np(L.estep(L.FGMM_VARIANT_DIAG, Xd, mud, lssd, lpid, force_general=True))
+    assert_parity(tc, ref, what=f"diag wide {N}x{K}x{D} vs oracle")
+    assert_parity(tc, gen, what=f"diag wide {N}x{K}x{D} vs general")
