@@ -1080,14 +1080,22 @@ TcPlan plan_tc(int variant, int64_t N, int K, int D, bool query_device) {
 
 // Large calls run in kChunks row chunks so the split pass of chunk c+1
 // (low-priority stream) overlaps the fused kernel of chunk c (high-priority
-// stream, which the fused CTAs need to get their 120 SMs first); the split
-// pass then uses the SMs the 8-CTA clusters leave free.  Smaller calls (and
-// the whole path's workspace-free entry, which stays far below the
+// stream, which the fused CTAs need to get their SMs first); the split pass
+// then uses the SMs the clusters leave free.  The chunks grow (1/8, 3/8, 1/2
+// of the tiles): only the first, short split is exposed, and each later split
+// has a longer fused kernel to hide behind on the few free SMs.  Smaller
+// calls (and the whole path's workspace-free entry, which stays far below the
 // threshold) run on the caller's stream alone.
-constexpr int kChunks = 4;
+constexpr int kChunks = 3;
 constexpr int kChunkMinTiles = 2048;
 
 int plan_chunks(const TcPlan& pl) { return pl.num_tiles >= kChunkMinTiles ? kChunks : 1; }
+// First tile of chunk c of n (c = n gives num_tiles).
+int chunk_begin(int c, int n, int num_tiles) {
+  if (n == 1) return c == 0 ? 0 : num_tiles;
+  static const int kEighths[kChunks + 1] = {0, 1, 4, 8};
+  return (int)((int64_t)num_tiles * kEighths[c] / 8);
+}
 
 struct SideStreams {
   bool ready = false;
@@ -1410,11 +1418,11 @@ cudaError_t tc_estep(int variant, const EstepArgs& a) {
                                             pl.Dp, Whi, Wlo, consts);
   launches += 2;
   const int vec_ok = a.sxd == 1 && (reinterpret_cast<uintptr_t>(a.X) & 15) == 0 && a.sxn % 4 == 0;
-  const int tiles_per_chunk = (pl.num_tiles + nchunks - 1) / nchunks;
 
   // split passes (stream lo), one per chunk of tiles [t0, t1)
   for (int c = 0; c < nchunks; ++c) {
-    const int t0 = c * tiles_per_chunk, t1 = std::min(pl.num_tiles, t0 + tiles_per_chunk);
+    const int t0 = chunk_begin(c, nchunks, pl.num_tiles);
+    const int t1 = chunk_begin(c + 1, nchunks, pl.num_tiles);
     if (t0 >= t1) break;
     const int64_t row0 = (int64_t)t0 * pl.rows;
     const int64_t rows = std::min<int64_t>(a.N, (int64_t)t1 * pl.rows) - row0;
@@ -1451,7 +1459,8 @@ cudaError_t tc_estep(int variant, const EstepArgs& a) {
   p.err = err;
   int part_clusters = 0, presummed = 0;
   for (int c = 0; c < nchunks; ++c) {
-    const int t0 = c * tiles_per_chunk, t1 = std::min(pl.num_tiles, t0 + tiles_per_chunk);
+    const int t0 = chunk_begin(c, nchunks, pl.num_tiles);
+    const int t1 = chunk_begin(c + 1, nchunks, pl.num_tiles);
     if (t0 >= t1) break;
     if (nchunks > 1 && (e = cudaStreamWaitEvent(hi, ss->ev[2 + c], 0)) != cudaSuccess) return e;
     if (c == 0) profile_mark(false, hi);  // the fused kernels of all chunks are bracketed
