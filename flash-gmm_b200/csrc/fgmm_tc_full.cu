@@ -107,7 +107,9 @@ struct P2Params {
 };
 
 struct __align__(8) P2Ctl {
-  uint64_t in_full[2], in_empty[2], zfull[2], zempty[2], tdone;
+  // x rows (consumed by the z warps) and R^T (consumed by the MMAs) have
+  // their own barriers, so the next x rows load as soon as a z chunk is built
+  uint64_t xin_full[2], xin_empty[2], rin_full[2], rin_empty[2], zfull[2], zempty[2], tdone;
   uint32_t tmem_base;
   volatile int abort_flag;
 };
@@ -631,9 +633,10 @@ __global__ void __launch_bounds__(kP2Comps) full_resp_kernel(const float* __rest
 
 // ---------------------------------------------------------------------------
 // Pass 2: T[k, f] = sum_n r_nk z_nf for one (feature block, component block,
-// row slab) per CTA.  Per 64-row chunk a loader thread bulk-copies R^T
-// (32 KB) and the x~ rows (64 x (D+1) floats); 16 warps build the z chunk;
-// one thread issues the MMAs (A = R^T, B = z, both from shared memory).
+// row slab) per CTA.  Per 64-row chunk one loader lane bulk-copies the x~
+// rows (64 x (D+1) floats) and another R^T (32 KB), each double-buffered on
+// its own barriers; 16 warps build the z chunk; one thread issues the MMAs
+// (A = R^T, B = z, both from shared memory).
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(kP2Threads, 1) full_stats_kernel(const P2Params p) {
   extern __shared__ uint8_t smem_raw[];
@@ -657,8 +660,10 @@ __global__ void __launch_bounds__(kP2Threads, 1) full_stats_kernel(const P2Param
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&ctl->in_full[i], 1);
-      mbar_init(&ctl->in_empty[i], kP2ZWarps + 1);  // z warps (x rows) + MMA commit (R^T)
+      mbar_init(&ctl->xin_full[i], 1);
+      mbar_init(&ctl->xin_empty[i], kP2ZWarps);  // z warps
+      mbar_init(&ctl->rin_full[i], 1);
+      mbar_init(&ctl->rin_empty[i], 1);          // MMA commit
       mbar_init(&ctl->zfull[i], kP2ZWarps);
       mbar_init(&ctl->zempty[i], 1);
     }
@@ -678,18 +683,24 @@ __global__ void __launch_bounds__(kP2Threads, 1) full_stats_kernel(const P2Param
   const uint32_t tmem = ctl->tmem_base;
 
   if (warp == kP2LoadWarp) {
-    if (lane == 0) {
+    // lane 0 streams the x rows, lane 1 the R^T blocks
+    if (lane < 2) {
       for (int c = 0; c < nchunks; ++c) {
         const int b = c & 1;
-        if (!mbar_wait_flag(&ctl->in_empty[b], ((c >> 1) & 1) ^ 1, abort_flag, p.err, 1)) break;
         const int64_t r0 = row_begin + (int64_t)c * kP2Rows;
         const int64_t chunk = r0 / kP2Rows;
-        mbar_arrive_expect_tx(&ctl->in_full[b], 2 * kRBlock + xs_bytes);
-        bulk_g2s(smem_u32(rst + b * 2 * kRBlock),
-                 p.rt + ((size_t)chunk * p.ncb + cbk) * (2 * kRBlock), 2 * kRBlock,
-                 &ctl->in_full[b]);
-        bulk_g2s(smem_u32(xst + b * kP2Rows * xs_stride), p.xs2 + r0 * xs_stride, xs_bytes,
-                 &ctl->in_full[b]);
+        if (lane == 0) {
+          if (!mbar_wait_flag(&ctl->xin_empty[b], ((c >> 1) & 1) ^ 1, abort_flag, p.err, 1)) break;
+          mbar_arrive_expect_tx(&ctl->xin_full[b], xs_bytes);
+          bulk_g2s(smem_u32(xst + b * kP2Rows * xs_stride), p.xs2 + r0 * xs_stride, xs_bytes,
+                   &ctl->xin_full[b]);
+        } else {
+          if (!mbar_wait_flag(&ctl->rin_empty[b], ((c >> 1) & 1) ^ 1, abort_flag, p.err, 1)) break;
+          mbar_arrive_expect_tx(&ctl->rin_full[b], 2 * kRBlock);
+          bulk_g2s(smem_u32(rst + b * 2 * kRBlock),
+                   p.rt + ((size_t)chunk * p.ncb + cbk) * (2 * kRBlock), 2 * kRBlock,
+                   &ctl->rin_full[b]);
+        }
       }
     }
     __syncwarp();
@@ -699,7 +710,7 @@ __global__ void __launch_bounds__(kP2Threads, 1) full_stats_kernel(const P2Param
       for (int c = 0; c < nchunks; ++c) {
         const int b = c & 1;
         if (!mbar_wait_flag(&ctl->zfull[b], (c >> 1) & 1, abort_flag, p.err, 2) ||
-            !mbar_wait_flag(&ctl->in_full[b], (c >> 1) & 1, abort_flag, p.err, 4))
+            !mbar_wait_flag(&ctl->rin_full[b], (c >> 1) & 1, abort_flag, p.err, 4))
           break;
         tc_fence_after();
         const uint32_t rhi = smem_u32(rst + b * 2 * kRBlock), rlo = rhi + kRBlock;
@@ -712,7 +723,7 @@ __global__ void __launch_bounds__(kP2Threads, 1) full_stats_kernel(const P2Param
                    (c == 0 && term == 0 && s == 0) ? 0u : 1u);
         }
         tc_commit(&ctl->zempty[b]);
-        tc_commit(&ctl->in_empty[b]);
+        tc_commit(&ctl->rin_empty[b]);
       }
       tc_commit(&ctl->tdone);
     }
@@ -727,7 +738,7 @@ __global__ void __launch_bounds__(kP2Threads, 1) full_stats_kernel(const P2Param
     int c = 0;
     for (; c < nchunks; ++c) {
       const int b = c & 1;
-      if (!mbar_wait_flag(&ctl->in_full[b], (c >> 1) & 1, abort_flag, p.err, 8) ||
+      if (!mbar_wait_flag(&ctl->xin_full[b], (c >> 1) & 1, abort_flag, p.err, 8) ||
           !mbar_wait_flag(&ctl->zempty[b], ((c >> 1) & 1) ^ 1, abort_flag, p.err, 16))
         break;
       const float* xsb = xst + b * kP2Rows * xs_stride;
@@ -768,7 +779,7 @@ __global__ void __launch_bounds__(kP2Threads, 1) full_stats_kernel(const P2Param
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(&ctl->zfull[b]);
-        mbar_arrive(&ctl->in_empty[b]);
+        mbar_arrive(&ctl->xin_empty[b]);
       }
     }
     // partial statistics of this CTA -> workspace: warp (quadrant q, quarter h)
