@@ -58,6 +58,8 @@
 
 #include <algorithm>
 #include <atomic>
+#include <mutex>
+#include <vector>
 
 #include "fgmm_internal.cuh"
 #include "fgmm_ptx.cuh"
@@ -74,8 +76,8 @@ constexpr int kEpiWarps = 16;
 constexpr int kLoadWarp = kEpiWarps;                        // 16
 constexpr int kMmaWarp = kEpiWarps + 1;                     // 17
 constexpr int kThreads = (kEpiWarps + 4) * 32;              // 640: 5 warpgroups
-constexpr int kMaxCluster = 8;
-constexpr int kBlockComps = kComps * kMaxCluster;          // 1024 components per cluster
+constexpr int kMaxCluster = 16;                             // non-portable size, K <= 2048
+constexpr int kBlockComps = kComps * 8;                     // components per block (K > 2048)
 constexpr int kMaxBlocks = 16;                              // K <= 16384 on the tensor cores
 constexpr int kMaxStages = 4;
 constexpr int kSplitRows = 4;                               // rows per warp step (split pass)
@@ -95,8 +97,13 @@ constexpr int kSms = 148;                                   // B200
 // The wide kernels (isotropic 128 < D <= 256, diagonal 96 < D <= 128: up to
 // 256 features) use 64-row tiles with the iso stage layout, W_hi in TMEM and
 // W_lo in shared memory: TMEM T 256 | S 64 | R^T 64 | W_hi 128.
-template <int ROWS, bool DIAG, int MAXFEAT, int STAGES, bool WLO_SMEM, bool STACK>
+//
+// CL is the largest cluster the instantiation runs with: 8 (K <= 1024, and
+// the 1024-component blocks of larger K), or 16 for one pass over
+// K <= 2048 (the exchange buffer grows; the 128-row kernel drops to 2 stages).
+template <int ROWS, bool DIAG, int MAXFEAT, int STAGES, bool WLO_SMEM, bool STACK, int CL = 8>
 struct Cfg {
+  static constexpr int kCluster = CL;
   static constexpr int kRows = ROWS;                  // rows per tile (distance MMA N)
   static constexpr bool kDiag = DIAG;
   static constexpr bool kStack = STACK;               // [hi | lo] rows per chunk (diag)
@@ -133,10 +140,21 @@ using IsoCfg = Cfg<128, false, kMaxDIso, 3, false, false>;
 using DiagCfg = Cfg<64, true, 2 * kMaxDDiag, 3, true, true>;
 using WideCfg = Cfg<64, false, kMaxDIsoWide, 2, true, false>;
 using DiagWideCfg = Cfg<64, true, 2 * kMaxDDiagWide, 2, true, false>;
+using IsoCfg16 = Cfg<128, false, kMaxDIso, 2, false, false, 16>;
+using DiagCfg16 = Cfg<64, true, 2 * kMaxDDiag, 3, true, true, 16>;
+using WideCfg16 = Cfg<64, false, kMaxDIsoWide, 2, true, false, 16>;
+using DiagWideCfg16 = Cfg<64, true, 2 * kMaxDDiagWide, 2, true, false, 16>;
 enum CfgId { kCfgIso = 0, kCfgDiag = 1, kCfgWide = 2, kCfgDiagWide = 3 };
-// Calls f with a value of the configuration type (an empty struct).
+// Calls f with a value of the configuration type (an empty struct); big:
+// the 16-CTA-cluster instantiation of the same layout.
 template <class F>
-decltype(auto) with_cfg(int id, F&& f) {
+decltype(auto) with_cfg(int id, F&& f, bool big = false) {
+  if (big) {
+    if (id == kCfgDiag) return f(DiagCfg16{});
+    if (id == kCfgWide) return f(WideCfg16{});
+    if (id == kCfgDiagWide) return f(DiagWideCfg16{});
+    return f(IsoCfg16{});
+  }
   if (id == kCfgDiag) return f(DiagCfg{});
   if (id == kCfgWide) return f(WideCfg{});
   if (id == kCfgDiagWide) return f(DiagWideCfg{});
@@ -329,8 +347,9 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fused_kernel(const TcParams p)
   float* red_l = red_m + kEpiWarps * RB;             // [16 warps][RB]
   float* scale_s = red_l + kEpiWarps * RB;           // [4 quadrants][R rows]
   float* fin = scale_s + 4 * R;                      // [8][128] end-of-kernel sums
-  float2* xchg = reinterpret_cast<float2*>(fin + 8 * kComps);  // [2][kMaxCluster][R]
-  float* lzs = reinterpret_cast<float*>(xchg + 2 * kMaxCluster * R);  // mode 2: [NS][R]
+  constexpr int CL = G::kCluster;
+  float2* xchg = reinterpret_cast<float2*>(fin + 8 * kComps);  // [2][CL][R]
+  float* lzs = reinterpret_cast<float*>(xchg + 2 * CL * R);    // mode 2: [NS][R]
   SmemCtl* ctl = reinterpret_cast<SmemCtl*>(lzs + NS * R);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -668,7 +687,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fused_kernel(const TcParams p)
       if (!mbar_wait(&ctl->e_bar[0][grp], t & 1, ctl, p.err, 256)) break;
 
       // ---- B + C: warp w < R/8 owns rows Rw = 8w + (lane & 7); lane group g
-      // handles lane quadrant g and cluster peers g and g + 4.
+      // handles lane quadrant g and cluster peers g + 4 j (j < CL / 4).
       const int slot = t & 1;
       if (row_owner) {
         const int ri = Rw % RB, blk = Rw / RB;
@@ -679,21 +698,30 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fused_kernel(const TcParams p)
         float L = ug * ex2(mg - M);
         L += __shfl_xor_sync(0xffffffffu, L, 8);
         L += __shfl_xor_sync(0xffffffffu, L, 16);
-        const uint32_t my_slot = smem_u32(&xchg[(slot * kMaxCluster + rank) * R + Rw]);
+        const uint32_t my_slot = smem_u32(&xchg[(slot * CL + rank) * R + Rw]);
         const int rg = Rw / kGroupRows;               // row group of this row (== grp)
         const uint32_t my_bar = smem_u32(&ctl->xchg_full[slot][rg]);
         if (tid_e == 32 * (rg * kGroupRows / 8))      // first owner warp of the group, lane 0
           mbar_arrive_expect_tx(&ctl->xchg_full[slot][rg], (uint32_t)(p.C * kGroupRows * 8));
-        if (g < p.C) st_async_f2(map_to_cta(my_slot, g), M, L, map_to_cta(my_bar, g));
-        if (g + 4 < p.C) st_async_f2(map_to_cta(my_slot, g + 4), M, L, map_to_cta(my_bar, g + 4));
+#pragma unroll
+        for (int j = 0; j < CL / 4; ++j)
+          if (g + 4 * j < p.C)
+            st_async_f2(map_to_cta(my_slot, g + 4 * j), M, L, map_to_cta(my_bar, g + 4 * j));
         const bool ok = mbar_wait<true>(&ctl->xchg_full[slot][rg], (t >> 1) & 1, ctl, p.err, 32);
-        float2 e0 = make_float2(-3e38f, 0.f), e1 = make_float2(-3e38f, 0.f);
-        if (g < p.C) e0 = xchg[(slot * kMaxCluster + g) * R + Rw];
-        if (g + 4 < p.C) e1 = xchg[(slot * kMaxCluster + g + 4) * R + Rw];
-        float GM = fmaxf(e0.x, e1.x);
+        float2 e[CL / 4];
+#pragma unroll
+        for (int j = 0; j < CL / 4; ++j) {
+          e[j] = make_float2(-3e38f, 0.f);
+          if (g + 4 * j < p.C) e[j] = xchg[(slot * CL + g + 4 * j) * R + Rw];
+        }
+        float GM = e[0].x;
+#pragma unroll
+        for (int j = 1; j < CL / 4; ++j) GM = fmaxf(GM, e[j].x);
         GM = fmaxf(GM, __shfl_xor_sync(0xffffffffu, GM, 8));
         GM = fmaxf(GM, __shfl_xor_sync(0xffffffffu, GM, 16));
-        float GL = e0.y * ex2(e0.x - GM) + e1.y * ex2(e1.x - GM);
+        float GL = e[0].y * ex2(e[0].x - GM);
+#pragma unroll
+        for (int j = 1; j < CL / 4; ++j) GL += e[j].y * ex2(e[j].x - GM);
         GL += __shfl_xor_sync(0xffffffffu, GL, 8);
         GL += __shfl_xor_sync(0xffffffffu, GL, 16);
         const float lz2 = GM + lg2(GL);
@@ -1014,24 +1042,45 @@ __global__ void tc_lse_combine_kernel(const float* __restrict__ lse_part, int nb
 struct TcPlan {
   bool diag;
   int cfg, rows, C, Kpad, Dp, nfeat, nch, num_tiles, clusters, plen;
+  bool big;  // 16-CTA clusters (one pass over 1024 < K <= 2048)
   size_t stage_bytes, smem;
 };
+
+// 16-CTA clusters are a non-portable size: opt in once per kernel.
+cudaError_t allow_big_clusters(const void* kernel) {
+  static std::mutex mu;
+  static std::vector<const void*> done;
+  std::lock_guard<std::mutex> lock(mu);
+  for (const void* k : done)
+    if (k == kernel) return cudaSuccess;
+  const cudaError_t e =
+      cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  if (e == cudaSuccess) done.push_back(kernel);
+  return e;
+}
 
 template <class G>
 size_t tc_smem_bytes(int nch) {
   return 1024 + (size_t)G::kStages * 2 * nch * G::kChunk + (size_t)G::kWSmem +
          ((size_t)G::kStages * G::kRows + 2 * kEpiWarps * G::kRB + 4 * G::kRows + 8 * kComps) * 4 +
-         (size_t)2 * kMaxCluster * G::kRows * 8 + (size_t)G::kStages * G::kRows * 4 +
+         (size_t)2 * G::kCluster * G::kRows * 8 + (size_t)G::kStages * G::kRows * 4 +
          sizeof(SmemCtl) + 64;
 }
 
 template <class G>
 int max_active_clusters(int C) {
+  // 0: not queried yet; -1: this cluster size cannot be co-resident
   static std::atomic<int> cache[kMaxCluster + 1];
   if (cache[C].load(std::memory_order_relaxed) == 0) {
     const int max_nch = (G::kMaxFeat + 63) / 64;
     ensure_dynamic_smem(reinterpret_cast<const void*>(tc_fused_kernel<G, 0>),
                         tc_smem_bytes<G>(max_nch));
+    if (C > 8 && allow_big_clusters(reinterpret_cast<const void*>(tc_fused_kernel<G, 0>)) !=
+                     cudaSuccess) {
+      cudaGetLastError();
+      cache[C].store(-1, std::memory_order_relaxed);
+      return 0;
+    }
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -1046,11 +1095,12 @@ int max_active_clusters(int C) {
     int n = 0;
     if (cudaOccupancyMaxActiveClusters(&n, tc_fused_kernel<G, 0>, &cfg) != cudaSuccess || n <= 0) {
       cudaGetLastError();
-      n = kSms / C;
+      n = C > 8 ? -1 : kSms / C;  // a 16-CTA cluster must be confirmed, not assumed
     }
-    cache[C].store(std::min(n, kSms / C), std::memory_order_relaxed);
+    cache[C].store(n < 0 ? -1 : std::min(n, kSms / C), std::memory_order_relaxed);
   }
-  return cache[C].load(std::memory_order_relaxed);
+  const int n = cache[C].load(std::memory_order_relaxed);
+  return n < 0 ? 0 : n;
 }
 
 TcPlan plan_tc(int variant, int64_t N, int K, int D, bool query_device) {
@@ -1070,10 +1120,11 @@ TcPlan plan_tc(int variant, int64_t N, int K, int D, bool query_device) {
   pl.plen = pl.diag ? 1 + 2 * D : D + 2;
   pl.stage_bytes = (size_t)2 * pl.nch * pl.rows * 128;
   const int nch = pl.nch, C = pl.C;
-  pl.smem = with_cfg(pl.cfg, [nch](auto g) { return tc_smem_bytes<decltype(g)>(nch); });
+  pl.big = pl.C > 8;
+  pl.smem = with_cfg(pl.cfg, [nch](auto g) { return tc_smem_bytes<decltype(g)>(nch); }, pl.big);
   int maxc = kSms / pl.C;
   if (query_device && pl.C <= kMaxCluster)
-    maxc = with_cfg(pl.cfg, [C](auto g) { return max_active_clusters<decltype(g)>(C); });
+    maxc = with_cfg(pl.cfg, [C](auto g) { return max_active_clusters<decltype(g)>(C); }, pl.big);
   pl.clusters = std::max(1, std::min(maxc, pl.num_tiles));
   return pl;
 }
@@ -1126,10 +1177,17 @@ SideStreams* side_streams() {
 
 template <class G>
 cudaError_t launch_fused(const TcPlan& pl, const TcParams& p, cudaStream_t stream, int mode = 0) {
-  auto kern = mode == 1 ? tc_fused_kernel<G, 1> : mode == 2 ? tc_fused_kernel<G, 2>
-                                                             : tc_fused_kernel<G, 0>;
+  void (*kern)(const TcParams) = tc_fused_kernel<G, 0>;
+  if constexpr (G::kCluster <= 8) {  // the 16-CTA instantiations run the single pass only
+    if (mode == 1) kern = tc_fused_kernel<G, 1>;
+    if (mode == 2) kern = tc_fused_kernel<G, 2>;
+  }
   cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), pl.smem);
   if (e != cudaSuccess) return e;
+  if constexpr (G::kCluster > 8) {
+    e = allow_big_clusters(reinterpret_cast<const void*>(kern));
+    if (e != cudaSuccess) return e;
+  }
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -1356,7 +1414,10 @@ size_t tc_workspace_bytes(int variant, int64_t N, int K, int D) {
   probe.K = K;
   probe.D = D;
   if (!tc_supported(variant, probe, nullptr)) return 0;
-  if (K > kBlockComps) return carve_mb(nullptr, variant, N, K, D, false).bytes;
+  if (K > 2 * kBlockComps) return carve_mb(nullptr, variant, N, K, D, false).bytes;
+  // 1024 < K <= 2048: one pass on 16-CTA clusters where the device can hold
+  // them, else the blocked path; the workspace covers either
+  const size_t blocked = K > kBlockComps ? carve_mb(nullptr, variant, N, K, D, false).bytes : 0;
   TcPlan pl = plan_tc(variant, N, K, D, false);
   WsCarve w(nullptr);
   w.take<int>(64);
@@ -1369,13 +1430,19 @@ size_t tc_workspace_bytes(int variant, int64_t N, int K, int D) {
   w.take<float>((size_t)plan_chunks(pl) * (kSms / pl.C) * pl.Kpad * pl.plen);
   w.take<uint8_t>((size_t)pl.num_tiles * pl.stage_bytes);             // split features
   if (!pl.diag) w.take<float>((size_t)pl.num_tiles * pl.rows);         // |x|^2
-  return w.used + 256;
+  return std::max(w.used + 256, blocked);
 }
 
 cudaError_t tc_estep(int variant, const EstepArgs& a) {
   if (variant == kFull) return full_tc_estep(a);
-  if (a.K > kBlockComps) return tc_estep_blocks(variant, a);
+  if (a.K > 2 * kBlockComps) return tc_estep_blocks(variant, a);
   TcPlan pl = plan_tc(variant, a.N, a.K, a.D, true);
+  if (pl.big) {  // 1024 < K <= 2048: one pass if 16-CTA clusters fit on this device
+    const int C = pl.C;
+    const int n = with_cfg(pl.cfg, [C](auto g) { return max_active_clusters<decltype(g)>(C); },
+                           true);
+    if (n <= 0) return tc_estep_blocks(variant, a);
+  }
   WsCarve w(a.ws);
   int* err = w.take<int>(64);
   float* cvec = w.take<float>(pl.Dp);
@@ -1474,7 +1541,7 @@ cudaError_t tc_estep(int variant, const EstepArgs& a) {
     p.num_tiles = pc.num_tiles;
     p.logZ = a.logZ + row0;
     p.part = part + (size_t)part_clusters * pl.Kpad * pl.plen;
-    e = with_cfg(pl.cfg, [&](auto g) { return launch_fused<decltype(g)>(pc, p, hi); });
+    e = with_cfg(pl.cfg, [&](auto g) { return launch_fused<decltype(g)>(pc, p, hi); }, pl.big);
     if (e != cudaSuccess) return e;
     part_clusters += pc.clusters;
     ++launches;
