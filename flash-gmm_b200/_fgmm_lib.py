@@ -9,6 +9,7 @@ library is missing or the device is not sm_100 the call raises.
 from __future__ import annotations
 
 import ctypes
+import functools
 import os
 import threading
 
@@ -22,6 +23,8 @@ FGMM_VARIANT_DIAG = 1
 FGMM_VARIANT_FULL = 2
 FGMM_FLAG_ACCUMULATE = 1
 FGMM_FLAG_FORCE_GENERAL = 2
+FGMM_X_F32 = 0
+FGMM_X_BF16 = 1
 
 _ERRORS = {1: "invalid argument", 2: "workspace", 3: "unsupported shape",
            4: "CUDA error", 5: "unsupported device"}
@@ -62,6 +65,8 @@ def load():
             f = getattr(lib, name)
             f.argtypes = est
             f.restype = ctypes.c_int
+        lib.fgmm_estep_x.argtypes = [ctypes.c_int, ctypes.c_int] + est
+        lib.fgmm_estep_x.restype = ctypes.c_int
         lib.fgmm_workspace_bytes.argtypes = [ctypes.c_int, _c_i64, _c_i32, _c_i32]
         lib.fgmm_workspace_bytes.restype = ctypes.c_size_t
         lib.fgmm_last_error.argtypes = []
@@ -120,7 +125,9 @@ def estep(variant: int, X: torch.Tensor, mu: torch.Tensor, cov: torch.Tensor,
     dev = X.device
     N, D = X.shape
     K = mu.shape[0]
-    X = _f32(X, dev)
+    x_bf16 = X.dtype == torch.bfloat16   # passed as is (FGMM_X_BF16), widened exactly on read
+    if not x_bf16:
+        X = _f32(X, dev)
     mu = _f32(mu, dev)
     cov = _f32(cov, dev).contiguous()
     log_pi = _f32(log_pi, dev).contiguous()
@@ -142,6 +149,8 @@ def estep(variant: int, X: torch.Tensor, mu: torch.Tensor, cov: torch.Tensor,
     flags = (FGMM_FLAG_ACCUMULATE if accumulate else 0) | \
         (FGMM_FLAG_FORCE_GENERAL if force_general else 0)
     fn = (lib.fgmm_estep_iso, lib.fgmm_estep_diag, lib.fgmm_estep_full)[variant]
+    if x_bf16:
+        fn = functools.partial(lib.fgmm_estep_x, variant, FGMM_X_BF16)
     stream = torch.cuda.current_stream(dev).cuda_stream
     with torch.cuda.device(dev):
         _check(fn(X.data_ptr(), X.stride(0), X.stride(1), mu.data_ptr(), mu.stride(0),

@@ -276,6 +276,23 @@ int fgmm_estep_full(const float* X, int64_t x_stride_n, int64_t x_stride_d, cons
 #undef SIG
 }
 
+int fgmm_estep_x(int variant, int x_type, const void* X, int64_t x_stride_n, int64_t x_stride_d,
+                 const float* mu, int64_t mu_stride_k, int64_t mu_stride_d, const float* cov,
+                 const float* log_pi, int64_t N, int32_t K, int32_t D, float* logZ, float* Nk,
+                 float* mu_acc, float* sig, void* workspace, size_t workspace_bytes,
+                 unsigned flags, void* stream) {
+  fgmm::g_last_error.clear();
+  if (variant < 0 || variant > 2)
+    return fgmm::fail(FGMM_ERR_ARG, "fgmm_estep_x: unknown variant " + std::to_string(variant));
+  if (x_type != FGMM_X_F32 && x_type != FGMM_X_BF16)
+    return fgmm::fail(FGMM_ERR_ARG, "fgmm_estep_x: unknown x_type " + std::to_string(x_type));
+  EstepArgs a{X, x_stride_n, x_stride_d, mu, mu_stride_k, mu_stride_d, cov, log_pi, N,
+              K, D, logZ, Nk, mu_acc, sig, workspace, workspace_bytes, flags,
+              reinterpret_cast<cudaStream_t>(stream)};
+  a.xtype = x_type == FGMM_X_BF16 ? fgmm::kXBF16 : fgmm::kXF32;
+  return fgmm::run_estep(variant, a);
+}
+
 int fgmm_generate_iso_rows(float* X, const int64_t* row_ids, int64_t row0, int64_t nrows,
                            int32_t D, const float* centres, int32_t K, uint64_t seed,
                            void* stream) {

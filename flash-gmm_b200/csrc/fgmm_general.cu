@@ -11,6 +11,7 @@
 #include <math.h>
 
 #include <algorithm>
+#include <type_traits>
 
 #include "fgmm_internal.cuh"
 
@@ -72,9 +73,9 @@ __global__ void prep_kernel(int variant, const float* __restrict__ cov,
 // Distance tile: acc[i][j] = sum_d (x_{row i} - mu_{comp j})^2 [* inv_{comp j, d}]
 // for the 64x64 tile (rows row0.., comps c0..); thread (ty, tx) owns rows
 // ty*4+i and components tx*4+j.
-template <bool DIAG>
+template <bool DIAG, class TX>
 __device__ __forceinline__ void distance_tile(
-    const float* __restrict__ X, int64_t sxn, int64_t sxd, const float* __restrict__ mu,
+    const TX* __restrict__ X, int64_t sxn, int64_t sxd, const float* __restrict__ mu,
     int64_t smk, int64_t smd, const float* __restrict__ inv, int64_t N, int K, int D,
     int64_t row0, int c0, float (*xs)[BR + PAD], float (*ms)[BC + PAD],
     float (*is)[BC + PAD], float acc[4][4]) {
@@ -88,7 +89,7 @@ __device__ __forceinline__ void distance_tile(
       int r = e / DC, d = e % DC;
       int64_t row = row0 + r;
       int dd = d0 + d;
-      xs[d][r] = (row < N && dd < D) ? X[row * sxn + (int64_t)dd * sxd] : 0.f;
+      xs[d][r] = (row < N && dd < D) ? ldx(X + (row * sxn + (int64_t)dd * sxd)) : 0.f;
     }
     for (int e = tid; e < BC * DC; e += kThreads) {
       int c = e / DC, d = e % DC;
@@ -140,9 +141,9 @@ __device__ __forceinline__ float loglik(float q, int c, int K, const float* __re
 // Pass 1 (iso / diag): logZ per row by an online log-sum-exp over component
 // tiles (flash_gmm.py:72-103).
 // ---------------------------------------------------------------------------
-template <bool DIAG>
+template <bool DIAG, class TX>
 __global__ void __launch_bounds__(kThreads) lse_kernel(
-    const float* __restrict__ X, int64_t sxn, int64_t sxd, const float* __restrict__ mu,
+    const TX* __restrict__ X, int64_t sxn, int64_t sxd, const float* __restrict__ mu,
     int64_t smk, int64_t smd, const float* __restrict__ inv, const float* __restrict__ cst,
     int64_t N, int K, int D, float* __restrict__ logZ) {
   __shared__ __align__(16) float xs[DC][BR + PAD];
@@ -194,9 +195,9 @@ __global__ void __launch_bounds__(kThreads) lse_kernel(
 // visited twice; cf. the overlap at flash_gmm_diag_h100.py:220-236).
 // Dynamic shared memory: acc_mu[BC][D], (diag) acc_x2[BC][D].
 // ---------------------------------------------------------------------------
-template <bool DIAG>
+template <bool DIAG, class TX>
 __global__ void __launch_bounds__(kThreads) stats_kernel(
-    const float* __restrict__ X, int64_t sxn, int64_t sxd, const float* __restrict__ mu,
+    const TX* __restrict__ X, int64_t sxn, int64_t sxd, const float* __restrict__ mu,
     int64_t smk, int64_t smd, const float* __restrict__ inv, const float* __restrict__ cst,
     int64_t N, int K, int D, const float* __restrict__ logZ, int64_t rows_per_slab,
     int part_len, float* __restrict__ part) {
@@ -250,7 +251,7 @@ __global__ void __launch_bounds__(kThreads) stats_kernel(
         int r = e / 64, d = e % 64;
         int64_t row = row0 + r;
         int dd = f0 + d;
-        xc[r][d] = (row < r_end && dd < D) ? X[row * sxn + (int64_t)dd * sxd] : 0.f;
+        xc[r][d] = (row < r_end && dd < D) ? ldx(X + (row * sxn + (int64_t)dd * sxd)) : 0.f;
       }
       __syncthreads();
       float am[4][4], a2[4][4];
@@ -317,8 +318,9 @@ __device__ __forceinline__ float full_maha_part(const float* __restrict__ yrow,
   return s;
 }
 
+template <class TX>
 __global__ void __launch_bounds__(kThreads) full_lse_kernel(
-    const float* __restrict__ X, int64_t sxn, int64_t sxd, const float* __restrict__ mu,
+    const TX* __restrict__ X, int64_t sxn, int64_t sxd, const float* __restrict__ mu,
     int64_t smk, int64_t smd, const float* __restrict__ L, const float* __restrict__ cst,
     int64_t N, int K, int D, float* __restrict__ logZ) {
   extern __shared__ __align__(16) float dyn[];
@@ -331,7 +333,7 @@ __global__ void __launch_bounds__(kThreads) full_lse_kernel(
   for (int e = tid; e < BR * D; e += kThreads) {
     int r = e / D, d = e % D;
     int64_t row = row0 + r;
-    xs[r * ld + d] = row < N ? X[row * sxn + (int64_t)d * sxd] : 0.f;
+    xs[r * ld + d] = row < N ? ldx(X + (row * sxn + (int64_t)d * sxd)) : 0.f;
   }
   float run_m = -INFINITY, run_s = 0.f;
   for (int k = 0; k < K; ++k) {
@@ -357,9 +359,9 @@ __global__ void __launch_bounds__(kThreads) full_lse_kernel(
 // Pass 2, full covariance: block = (component k, row slab).  Thread t owns a
 // DT x DT block of sig_outer[k] (DT = D_MAX/16) and, for t < D, mu_acc[k][t].
 // part[(slab*K + k)*part_len + ...] = { Nk, mu_acc[0..D), outer[0..D*D) }.
-template <int DT>
+template <int DT, class TX>
 __global__ void __launch_bounds__(kThreads) full_stats_kernel(
-    const float* __restrict__ X, int64_t sxn, int64_t sxd, const float* __restrict__ mu,
+    const TX* __restrict__ X, int64_t sxn, int64_t sxd, const float* __restrict__ mu,
     int64_t smk, int64_t smd, const float* __restrict__ L, const float* __restrict__ cst,
     int64_t N, int K, int D, const float* __restrict__ logZ, int64_t rows_per_slab,
     int part_len, float* __restrict__ part) {
@@ -388,7 +390,7 @@ __global__ void __launch_bounds__(kThreads) full_stats_kernel(
     for (int e = tid; e < BR * D; e += kThreads) {
       int r = e / D, d = e % D;
       int64_t row = row0 + r;
-      float x = row < r_end ? X[row * sxn + (int64_t)d * sxd] : 0.f;
+      float x = row < r_end ? ldx(X + (row * sxn + (int64_t)d * sxd)) : 0.f;
       xs[r * ld + d] = x;
       ys[r * ld + d] = x - mu[(int64_t)k * smk + (int64_t)d * smd];
     }
@@ -515,48 +517,53 @@ cudaError_t general_estep(int variant, const EstepArgs& a) {
 
   prep_kernel<<<(K + 127) / 128, 128, 0, st>>>(variant, a.cov, a.lpi, K, D, cst, inv);
   const unsigned row_blocks = (unsigned)((N + BR - 1) / BR);
-  if (variant != kFull) {
-    const bool diag = variant == kDiag;
-    if (diag)
-      lse_kernel<true><<<row_blocks, kThreads, 0, st>>>(a.X, a.sxn, a.sxd, a.mu, a.smk, a.smd,
-                                                         inv, cst, N, K, D, a.logZ);
-    else
-      lse_kernel<false><<<row_blocks, kThreads, 0, st>>>(a.X, a.sxn, a.sxd, a.mu, a.smk, a.smd,
-                                                          inv, cst, N, K, D, a.logZ);
-    const size_t dyn = ((size_t)3 * DC * (BR + PAD) + (size_t)3 * BR * (BC + PAD) +
-                        (size_t)BC * D * (diag ? 2 : 1)) * sizeof(float);
-    dim3 grid((K + BC - 1) / BC, p.slabs);
-    profile_mark(false, st);
-    if (diag) {
-      ensure_dynamic_smem(reinterpret_cast<const void*>(stats_kernel<true>), dyn);
-      stats_kernel<true><<<grid, kThreads, dyn, st>>>(a.X, a.sxn, a.sxd, a.mu, a.smk, a.smd,
-                                                       inv, cst, N, K, D, a.logZ,
-                                                       p.rows_per_slab, p.part_len, part);
+  with_xtype(a.xtype, [&](auto tx) {
+    using TX = std::remove_const_t<std::remove_pointer_t<decltype(tx)>>;
+    const TX* X = a.x<TX>();
+    if (variant != kFull) {
+      const bool diag = variant == kDiag;
+      if (diag)
+        lse_kernel<true, TX><<<row_blocks, kThreads, 0, st>>>(X, a.sxn, a.sxd, a.mu, a.smk,
+                                                              a.smd, inv, cst, N, K, D, a.logZ);
+      else
+        lse_kernel<false, TX><<<row_blocks, kThreads, 0, st>>>(X, a.sxn, a.sxd, a.mu, a.smk,
+                                                               a.smd, inv, cst, N, K, D, a.logZ);
+      const size_t dyn = ((size_t)3 * DC * (BR + PAD) + (size_t)3 * BR * (BC + PAD) +
+                          (size_t)BC * D * (diag ? 2 : 1)) * sizeof(float);
+      dim3 grid((K + BC - 1) / BC, p.slabs);
+      profile_mark(false, st);
+      if (diag) {
+        ensure_dynamic_smem(reinterpret_cast<const void*>(stats_kernel<true, TX>), dyn);
+        stats_kernel<true, TX><<<grid, kThreads, dyn, st>>>(X, a.sxn, a.sxd, a.mu, a.smk, a.smd,
+                                                            inv, cst, N, K, D, a.logZ,
+                                                            p.rows_per_slab, p.part_len, part);
+      } else {
+        ensure_dynamic_smem(reinterpret_cast<const void*>(stats_kernel<false, TX>), dyn);
+        stats_kernel<false, TX><<<grid, kThreads, dyn, st>>>(X, a.sxn, a.sxd, a.mu, a.smk,
+                                                             a.smd, inv, cst, N, K, D, a.logZ,
+                                                             p.rows_per_slab, p.part_len, part);
+      }
     } else {
-      ensure_dynamic_smem(reinterpret_cast<const void*>(stats_kernel<false>), dyn);
-      stats_kernel<false><<<grid, kThreads, dyn, st>>>(a.X, a.sxn, a.sxd, a.mu, a.smk, a.smd,
-                                                        inv, cst, N, K, D, a.logZ,
-                                                        p.rows_per_slab, p.part_len, part);
+      const size_t dyn = ((size_t)D * D + 2 * (size_t)BR * (D + 1)) * sizeof(float);
+      ensure_dynamic_smem(reinterpret_cast<const void*>(full_lse_kernel<TX>), dyn);
+      full_lse_kernel<TX><<<row_blocks, kThreads, dyn, st>>>(X, a.sxn, a.sxd, a.mu, a.smk, a.smd,
+                                                             a.cov, cst, N, K, D, a.logZ);
+      dim3 grid(K, p.slabs);
+      profile_mark(false, st);
+      if (D <= 64) {
+        ensure_dynamic_smem(reinterpret_cast<const void*>(full_stats_kernel<4, TX>), dyn);
+        full_stats_kernel<4, TX><<<grid, kThreads, dyn, st>>>(X, a.sxn, a.sxd, a.mu, a.smk,
+                                                              a.smd, a.cov, cst, N, K, D, a.logZ,
+                                                              p.rows_per_slab, p.part_len, part);
+      } else {
+        ensure_dynamic_smem(reinterpret_cast<const void*>(full_stats_kernel<8, TX>), dyn);
+        full_stats_kernel<8, TX><<<grid, kThreads, dyn, st>>>(X, a.sxn, a.sxd, a.mu, a.smk,
+                                                              a.smd, a.cov, cst, N, K, D, a.logZ,
+                                                              p.rows_per_slab, p.part_len, part);
+      }
     }
-  } else {
-    const size_t dyn = ((size_t)D * D + 2 * (size_t)BR * (D + 1)) * sizeof(float);
-    ensure_dynamic_smem(reinterpret_cast<const void*>(full_lse_kernel), dyn);
-    full_lse_kernel<<<row_blocks, kThreads, dyn, st>>>(a.X, a.sxn, a.sxd, a.mu, a.smk, a.smd,
-                                                        a.cov, cst, N, K, D, a.logZ);
-    dim3 grid(K, p.slabs);
-    profile_mark(false, st);
-    if (D <= 64) {
-      ensure_dynamic_smem(reinterpret_cast<const void*>(full_stats_kernel<4>), dyn);
-      full_stats_kernel<4><<<grid, kThreads, dyn, st>>>(a.X, a.sxn, a.sxd, a.mu, a.smk, a.smd,
-                                                         a.cov, cst, N, K, D, a.logZ,
-                                                         p.rows_per_slab, p.part_len, part);
-    } else {
-      ensure_dynamic_smem(reinterpret_cast<const void*>(full_stats_kernel<8>), dyn);
-      full_stats_kernel<8><<<grid, kThreads, dyn, st>>>(a.X, a.sxn, a.sxd, a.mu, a.smk, a.smd,
-                                                         a.cov, cst, N, K, D, a.logZ,
-                                                         p.rows_per_slab, p.part_len, part);
-    }
-  }
+    return 0;
+  });
   profile_mark(true, st);
   const int64_t total = (int64_t)K * p.part_len;
   const int rblocks = (int)std::min<int64_t>((total + 255) / 256, 8 * num_sms());

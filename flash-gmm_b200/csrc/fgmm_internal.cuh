@@ -14,9 +14,33 @@ constexpr double kLog2E = 1.4426950408889634;   // 1 / ln 2
 
 enum Variant { kIso = 0, kDiag = 1, kFull = 2 };
 
+// Element type of X: fp32, or bfloat16 stored as its 16 bits (uint16_t).
+enum XType { kXF32 = 0, kXBF16 = 1 };
+
+// X loads widened to fp32 (a bfloat16 is the top half of an fp32: exact).
+__device__ __forceinline__ float ldx(const float* p) { return __ldg(p); }
+__device__ __forceinline__ float ldx(const uint16_t* p) {
+  return __uint_as_float((uint32_t)__ldg(p) << 16);
+}
+// Four consecutive elements from a 16-byte (fp32) or 8-byte (bf16) aligned address.
+__device__ __forceinline__ float4 ldx4(const float* p) {
+  return __ldg(reinterpret_cast<const float4*>(p));
+}
+__device__ __forceinline__ float4 ldx4(const uint16_t* p) {
+  const uint2 u = __ldg(reinterpret_cast<const uint2*>(p));
+  return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u),
+                     __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xffff0000u));
+}
+// Calls f with a null pointer of X's element type (a type tag).
+template <class F>
+decltype(auto) with_xtype(int xtype, F&& f) {
+  if (xtype == kXBF16) return f(static_cast<const uint16_t*>(nullptr));
+  return f(static_cast<const float*>(nullptr));
+}
+
 // Arguments of one E-step call, as received through the C ABI.
 struct EstepArgs {
-  const float* X;
+  const void* X;     // xtype elements
   int64_t sxn, sxd;
   const float* mu;
   int64_t smk, smd;
@@ -33,6 +57,15 @@ struct EstepArgs {
   size_t ws_bytes;
   unsigned flags;
   cudaStream_t stream;
+  int xtype = kXF32;
+  // X as its element type, and its 16-byte-vector loads allowed (unit
+  // feature stride, aligned base, rows of a multiple of 4 elements)
+  template <class TX>
+  const TX* x() const { return static_cast<const TX*>(X); }
+  int x_vec_ok() const {
+    const uintptr_t align = xtype == kXBF16 ? 7 : 15;
+    return sxd == 1 && (reinterpret_cast<uintptr_t>(X) & align) == 0 && sxn % 4 == 0;
+  }
 };
 
 // Bump allocator over the caller's workspace; every block 256-byte aligned.

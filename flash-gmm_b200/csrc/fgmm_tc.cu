@@ -59,6 +59,7 @@
 #include <algorithm>
 #include <atomic>
 #include <mutex>
+#include <type_traits>
 #include <vector>
 
 #include "fgmm_internal.cuh"
@@ -833,9 +834,9 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fused_kernel(const TcParams p)
 //   iso:  features (x-c) 2^-a, plus |x-c|^2 per row;
 //   diag: features [((x-c) 2^-a)^2 | (x-c) 2^-a].
 // ---------------------------------------------------------------------------
-template <class G>
+template <class G, class TX>
 __global__ void __launch_bounds__(256) tc_split_kernel(
-    const float* __restrict__ X, int64_t sxn, int64_t sxd, int vec_ok, int64_t N, int D, int Dp,
+    const TX* __restrict__ X, int64_t sxn, int64_t sxd, int vec_ok, int64_t N, int D, int Dp,
     int nch, int64_t rows_pad, const int* __restrict__ amax, const float* __restrict__ cvec,
     uint8_t* __restrict__ xsplit, float* __restrict__ xsq, int* __restrict__ err) {
   constexpr int ROWS = G::kRows, NV = G::kNV;
@@ -866,14 +867,14 @@ __global__ void __launch_bounds__(256) tc_split_kernel(
         const int f = 128 * v + 4 * lane;
         float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
         if (f < Dp && row < N) {
-          const float* src = X + row * sxn;
+          const TX* src = X + row * sxn;
           if (vec_ok && f + 3 < D) {
-            x = __ldg(reinterpret_cast<const float4*>(src + f));
+            x = ldx4(src + f);
           } else {
-            if (f + 0 < D) x.x = __ldg(src + (int64_t)(f + 0) * sxd);
-            if (f + 1 < D) x.y = __ldg(src + (int64_t)(f + 1) * sxd);
-            if (f + 2 < D) x.z = __ldg(src + (int64_t)(f + 2) * sxd);
-            if (f + 3 < D) x.w = __ldg(src + (int64_t)(f + 3) * sxd);
+            if (f + 0 < D) x.x = ldx(src + (int64_t)(f + 0) * sxd);
+            if (f + 1 < D) x.y = ldx(src + (int64_t)(f + 1) * sxd);
+            if (f + 2 < D) x.z = ldx(src + (int64_t)(f + 2) * sxd);
+            if (f + 3 < D) x.w = ldx(src + (int64_t)(f + 3) * sxd);
           }
         }
         xr[u][v] = x;
@@ -1276,14 +1277,17 @@ cudaError_t tc_estep_blocks(int variant, const EstepArgs& a) {
           m.Wlo[b], m.consts[b]);
     ++launches;
   }
-  const int vec_ok = a.sxd == 1 && (reinterpret_cast<uintptr_t>(a.X) & 15) == 0 && a.sxn % 4 == 0;
+  const int vec_ok = a.x_vec_ok();
   const int sblocks =
       (int)std::min<int64_t>((m.npad + 8 * kSplitRows - 1) / (8 * kSplitRows), 16 * kSms);
   with_cfg(p0.cfg, [&](auto g) {
-    tc_split_kernel<decltype(g)><<<sblocks, 256, 0, st>>>(
-        a.X, a.sxn, a.sxd, vec_ok, a.N, a.D, p0.Dp, p0.nch, m.npad, m.err + 1, m.cvec, m.xsplit,
-        m.xsq, m.err);
-    return 0;
+    return with_xtype(a.xtype, [&](auto tx) {
+      using TX = std::remove_const_t<std::remove_pointer_t<decltype(tx)>>;
+      tc_split_kernel<decltype(g), TX><<<sblocks, 256, 0, st>>>(
+          a.x<TX>(), a.sxn, a.sxd, vec_ok, a.N, a.D, p0.Dp, p0.nch, m.npad, m.err + 1, m.cvec,
+          m.xsplit, m.xsq, m.err);
+      return 0;
+    });
   });
   ++launches;
 
@@ -1484,7 +1488,7 @@ cudaError_t tc_estep(int variant, const EstepArgs& a) {
     tc_prep_kernel<<<pl.Kpad, prep_threads(pl.Dp), 0, hi>>>(a.mu, a.smk, a.smd, a.cov, a.lpi, cvec, a.K, a.D,
                                             pl.Dp, Whi, Wlo, consts);
   launches += 2;
-  const int vec_ok = a.sxd == 1 && (reinterpret_cast<uintptr_t>(a.X) & 15) == 0 && a.sxn % 4 == 0;
+  const int vec_ok = a.x_vec_ok();
 
   // split passes (stream lo), one per chunk of tiles [t0, t1)
   for (int c = 0; c < nchunks; ++c) {
@@ -1496,14 +1500,17 @@ cudaError_t tc_estep(int variant, const EstepArgs& a) {
     const int64_t rows_pad = (int64_t)(t1 - t0) * pl.rows;
     const int sblocks =
         (int)std::min<int64_t>((rows_pad + 8 * kSplitRows - 1) / (8 * kSplitRows), 16 * kSms);
-    const float* Xc = a.X + row0 * a.sxn;
     uint8_t* xs_c = xsplit + (size_t)t0 * pl.stage_bytes;
     float* xsq_c = pl.diag ? nullptr : xsq + (size_t)t0 * pl.rows;
     with_cfg(pl.cfg, [&](auto g) {
-      tc_split_kernel<decltype(g)><<<sblocks, 256, 0, lo>>>(Xc, a.sxn, a.sxd, vec_ok, rows, a.D,
-                                                            pl.Dp, pl.nch, rows_pad, err + 1,
-                                                            cvec, xs_c, xsq_c, err);
-      return 0;
+      return with_xtype(a.xtype, [&](auto tx) {
+        using TX = std::remove_const_t<std::remove_pointer_t<decltype(tx)>>;
+        const TX* Xc = a.x<TX>() + row0 * a.sxn;
+        tc_split_kernel<decltype(g), TX><<<sblocks, 256, 0, lo>>>(
+            Xc, a.sxn, a.sxd, vec_ok, rows, a.D, pl.Dp, pl.nch, rows_pad, err + 1, cvec, xs_c,
+            xsq_c, err);
+        return 0;
+      });
     });
     ++launches;
     if (nchunks > 1 && (e = cudaEventRecord(ss->ev[2 + c], lo)) != cudaSuccess) return e;

@@ -33,6 +33,7 @@
 #include <math.h>
 
 #include <algorithm>
+#include <type_traits>
 
 #include "fgmm_internal.cuh"
 #include "fgmm_ptx.cuh"
@@ -196,8 +197,9 @@ __host__ __device__ __forceinline__ int xs2_stride(int D) {
 // 4l..4l+3 (features >= D and rows >= N are zero):
 //   xsplit: x~ 2^-a1 as fp16 hi/lo in 128-row swizzled K-major tiles (pass 1);
 //   xs2:    x~ 2^-a2 in fp32, D values then a constant 1 per row (pass 2).
+template <class TX>
 __global__ void __launch_bounds__(256) full_split_kernel(
-    const float* __restrict__ X, int64_t sxn, int64_t sxd, int vec_ok, int64_t N, int D,
+    const TX* __restrict__ X, int64_t sxn, int64_t sxd, int vec_ok, int64_t N, int D,
     int64_t rows_pad, const float* __restrict__ cvec, const int* __restrict__ amax,
     uint8_t* __restrict__ xsplit, float* __restrict__ xs2, int* __restrict__ err) {
   const int lane = threadIdx.x & 31;
@@ -223,14 +225,14 @@ __global__ void __launch_bounds__(256) full_split_kernel(
     if (!active) continue;
     float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
     if (row < N) {
-      const float* src = X + row * sxn;
+      const TX* src = X + row * sxn;
       if (vec_ok && f + 3 < D) {
-        x = __ldg(reinterpret_cast<const float4*>(src + f));
+        x = ldx4(src + f);
       } else {
-        if (f + 0 < D) x.x = __ldg(src + (int64_t)(f + 0) * sxd);
-        if (f + 1 < D) x.y = __ldg(src + (int64_t)(f + 1) * sxd);
-        if (f + 2 < D) x.z = __ldg(src + (int64_t)(f + 2) * sxd);
-        if (f + 3 < D) x.w = __ldg(src + (int64_t)(f + 3) * sxd);
+        if (f + 0 < D) x.x = ldx(src + (int64_t)(f + 0) * sxd);
+        if (f + 1 < D) x.y = ldx(src + (int64_t)(f + 1) * sxd);
+        if (f + 2 < D) x.z = ldx(src + (int64_t)(f + 2) * sxd);
+        if (f + 3 < D) x.w = ldx(src + (int64_t)(f + 3) * sxd);
       }
       x.x -= cc.x;
       x.y -= cc.y;
@@ -952,10 +954,15 @@ cudaError_t full_tc_estep(const EstepArgs& a) {
   centre_kernel<<<pl.Dp, 256, 0, st>>>(a.mu, a.smk, a.smd, a.K, a.D, ws.cvec, amax);
   full_prep_kernel<<<pl.Kpad, 64, 0, st>>>(a.mu, a.smk, a.smd, a.cov, a.lpi, ws.cvec, a.K, a.D,
                                            pl.Dp, ws.lgroups, ws.bvec, ws.kconst);
-  const int vec_ok = a.sxd == 1 && (reinterpret_cast<uintptr_t>(a.X) & 15) == 0 && a.sxn % 4 == 0;
+  const int vec_ok = a.x_vec_ok();
   const int sblocks = (int)std::min<int64_t>((pl.Npad + 7) / 8, 16 * kSmsFull);
-  full_split_kernel<<<sblocks, 256, 0, st>>>(a.X, a.sxn, a.sxd, vec_ok, a.N, a.D, pl.Npad,
-                                             ws.cvec, amax, ws.xsplit, ws.xs2, ws.err);
+  with_xtype(a.xtype, [&](auto tx) {
+    using TX = std::remove_const_t<std::remove_pointer_t<decltype(tx)>>;
+    full_split_kernel<TX><<<sblocks, 256, 0, st>>>(a.x<TX>(), a.sxn, a.sxd, vec_ok, a.N, a.D,
+                                                   pl.Npad, ws.cvec, amax, ws.xsplit, ws.xs2,
+                                                   ws.err);
+    return 0;
+  });
 
   P1Params p1;
   p1.xsplit = ws.xsplit;

@@ -69,6 +69,9 @@ extern "C" {
 #define FGMM_VARIANT_FULL 2
 
 #define FGMM_FLAG_ACCUMULATE 1u /* add Nk/mu_acc/sig into the outputs      */
+
+#define FGMM_X_F32 0            /* X element types of fgmm_estep_x */
+#define FGMM_X_BF16 1
 #define FGMM_FLAG_FORCE_GENERAL 2u /* use the general (non-tensor-core)
                                       kernels even when the fast path applies */
 
@@ -114,6 +117,23 @@ FGMM_API int fgmm_estep_full(const float* X, int64_t x_stride_n, int64_t x_strid
                     float* logZ, float* Nk, float* mu_acc, float* sig_outer,
                     void* workspace, size_t workspace_bytes,
                     unsigned flags, void* stream);
+
+/* Any variant (FGMM_VARIANT_*) with X stored as x_type elements: FGMM_X_F32
+ * (the three entries above) or FGMM_X_BF16 (bfloat16 bit patterns, 2 bytes
+ * each; strides in elements).  A bfloat16 X is widened exactly to fp32 as it
+ * is read, so the results equal those of the fp32 entries on the widened
+ * values.  No counterpart in the reference: its H100 module casts X to
+ * bfloat16 on the host side of each call (flash_gmm_h100.py:272-276); here a
+ * caller that already holds bfloat16 data passes it as is.  cov is
+ * log_sigma_sq (iso, diag) or prec_chol (full); sig is sig_acc or
+ * sig_outer. */
+FGMM_API int fgmm_estep_x(int variant, int x_type, const void* X, int64_t x_stride_n,
+                 int64_t x_stride_d, const float* mu, int64_t mu_stride_k,
+                 int64_t mu_stride_d, const float* cov, const float* log_pi,
+                 int64_t N, int32_t K, int32_t D,
+                 float* logZ, float* Nk, float* mu_acc, float* sig,
+                 void* workspace, size_t workspace_bytes,
+                 unsigned flags, void* stream);
 
 /* Isotropic E-step that allocates nothing and takes no workspace: same
  * arguments, results and paths as fgmm_estep_iso, with the scratch in a

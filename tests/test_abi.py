@@ -59,3 +59,14 @@ def test_bad_arguments_are_reported_without_a_device(lib):
     code = lib.fgmm_estep_full(None, 1, 1, None, 1, 1, None, None, 10, 4, 4,
                                None, None, None, None, None, 0, 0, None)
     assert code == 1 and b"null pointer" in lib.fgmm_last_error()
+
+
+def test_estep_x_rejects_unknown_types_without_a_device(lib):
+    f = ctypes.CDLL(L.LIB_PATH).fgmm_estep_x
+    f.restype = ctypes.c_int
+    args = [None, 1, 1, None, 1, 1, None, None, ctypes.c_int64(10), 4, 4,
+            None, None, None, None, None, ctypes.c_size_t(0), ctypes.c_uint(0), None]
+    assert f(0, 7, *args) == 1
+    assert b"unknown x_type" in lib.fgmm_last_error()
+    assert f(5, 0, *args) == 1
+    assert b"unknown variant" in lib.fgmm_last_error()
