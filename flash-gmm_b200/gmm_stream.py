@@ -119,6 +119,9 @@ def stream_estep(chunks: Iterable[torch.Tensor], mu: torch.Tensor, cov: torch.Te
     copy_stream = torch.cuda.Stream(device)
     compute = torch.cuda.current_stream(device)
     logZ_parts = []
+    # two device staging buffers, reused for every chunk (grown if a larger
+    # chunk comes): no allocation per chunk, and no cross-stream frees
+    bufs = [None, None]
     staged = [None, None]
     events = [torch.cuda.Event(), torch.cuda.Event()]
     first = True
@@ -127,9 +130,16 @@ def stream_estep(chunks: Iterable[torch.Tensor], mu: torch.Tensor, cov: torch.Te
     slot = 0
 
     def stage(chunk, s):
+        n = chunk.shape[0]
+        b = bufs[s]
+        if b is None or b.shape[0] < n or b.dtype != chunk.dtype or b.shape[1:] != chunk.shape[1:]:
+            # allocated on the compute stream, whose E-step is the last user
+            bufs[s] = b = torch.empty((n,) + tuple(chunk.shape[1:]), device=device,
+                                      dtype=chunk.dtype)
         with torch.cuda.stream(copy_stream):
-            copy_stream.wait_stream(compute)  # buffer s free once its E-step ran
-            staged[s] = chunk.to(device, non_blocking=True)
+            copy_stream.wait_stream(compute)  # buffer s free once its last E-step ran
+            staged[s] = b[:n]
+            staged[s].copy_(chunk, non_blocking=True)
             events[s].record(copy_stream)
 
     if nxt is not None:
@@ -145,7 +155,6 @@ def stream_estep(chunks: Iterable[torch.Tensor], mu: torch.Tensor, cov: torch.Te
         logZ = torch.empty(Xd.shape[0], device=device, dtype=torch.float32)
         L.estep(VARIANTS[variant], Xd, mu, cov, log_pi, out=(logZ, Nk, mu_acc, sig),
                 accumulate=init is not None or not first)
-        Xd.record_stream(compute)
         first = False
         if keep_logZ:
             logZ_parts.append(logZ)
