@@ -193,75 +193,83 @@ __host__ __device__ __forceinline__ int xs2_stride(int D) {
   return (need + 1) & ~1;
 }
 
-// Split pass (any X strides), one warp per row, lane l carries features
-// 4l..4l+3 (features >= D and rows >= N are zero):
+// Split pass (any X strides): a half-warp per row, lane l of the half
+// carries features 4l..4l+3 (features >= D and rows >= N are zero); each warp
+// takes 8 consecutive rows per step and issues all their loads first:
 //   xsplit: x~ 2^-a1 as fp16 hi/lo in 128-row swizzled K-major tiles (pass 1);
 //   xs2:    x~ 2^-a2 in fp32, D values then a constant 1 per row (pass 2).
+constexpr int kFullSplitRows = 8;
 template <class TX>
 __global__ void __launch_bounds__(256) full_split_kernel(
     const TX* __restrict__ X, int64_t sxn, int64_t sxd, int vec_ok, int64_t N, int D,
     int64_t rows_pad, const float* __restrict__ cvec, const int* __restrict__ amax,
     uint8_t* __restrict__ xsplit, float* __restrict__ xs2, int* __restrict__ err) {
-  const int lane = threadIdx.x & 31;
+  const int lane = threadIdx.x & 31, hw = lane >> 4, l16 = lane & 15;
   const float am = __int_as_float(*amax);
   const int a1 = scale_exp_to(am, 5), a2 = scale_exp_to(am, 3);
-  const int f = 4 * lane;
-  const bool active = lane < 16;  // 64 features
+  const int f = 4 * l16;  // 64 features per half-warp
+  const int xs_stride = xs2_stride(D);
   float4 cc = make_float4(0.f, 0.f, 0.f, 0.f);
-  if (active) {
-    if (f + 0 < D) cc.x = cvec[f + 0];
-    if (f + 1 < D) cc.y = cvec[f + 1];
-    if (f + 2 < D) cc.z = cvec[f + 2];
-    if (f + 3 < D) cc.w = cvec[f + 3];
-  }
-  for (int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5); row < rows_pad;
-       row += (int64_t)gridDim.x * 8) {
-    const int xs_stride = xs2_stride(D);
-    float* x2row = xs2 + row * xs_stride;
-    if (lane == 16) {  // constant slot D, zeros up to the stride
-      x2row[D] = 1.0f;
-      for (int d = D + 1; d < xs_stride; ++d) x2row[d] = 0.f;
-    }
-    if (!active) continue;
-    float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (row < N) {
-      const TX* src = X + row * sxn;
-      if (vec_ok && f + 3 < D) {
-        x = ldx4(src + f);
-      } else {
-        if (f + 0 < D) x.x = ldx(src + (int64_t)(f + 0) * sxd);
-        if (f + 1 < D) x.y = ldx(src + (int64_t)(f + 1) * sxd);
-        if (f + 2 < D) x.z = ldx(src + (int64_t)(f + 2) * sxd);
-        if (f + 3 < D) x.w = ldx(src + (int64_t)(f + 3) * sxd);
+  if (f + 0 < D) cc.x = cvec[f + 0];
+  if (f + 1 < D) cc.y = cvec[f + 1];
+  if (f + 2 < D) cc.z = cvec[f + 2];
+  if (f + 3 < D) cc.w = cvec[f + 3];
+  // rows_pad is a multiple of 128, so every row of a step is < rows_pad
+  for (int64_t row0 = ((int64_t)blockIdx.x * 8 + (threadIdx.x >> 5)) * kFullSplitRows;
+       row0 < rows_pad; row0 += (int64_t)gridDim.x * 8 * kFullSplitRows) {
+    float4 xr[kFullSplitRows / 2];
+#pragma unroll
+    for (int u = 0; u < kFullSplitRows / 2; ++u) {
+      const int64_t row = row0 + 2 * u + hw;
+      float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (row < N) {
+        const TX* src = X + row * sxn;
+        if (vec_ok && f + 3 < D) {
+          x = ldx4(src + f);
+        } else {
+          if (f + 0 < D) x.x = ldx(src + (int64_t)(f + 0) * sxd);
+          if (f + 1 < D) x.y = ldx(src + (int64_t)(f + 1) * sxd);
+          if (f + 2 < D) x.z = ldx(src + (int64_t)(f + 2) * sxd);
+          if (f + 3 < D) x.w = ldx(src + (int64_t)(f + 3) * sxd);
+        }
       }
-      x.x -= cc.x;
-      x.y -= cc.y;
-      x.z -= cc.z;
-      x.w -= cc.w;
-      if (f + 0 >= D) x.x = 0.f;
-      if (f + 1 >= D) x.y = 0.f;
-      if (f + 2 >= D) x.z = 0.f;
-      if (f + 3 >= D) x.w = 0.f;
+      xr[u] = x;
     }
-    const float4 x2 = make_float4(ldexpf(x.x, -a2), ldexpf(x.y, -a2), ldexpf(x.z, -a2),
-                                  ldexpf(x.w, -a2));
-    if (f + 0 < D) x2row[f + 0] = x2.x;
-    if (f + 1 < D) x2row[f + 1] = x2.y;
-    if (f + 2 < D) x2row[f + 2] = x2.z;
-    if (f + 3 < D) x2row[f + 3] = x2.w;
-    // products of two such values must stay inside fp16's range in pass 2
-    if (!(fmaxf(fmaxf(fabsf(x2.x), fabsf(x2.y)), fmaxf(fabsf(x2.z), fabsf(x2.w))) < 255.f))
-      atomicOr(err, 0x20000);
-    x = make_float4(ldexpf(x.x, -a1), ldexpf(x.y, -a1), ldexpf(x.z, -a1), ldexpf(x.w, -a1));
-    const float mx = fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w)));
-    if (!(mx < 65504.f)) atomicOr(err, 0x10000);  // outside fp16 range (or NaN)
-    uint32_t h0, l0, h1, l1;
-    split2(x.x, x.y, h0, l0);
-    split2(x.z, x.w, h1, l1);
-    uint8_t* tile = xsplit + (row / kP1Rows) * (2 * kXTile);
-    const uint32_t off = xoff((int)(row % kP1Rows), f, kXTile);
-    *reinterpret_cast<uint2*>(tile + off) = make_uint2(h0, h1);
-    *reinterpret_cast<uint2*>(tile + kXTile + off) = make_uint2(l0, l1);
+#pragma unroll
+    for (int u = 0; u < kFullSplitRows / 2; ++u) {
+      const int64_t row = row0 + 2 * u + hw;
+      float4 x = xr[u];
+      if (row < N) {
+        x.x = f + 0 < D ? x.x - cc.x : 0.f;
+        x.y = f + 1 < D ? x.y - cc.y : 0.f;
+        x.z = f + 2 < D ? x.z - cc.z : 0.f;
+        x.w = f + 3 < D ? x.w - cc.w : 0.f;
+      }
+      float* x2row = xs2 + row * xs_stride;
+      if (l16 == 0) {  // constant slot D, zeros up to the stride
+        x2row[D] = 1.0f;
+        for (int d = D + 1; d < xs_stride; ++d) x2row[d] = 0.f;
+      }
+      const float4 x2 = make_float4(ldexpf(x.x, -a2), ldexpf(x.y, -a2), ldexpf(x.z, -a2),
+                                    ldexpf(x.w, -a2));
+      if (f + 0 < D) x2row[f + 0] = x2.x;
+      if (f + 1 < D) x2row[f + 1] = x2.y;
+      if (f + 2 < D) x2row[f + 2] = x2.z;
+      if (f + 3 < D) x2row[f + 3] = x2.w;
+      // products of two such values must stay inside fp16's range in pass 2
+      if (!(fmaxf(fmaxf(fabsf(x2.x), fabsf(x2.y)), fmaxf(fabsf(x2.z), fabsf(x2.w))) < 255.f))
+        atomicOr(err, 0x20000);
+      x = make_float4(ldexpf(x.x, -a1), ldexpf(x.y, -a1), ldexpf(x.z, -a1), ldexpf(x.w, -a1));
+      const float mx = fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w)));
+      if (!(mx < 65504.f)) atomicOr(err, 0x10000);  // outside fp16 range (or NaN)
+      uint32_t h0, l0, h1, l1;
+      split2(x.x, x.y, h0, l0);
+      split2(x.z, x.w, h1, l1);
+      uint8_t* tile = xsplit + (row / kP1Rows) * (2 * kXTile);
+      const uint32_t off = xoff((int)(row % kP1Rows), f, kXTile);
+      *reinterpret_cast<uint2*>(tile + off) = make_uint2(h0, h1);
+      *reinterpret_cast<uint2*>(tile + kXTile + off) = make_uint2(l0, l1);
+    }
   }
 }
 
@@ -588,7 +596,8 @@ __device__ __forceinline__ uint32_t quad_desc(int Q, int D) {
 // Responsibilities for pass 2, one block per (64-row chunk, component block),
 // thread = component: r = 2^(ll2 - lz2) (0 past N or K), split into fp16
 // hi/lo and written as the K-major, 128B-swizzled A operand of pass 2 (one
-// 128-byte row of 64 rows per component).
+// 128-byte row of 64 rows per component).  The 32 KB block is built in
+// shared memory and written out with coalesced 16-byte stores.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(kP2Comps) full_resp_kernel(const float* __restrict__ ll2,
                                                              int64_t ld_ll,
@@ -600,6 +609,7 @@ __global__ void __launch_bounds__(kP2Comps) full_resp_kernel(const float* __rest
   const int k = cbk * kP2Comps + t;
   const int64_t r0 = (int64_t)chunk * kP2Rows;
   __shared__ float lz[kP2Rows];
+  __shared__ __align__(16) uint8_t img[2 * kRBlock];
   if (t < kP2Rows) lz[t] = r0 + t < N ? lz2[r0 + t] : 0.f;
   __syncthreads();
   const bool kvalid = k < K;
@@ -628,9 +638,13 @@ __global__ void __launch_bounds__(kP2Comps) full_resp_kernel(const float* __rest
 #pragma unroll
     for (int u = 0; u < 4; ++u) split2(rv[8 * g + 2 * u], rv[8 * g + 2 * u + 1], hi[u], lo[u]);
     const uint32_t off = xoff(t, 8 * g, kRBlock);
-    *reinterpret_cast<uint4*>(blk + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-    *reinterpret_cast<uint4*>(blk + kRBlock + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    *reinterpret_cast<uint4*>(img + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+    *reinterpret_cast<uint4*>(img + kRBlock + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
   }
+  __syncthreads();
+#pragma unroll 4
+  for (int i = t; i < 2 * kRBlock / 16; i += kP2Comps)
+    reinterpret_cast<uint4*>(blk)[i] = reinterpret_cast<const uint4*>(img)[i];
 }
 
 // ---------------------------------------------------------------------------
@@ -823,40 +837,45 @@ __global__ void __launch_bounds__(kP2Threads, 1) full_stats_kernel(const P2Param
 //   sig_outer[i][j] = Sxx[min(i,j)][max(i,j)] 2^(2 a2) + c_i mu~_j + mu~_i c_j
 //                     + Nk c_i c_j        (mu~ = Sx 2^a2, uncentred: full:213-228)
 // NaN everywhere on a device-side error.
-__global__ void full_reduce_kernel(const float* __restrict__ part, int slabs, int Kp, int ldp,
-                                   int K, int D, const float* __restrict__ cvec,
-                                   const int* __restrict__ amax, const int* __restrict__ err,
-                                   float* __restrict__ Nk, float* __restrict__ mu_acc,
-                                   float* __restrict__ sig, int accumulate) {
+__global__ void __launch_bounds__(256) full_reduce_kernel(
+    const float* __restrict__ part, int slabs, int Kp, int ldp, int K, int D,
+    const float* __restrict__ cvec, const int* __restrict__ amax, const int* __restrict__ err,
+    float* __restrict__ Nk, float* __restrict__ mu_acc, float* __restrict__ sig, int accumulate) {
+  // one block per component: its Nk and mu~ (sums over slabs) once in shared
+  // memory, then every sig_outer element from its pair feature
+  const int k = blockIdx.x;
   const int a2 = scale_exp_to(__int_as_float(*amax), 3);
   const double s1 = ldexp(1.0, a2), s2 = ldexp(1.0, 2 * a2);
   const bool bad = *err != 0;
   const float qnan = __int_as_float(0x7fc00000);
-  const int per_k = D * D + D + 1;
-  auto feat_sum = [&](int k, int f) -> double {
+  auto feat_sum = [&](int f) -> double {
     double s = 0.0;
     for (int sl = 0; sl < slabs; ++sl) s += part[((size_t)sl * Kp + k) * ldp + f];
     return s;
   };
-  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < (int64_t)K * per_k;
-       e += (int64_t)gridDim.x * blockDim.x) {
-    const int k = (int)(e / per_k), w = (int)(e % per_k);
-    const double n = feat_sum(k, one_feature(D));
+  __shared__ double s_m[kFullMaxD], s_n;
+  for (int i = threadIdx.x; i <= D; i += blockDim.x) {
+    if (i < D) s_m[i] = feat_sum(x_feature(i, D)) * s1;
+    else s_n = feat_sum(one_feature(D));
+  }
+  __syncthreads();
+  const double n = s_n;
+  const int per_k = D * D + D + 1;
+  for (int w = threadIdx.x; w < per_k; w += blockDim.x) {
     if (w == D * D + D) {
       const float v = bad ? qnan : (float)n;
       Nk[k] = accumulate ? Nk[k] + v : v;
     } else if (w >= D * D) {
       const int i = w - D * D;
-      const float v = bad ? qnan : (float)(feat_sum(k, x_feature(i, D)) * s1 + (double)cvec[i] * n);
+      const float v = bad ? qnan : (float)(s_m[i] + (double)cvec[i] * n);
       float* dst = mu_acc + (size_t)k * D + i;
       *dst = accumulate ? *dst + v : v;
     } else {
       const int i = w / D, j = w % D;
       const int a = min(i, j), b = max(i, j);
-      const double sxx = feat_sum(k, pair_feature(a, b, D)) * s2;
-      const double mi = feat_sum(k, x_feature(i, D)) * s1, mj = feat_sum(k, x_feature(j, D)) * s1;
+      const double sxx = feat_sum(pair_feature(a, b, D)) * s2;
       const double ci = cvec[i], cj = cvec[j];
-      const float v = bad ? qnan : (float)(sxx + ci * mj + mi * cj + n * ci * cj);
+      const float v = bad ? qnan : (float)(sxx + ci * s_m[j] + s_m[i] * cj + n * ci * cj);
       float* dst = sig + (size_t)k * D * D + w;
       *dst = accumulate ? *dst + v : v;
     }
@@ -955,7 +974,9 @@ cudaError_t full_tc_estep(const EstepArgs& a) {
   full_prep_kernel<<<pl.Kpad, 64, 0, st>>>(a.mu, a.smk, a.smd, a.cov, a.lpi, ws.cvec, a.K, a.D,
                                            pl.Dp, ws.lgroups, ws.bvec, ws.kconst);
   const int vec_ok = a.x_vec_ok();
-  const int sblocks = (int)std::min<int64_t>((pl.Npad + 7) / 8, 16 * kSmsFull);
+  const int sblocks =
+      (int)std::min<int64_t>((pl.Npad + 8 * kFullSplitRows - 1) / (8 * kFullSplitRows),
+                             16 * kSmsFull);
   with_xtype(a.xtype, [&](auto tx) {
     using TX = std::remove_const_t<std::remove_pointer_t<decltype(tx)>>;
     full_split_kernel<TX><<<sblocks, 256, 0, st>>>(a.x<TX>(), a.sxn, a.sxd, vec_ok, a.N, a.D,
@@ -1007,9 +1028,7 @@ cudaError_t full_tc_estep(const EstepArgs& a) {
   full_stats_kernel<<<pl.nfb * pl.ncb * pl.slabs, kP2Threads, sm2, st>>>(p2);
   profile_mark(true, st);
 
-  const int64_t total = (int64_t)a.K * (a.D * a.D + a.D + 1);
-  const int rblocks = (int)std::min<int64_t>((total + 255) / 256, 8 * kSmsFull);
-  full_reduce_kernel<<<rblocks, 256, 0, st>>>(ws.part, pl.slabs, pl.ncb * kP2Comps,
+  full_reduce_kernel<<<a.K, 256, 0, st>>>(ws.part, pl.slabs, pl.ncb * kP2Comps,
                                               pl.nfb * kP2Feat, a.K, a.D, ws.cvec, amax, ws.err,
                                               a.Nk, a.mu_acc, a.sig, (a.flags & 1u) ? 1 : 0);
   count_launches(7);
