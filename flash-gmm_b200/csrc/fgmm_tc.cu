@@ -1179,9 +1179,11 @@ SideStreams* side_streams() {
 template <class G>
 cudaError_t launch_fused(const TcPlan& pl, const TcParams& p, cudaStream_t stream, int mode = 0) {
   void (*kern)(const TcParams) = tc_fused_kernel<G, 0>;
-  if constexpr (G::kCluster <= 8) {  // the 16-CTA instantiations run the single pass only
+  if constexpr (G::kCluster <= 8) {
     if (mode == 1) kern = tc_fused_kernel<G, 1>;
     if (mode == 2) kern = tc_fused_kernel<G, 2>;
+  } else if (mode != 0) {
+    return cudaErrorInvalidValue;  // the 16-CTA instantiations run the single pass only
   }
   cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), pl.smem);
   if (e != cudaSuccess) return e;
