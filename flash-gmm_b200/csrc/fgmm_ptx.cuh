@@ -172,11 +172,6 @@ __device__ __forceinline__ float redux_max(float v) {
   asm("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(v));
   return r;
 }
-__device__ __forceinline__ uint32_t redux_add(uint32_t v) {
-  uint32_t r;
-  asm("redux.sync.add.u32 %0, %1, 0xffffffff;" : "=r"(r) : "r"(v));
-  return r;
-}
 __device__ __forceinline__ float ex2(float x) {
   float r;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
