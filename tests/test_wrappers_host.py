@@ -36,3 +36,14 @@ def test_full_shape_assert():
     with pytest.raises(AssertionError,
                        match=r"prec_chol must be \(K, D, D\)=\(3, 8, 8\), got \(3, 8\)"):
         flash_gmm_full_h100.flash_gmm_estep_full(X, mu, torch.zeros(3, 8), torch.zeros(3))
+
+
+def test_missing_library_raises_instead_of_falling_back(monkeypatch, tmp_path):
+    """Without the built library the binding raises: there is no CPU path."""
+    import _fgmm_lib as L
+    monkeypatch.setattr(L, "_lib", None)
+    monkeypatch.setattr(L, "LIB_PATH", str(tmp_path / "libflashgmm_sm100.so"))
+    with pytest.raises(RuntimeError, match="no fallback implementation"):
+        L.load()
+    with pytest.raises(RuntimeError, match="no fallback implementation"):
+        L.workspace_bytes(L.FGMM_VARIANT_ISO, 10, 4, 8)
