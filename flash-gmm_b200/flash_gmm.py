@@ -33,8 +33,7 @@ def flash_gmm_estep(
     fixed per kernel.  ``BLOCK_D`` keeps its meaning as the D bound checked by
     the reference (flash_gmm.py:189).
     """
-    N, D = X.shape
-    K = mu.shape[0]
+    _, D = X.shape
     assert D <= BLOCK_D, f"D={D} exceeds BLOCK_D={BLOCK_D}; increase BLOCK_D."
     assert X.is_cuda and mu.is_cuda, "Inputs must be on GPU."
     return _fgmm_lib.estep(_fgmm_lib.FGMM_VARIANT_ISO, X, mu, log_sigma_sq, log_pi)

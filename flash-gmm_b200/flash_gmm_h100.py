@@ -14,9 +14,6 @@ import torch
 
 import _fgmm_lib
 
-_LOG_2PI = 1.8378770664093453
-_LOG2_E = 1.4426950408889634   # 1 / ln(2)
-
 
 def flash_gmm_estep(
     X: torch.Tensor,
@@ -28,7 +25,5 @@ def flash_gmm_estep(
 
     Returns (logZ, Nk, mu_acc, sig_acc).
     """
-    N, D = X.shape
-    K = mu.shape[0]
     assert X.is_cuda and mu.is_cuda
     return _fgmm_lib.estep(_fgmm_lib.FGMM_VARIANT_ISO, X, mu, log_sigma_sq, log_pi)
