@@ -3,7 +3,6 @@ monotone log-likelihood and recovery of a separated mixture on CPU with the
 oracle E-step, the sharded loop on 2 gloo ranks, and (GPU) the library
 E-step against the oracle inside the same loop."""
 
-import math
 import os
 
 import numpy as np

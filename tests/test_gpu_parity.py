@@ -4,7 +4,6 @@ Every call goes through the drop-in entry points -> C ABI ->
 libflashgmm_sm100.so.  Tolerances: logZ elementwise rel 1e-5, statistics
 normwise rel 1e-4 (tests/parity.py)."""
 
-import math
 
 import numpy as np
 import pytest

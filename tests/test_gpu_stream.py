@@ -5,7 +5,6 @@ import numpy as np
 import pytest
 import torch
 
-import _fgmm_lib as L
 import gmm_data
 import gmm_stream as GS
 from oracle import gmm_oracle as O
