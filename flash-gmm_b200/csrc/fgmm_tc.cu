@@ -37,7 +37,7 @@
 //     exp2, warp sum (fp32 transpose-reduce over shuffles), combine the 4 warps
 //     that share a row, then exchange one (max, sum) pair per row and CTA
 //     over distributed shared memory -- no second distance pass;
-//   * r = p * 2^(m - logZ2); statistics GEMM  T[k, f] += sum_n R^T[k, n] F[n, f]
+//   * r = 2^(ll - logZ2); statistics GEMM  T[k, f] += sum_n R^T[k, n] F[n, f]
 //       A = R^T (fp16 hi/lo written to TMEM by the epilogue warps),
 //       B = the same F tile read MN-major, three passes again;
 //     Nk_k = sum r (and, iso, sum r*ll2 for sig) are per-thread sums
@@ -346,7 +346,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fused_kernel(const TcParams p)
   float* xsq = reinterpret_cast<float*>(whs + G::kWSmem);  // iso: [NS][R]
   float* red_m = xsq + NS * R;                       // [16 warps][RB]
   float* red_l = red_m + kEpiWarps * RB;             // [16 warps][RB]
-  float* scale_s = red_l + kEpiWarps * RB;           // [4 quadrants][R rows]
+  float* scale_s = red_l + kEpiWarps * RB;           // [R rows] logZ2 (4 R reserved)
   float* fin = scale_s + 4 * R;                      // [8][128] end-of-kernel sums
   constexpr int CL = G::kCluster;
   float2* xchg = reinterpret_cast<float2*>(fin + 8 * kComps);  // [2][CL][R]
@@ -554,8 +554,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fused_kernel(const TcParams p)
     // ------------------------------------------------------------- epilogue
     // Per tile: A) S^T -> ll, warp max / exp2 / warp sum per row;
     // B) combine the 4 lane quadrants per row and send one (max, sum) pair to
-    // every CTA of the cluster; C) combine the cluster's pairs -> logZ2 and a
-    // per-(quadrant, row) scale; D) r = p * scale, per-component sums, R^T
+    // every CTA of the cluster; C) combine the cluster's pairs -> logZ2
+    // per row; D) r = 2^(ll - logZ2), per-component sums, R^T
     // (fp16 hi/lo) into TMEM for the statistics GEMM.
     const float c0p = kc.x, ish = kc.y, c0 = kc.z;
     const float sck = ldexpf(1.0f, (G::kDiag ? 0 : xa) + (int)kc.w);  // S = S' 2^(a + s_k)
@@ -731,7 +731,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fused_kernel(const TcParams p)
           if constexpr (MODE == 1) p.logZ[row0 + Rw] = lz2;
           else p.logZ[row0 + Rw] = lz2 * 0.6931471805599453f;
         }
-        scale_s[g * R + Rw] = valid ? ex2(mg - lz2) : 0.f;
+        if (g == 0) scale_s[Rw] = valid ? lz2 : __int_as_float(0x7f800000);  // +inf: r = 0
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&ctl->e_bar[1][grp]);
@@ -739,8 +739,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fused_kernel(const TcParams p)
       if constexpr (MODE == 1) continue;  // LSE only: no statistics
       }
 
-      // ---- D: r = p * scale, per-component sums, R^T into TMEM (16 rows at a time)
-      const float* sc = scale_s + q * R + RB * cb;
+      // ---- D: r = 2^(ll - logZ2), per-component sums, R^T into TMEM (16 rows at a time)
+      const float* sc = scale_s + RB * cb;            // log2 normaliser per row
       float nk_t = 0.f, rll_t = 0.f;
       if (t >= 1 && !mbar_wait(&ctl->r_empty, (t - 1) & 1, ctl, p.err, 64)) break;
       tc_fence_after();
@@ -749,11 +749,18 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fused_kernel(const TcParams p)
         uint32_t rh[8], rl[8];
 #pragma unroll
         for (int i = 0; i < 16; i += 4) {
-          float4 s4 = make_float4(1.f, 1.f, 1.f, 1.f);
-          if constexpr (MODE != 2) s4 = *reinterpret_cast<const float4*>(sc + 16 * h + i);
           const int o = 16 * h + i;
-          const float r0 = pv[o + 0] * s4.x, r1 = pv[o + 1] * s4.y;
-          const float r2 = pv[o + 2] * s4.z, r3 = pv[o + 3] * s4.w;
+          float r0, r1, r2, r3;
+          if constexpr (MODE == 2) {
+            r0 = pv[o + 0]; r1 = pv[o + 1]; r2 = pv[o + 2]; r3 = pv[o + 3];
+          } else {
+            // r = 2^(ll - logZ2) from the distances kept in registers: p of
+            // phase A is dead after the row sums, which keeps the epilogue
+            // within its 96 registers (no spills) for one more exp2 per pair
+            const float4 z4 = *reinterpret_cast<const float4*>(sc + 16 * h + i);
+            r0 = ex2(ll[o + 0] - z4.x); r1 = ex2(ll[o + 1] - z4.y);
+            r2 = ex2(ll[o + 2] - z4.z); r3 = ex2(ll[o + 3] - z4.w);
+          }
           nk_t += (r0 + r1) + (r2 + r3);
           if constexpr (!G::kDiag) {
             rll_t = fmaf(r0, ll[o + 0], rll_t);
