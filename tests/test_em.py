@@ -118,7 +118,7 @@ def _sharded_fit_worker(rank, world, kind, port, q):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("kind", ["iso", "full"])
+@pytest.mark.parametrize("kind", ["iso", "diag", "full"])
 def test_sharded_fit_on_two_gloo_ranks_matches_single_process(kind):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
