@@ -94,17 +94,26 @@ def workspace_bytes(variant: int, N: int, K: int, D: int) -> int:
 
 
 # Per-(device, stream) workspace cache: grows monotonically, reused across
-# calls so a steady-state E-step loop performs no allocation.
+# calls so a steady-state E-step loop performs no allocation.  Guarded by
+# _lock (callers may run on several Python threads).  A buffer is only ever
+# used in the order of its stream; when it is replaced by a larger one, the
+# old buffer is marked as used by that stream (record_stream), so the caching
+# allocator does not hand its memory out before the stream's queued work on
+# it has finished.
 _ws_cache: dict = {}
 
 
 def _workspace(device: torch.device, nbytes: int) -> torch.Tensor:
-    key = (device.index, torch.cuda.current_stream(device).cuda_stream)
-    buf = _ws_cache.get(key)
-    if buf is None or buf.numel() < nbytes:
-        buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
-        _ws_cache[key] = buf
-    return buf
+    stream = torch.cuda.current_stream(device)
+    key = (device.index, stream.cuda_stream)
+    with _lock:
+        buf = _ws_cache.get(key)
+        if buf is None or buf.numel() < nbytes:
+            if buf is not None:
+                buf.record_stream(stream)
+            buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+            _ws_cache[key] = buf
+        return buf
 
 
 def _f32(t: torch.Tensor, device) -> torch.Tensor:

@@ -48,7 +48,9 @@ std::mutex g_mu;
 void* g_scratch_ptr[kMaxDevices] = {nullptr};
 
 // Device address of the scratch on the current device; set up once per
-// device.  Returns FGMM_OK or an FGMM_ERR_* code with the message recorded.
+// device.  cudaDeviceReset unloads the module that holds the array, so the
+// cached address is only valid until the process resets that device; a
+// caller that resets a device must not call this entry point afterwards.  Returns FGMM_OK or an FGMM_ERR_* code with the message recorded.
 int scratch_for_current_device(void** out) {
   int dev = -1;
   cudaError_t e = cudaGetDevice(&dev);
@@ -89,6 +91,11 @@ int fgmm_estep_iso_noalloc(const float* X, int64_t x_stride_n, int64_t x_stride_
                     reinterpret_cast<cudaStream_t>(stream)};
   if (N < 0 || K < 1 || D < 1 || D > fgmm::kGeneralMaxD)
     return fgmm::entry_run_estep(fgmm::kIso, a);  // reports the shape error
+  // The device check comes before the shape query, so a device that is not
+  // sm_100 reports FGMM_ERR_DEVICE whatever the shape.
+  std::string why;
+  const int dc = fgmm::entry_check_device(&why);
+  if (dc != FGMM_OK) return fgmm::entry_fail(dc, "fgmm_estep_iso_noalloc: " + why);
   // Scratch the path this call takes needs, exactly as fgmm_estep_iso sizes it.
   const bool fast = !(flags & FGMM_FLAG_FORCE_GENERAL) && fgmm::tc_supported(fgmm::kIso, a, nullptr);
   const size_t need = N == 0 ? 0
@@ -102,9 +109,6 @@ int fgmm_estep_iso_noalloc(const float* X, int64_t x_stride_n, int64_t x_stride_
              (long long)N, K, D, need, kScratchBytes);
     return fgmm::entry_fail(FGMM_ERR_WORKSPACE, buf);
   }
-  std::string why;
-  const int dc = fgmm::entry_check_device(&why);
-  if (dc != FGMM_OK) return fgmm::entry_fail(dc, "fgmm_estep_iso_noalloc: " + why);
   void* scratch = nullptr;
   const int sc = scratch_for_current_device(&scratch);
   if (sc != FGMM_OK) return sc;

@@ -13,9 +13,6 @@ import torch
 
 import _fgmm_lib
 
-_LOG_2PI = 1.8378770664093453
-_LOG2_E = 1.4426950408889634
-
 
 def flash_gmm_estep_diag(
     X: torch.Tensor,
