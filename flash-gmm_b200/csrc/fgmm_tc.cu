@@ -201,6 +201,8 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, SmemCtl*
   return mbar_wait_flag<kCluster>(b, parity, &ctl->abort_flag, err, code);
 }
 
+#include "fgmm_tc_iso.cuh"
+
 // ---------------------------------------------------------------------------
 // Isotropic prep, one block per component (Kpad blocks of 128 threads), in
 // the centred form m = mu - c (c = mean of the mu's, as for diag):
@@ -1049,6 +1051,7 @@ __global__ void tc_lse_combine_kernel(const float* __restrict__ lse_part, int nb
 
 struct TcPlan {
   bool diag;
+  bool iso = false;  // isotropic, K <= 1024, D <= 128: tc_iso_kernel
   int cfg, rows, C, Kpad, Dp, nfeat, nch, num_tiles, clusters, plen;
   bool big;  // 16-CTA clusters (one pass over 1024 < K <= 2048)
   size_t stage_bytes, smem;
@@ -1111,7 +1114,54 @@ int max_active_clusters(int C) {
   return n < 0 ? 0 : n;
 }
 
-TcPlan plan_tc(int variant, int64_t N, int K, int D, bool query_device) {
+int max_active_clusters_iso(int C) {
+  // 0: not queried yet
+  static std::atomic<int> cache[kIsoCluster + 1];
+  if (cache[C].load(std::memory_order_relaxed) == 0) {
+    ensure_dynamic_smem(reinterpret_cast<const void*>(tc_iso_kernel), IsoSmem::kDynamic);
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = C;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(C * 64, 1, 1);
+    cfg.blockDim = dim3(kIsoThreads, 1, 1);
+    cfg.dynamicSmemBytes = IsoSmem::kDynamic;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, tc_iso_kernel, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = kSms / C;
+    }
+    cache[C].store(std::min(n, kSms / C), std::memory_order_relaxed);
+  }
+  return cache[C].load(std::memory_order_relaxed);
+}
+
+cudaError_t launch_iso(const TcPlan& pl, const TcParams& p, cudaStream_t stream) {
+  cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(tc_iso_kernel), pl.smem);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = pl.C;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(pl.C * pl.clusters, 1, 1);
+  cfg.blockDim = dim3(kIsoThreads, 1, 1);
+  cfg.dynamicSmemBytes = pl.smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, tc_iso_kernel, p);
+}
+
+// single_pass = false: the plan of one component block of the K > 2048 path
+// (the two-phase fused kernel, never tc_iso_kernel).
+TcPlan plan_tc(int variant, int64_t N, int K, int D, bool query_device,
+               bool single_pass = true) {
   TcPlan pl;
   pl.diag = variant == kDiag;
   pl.cfg = pl.diag ? (D > kMaxDDiag ? kCfgDiagWide : kCfgDiag)
@@ -1130,8 +1180,12 @@ TcPlan plan_tc(int variant, int64_t N, int K, int D, bool query_device) {
   const int nch = pl.nch, C = pl.C;
   pl.big = pl.C > 8;
   pl.smem = with_cfg(pl.cfg, [nch](auto g) { return tc_smem_bytes<decltype(g)>(nch); }, pl.big);
+  pl.iso = single_pass && !pl.diag && pl.cfg == kCfgIso && !pl.big;
+  if (pl.iso) pl.smem = IsoSmem::kDynamic;
   int maxc = kSms / pl.C;
-  if (query_device && pl.C <= kMaxCluster)
+  if (query_device && pl.iso)
+    maxc = max_active_clusters_iso(C);
+  else if (query_device && pl.C <= kMaxCluster)
     maxc = with_cfg(pl.cfg, [C](auto g) { return max_active_clusters<decltype(g)>(C); }, pl.big);
   pl.clusters = std::max(1, std::min(maxc, pl.num_tiles));
   return pl;
@@ -1241,7 +1295,7 @@ MbWs carve_mb(void* base, int variant, int64_t N, int K, int D, bool query_devic
   m.nb = (K + kBlockComps - 1) / kBlockComps;
   for (int b = 0; b < m.nb; ++b) {
     m.Kb[b] = std::min(kBlockComps, K - b * kBlockComps);
-    m.pl[b] = plan_tc(variant, N, m.Kb[b], D, query_device);
+    m.pl[b] = plan_tc(variant, N, m.Kb[b], D, query_device, false);
   }
   const TcPlan& p0 = m.pl[0];
   m.npad = (int64_t)p0.num_tiles * p0.rows;
@@ -1557,7 +1611,10 @@ cudaError_t tc_estep(int variant, const EstepArgs& a) {
     p.num_tiles = pc.num_tiles;
     p.logZ = a.logZ + row0;
     p.part = part + (size_t)part_clusters * pl.Kpad * pl.plen;
-    e = with_cfg(pl.cfg, [&](auto g) { return launch_fused<decltype(g)>(pc, p, hi); }, pl.big);
+    if (pl.iso)
+      e = launch_iso(pc, p, hi);
+    else
+      e = with_cfg(pl.cfg, [&](auto g) { return launch_fused<decltype(g)>(pc, p, hi); }, pl.big);
     if (e != cudaSuccess) return e;
     part_clusters += pc.clusters;
     ++launches;

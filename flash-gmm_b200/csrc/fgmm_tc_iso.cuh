@@ -1,0 +1,451 @@
+// Isotropic E-step kernel for K <= 1024 components and D <= 128 features
+// (the reference's headline shape, flash_gmm.py:50-166 and
+// flash_gmm_h100.py:85-243): one launch computes logZ and the per-cluster
+// partial statistics, with the distance GEMM evaluated once per
+// (row, component) pair.  Included by fgmm_tc.cu (namespace fgmm::{anon}),
+// whose split, prep and reduce kernels it shares.
+//
+// Orientation: a CTA owns 128 components (the TMEM lanes); a cluster of
+// C = ceil(K/128) CTAs covers all components and walks the same 128-row
+// tiles.  W (fp16 hi/lo) is the resident TMEM A operand, so the distance
+// MMAs read only the row tile from shared memory.
+//
+// Per 128-row tile j (S buffer b = j & 1), for each 32-row block and each
+// quadrant of 32 components (one epilogue warp; lane = component):
+//   MMA dist(j):  S[b] = W_lo X_hi + W_hi X_lo + W_hi X_hi   (24 MMAs, N = 128)
+//   A   ll = S 2^(a+s_k) + c0' - ish |x-c|^2 (log2 units) for the block's 32
+//       rows; per row the quadrant's max m (redux.sync.max) and the sum of
+//       p = 2^(ll - m) as fixed point (p 2^22 rounded, added with
+//       redux.sync.add.u32: at most 2^-18 relative error in the sum);
+//   B   the four quadrants' pairs (shared memory) -> the CTA's (max, sum)
+//       per row, sent to every CTA of the cluster (st.async); each CTA forms
+//       the row's log2-normaliser lz2 = M + log2 S;
+//   C   rows where the quadrant's max is within 2^25 of lz2:
+//       r = 2^(ll - lz2), split into fp16 hi/lo words and written to TMEM
+//       over the block's own S columns (hi in the first 16, lo in the next
+//       16); every other row's responsibilities are below 2^-25, which
+//       rounds to zero in fp16, and are written as zeros; Nk and sum r ll
+//       per component are per-thread sums (thread = component);
+//   MMA stats(j): T += R^T X  (3 terms r_lo x_hi + r_hi x_lo + r_hi x_hi,
+//       24 MMAs; A = R^T in TMEM, B = the row tile read MN-major).
+// The selection in C is made for 32 rows at once (lane = row,
+// vote.ballot), so the work follows the number of rows a quadrant takes part
+// in: all of them for overlapping components, about one in 32 when each row
+// belongs to one well separated component.  Up to four selected rows of a
+// block are re-read with single-column TMEM loads issued together; more,
+// with one 32-column load.  The results do not depend on the selection
+// beyond the stated cut-offs.
+//
+// Both GEMMs carry 22-bit operands (fp16 hi/lo, exact power-of-two scaling):
+// logZ is held to 1e-5 and the statistics to 1e-4 also where the rows of a
+// component nearly cancel.  The MMA warp issues dist(j+1) and stats(j-1)
+// while the epilogue works on tile j: S is double-buffered and the tensor
+// pipe executes in issue order, so dist(j+2) (into S[b]) follows stats(j),
+// which read R^T from S[b].
+//
+// TMEM (512 columns): W hi [0,64) lo [64,128) | T [128,256) | S0 [256,384) |
+// S1 [384,512).  Warps 0-15: epilogue (warp w: lane quadrant w & 3, row
+// block w >> 2); warp 16 loads row tiles (one bulk copy per stage); warp 17
+// issues MMAs.  Every wait is bounded; a timeout sets the error word and the
+// kernel leaves its loops (the reduction then writes NaN).
+
+constexpr int kIsoEpiWarps = 16;
+constexpr int kIsoWarps = kIsoEpiWarps + 2;      // 18
+constexpr int kIsoThreads = kIsoWarps * 32;      // 576
+constexpr int kIsoLoadWarp = kIsoEpiWarps;       // 16
+constexpr int kIsoMmaWarp = kIsoEpiWarps + 1;    // 17
+constexpr int kIsoStages = 3;
+constexpr int kIsoRows = 128;
+constexpr int kIsoMaxD = 128;
+constexpr int kIsoCluster = 8;
+constexpr uint32_t kIsoColW = 0, kIsoColT = 128, kIsoColS = 256;
+// fixed-point row sums: q = round(p 2^22) read from the bits of p 2^22 + 2^23
+constexpr float kFixScale = 4194304.0f, kFixBias = 8388608.0f;
+constexpr uint32_t kFixBits32 = 32u * 0x4B000000u;  // 32 biases, mod 2^32
+constexpr float kRespCut = 25.f;  // C: quadrant max below lz2 - 25: r = 0
+
+struct __align__(8) IsoCtl {
+  uint64_t xfull[kIsoStages];
+  uint64_t xempty[kIsoStages];
+  uint64_t s_full[2];
+  uint64_t r_full[2];
+  uint64_t t_done;
+  uint64_t xchg_full[2][4];  // [tile parity][row block]
+  uint64_t e_bar[2][4];      // [sync point][row block]: one arrival per quadrant warp
+  uint64_t e_end;
+  uint32_t tmem_base;
+  volatile int abort_flag;
+};
+
+// Shared-memory carve-up (offsets from the 1024-aligned base).
+struct IsoSmem {
+  static constexpr int kStageMax = 2 * 2 * kIsoRows * 128;           // 64 KB
+  static constexpr int kXs = 0;
+  static constexpr int kXsq = kXs + kIsoStages * kStageMax;          // [NS][128] f32
+  static constexpr int kRed = kXsq + kIsoStages * kIsoRows * 4;      // [4 blk][4 q][32] f2
+  static constexpr int kZ = kRed + 16 * 32 * 8;                      // [4 blk][32] f32 lz2
+  static constexpr int kFin = kZ + 4 * 32 * 4;                       // [8][128] f32
+  static constexpr int kXchg = kFin + 8 * kComps * 4;                // [2][8][128] f2
+  static constexpr int kCtl = kXchg + 2 * kIsoCluster * kIsoRows * 8;
+  static constexpr int kBytes = kCtl + (int)sizeof(IsoCtl);
+  static constexpr size_t kDynamic = 1024 + (size_t)kBytes;          // alignment slack
+};
+static_assert(IsoSmem::kDynamic <= 232448, "shared memory budget");
+
+__device__ __forceinline__ bool iso_wait(uint64_t* b, uint32_t parity, IsoCtl* ctl, int* err,
+                                         int code) {
+  return mbar_wait_flag<false>(b, parity, &ctl->abort_flag, err, code);
+}
+
+__global__ void __launch_bounds__(kIsoThreads, 1) tc_iso_kernel(const TcParams p) {
+  constexpr int NS = kIsoStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  const int stage_bytes = 2 * p.nch * kIsoRows * 128;  // hi + lo
+  uint8_t* xs = smem + IsoSmem::kXs;
+  float* xsq = reinterpret_cast<float*>(smem + IsoSmem::kXsq);
+  float2* red = reinterpret_cast<float2*>(smem + IsoSmem::kRed);
+  float* zrow = reinterpret_cast<float*>(smem + IsoSmem::kZ);
+  float* fin = reinterpret_cast<float*>(smem + IsoSmem::kFin);
+  float2* xchg = reinterpret_cast<float2*>(smem + IsoSmem::kXchg);  // [slot][CTA][row]
+  IsoCtl* ctl = reinterpret_cast<IsoCtl*>(smem + IsoSmem::kCtl);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const int cluster_id = blockIdx.x / p.C;
+  const int num_clusters = gridDim.x / p.C;
+  const int ntiles = (p.num_tiles - cluster_id + num_clusters - 1) / num_clusters;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&ctl->xfull[s], 1);   // loader's arrive.expect_tx + bulk-copy bytes
+      mbar_init(&ctl->xempty[s], 1);  // commit after the tile's statistics MMAs
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&ctl->s_full[b], 1);             // commit after the distance MMAs
+      mbar_init(&ctl->r_full[b], kIsoEpiWarps);  // every epilogue warp wrote its R^T
+    }
+    mbar_init(&ctl->t_done, 1);
+    for (int cb = 0; cb < 4; ++cb) {
+      mbar_init(&ctl->xchg_full[0][cb], 1);  // local arrive.expect_tx + peers' st.async bytes
+      mbar_init(&ctl->xchg_full[1][cb], 1);
+      mbar_init(&ctl->e_bar[0][cb], 4);
+      mbar_init(&ctl->e_bar[1][cb], 4);
+    }
+    mbar_init(&ctl->e_end, kIsoEpiWarps);
+    ctl->abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) {  // all 512 TMEM columns (one CTA per SM)
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(
+                     smem_u32(&ctl->tmem_base))
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  const int q = warp & 3, cb = (warp >> 2) & 3;  // epilogue: lane quadrant, row block
+  const int kl = q * 32 + lane;                  // local component (TMEM lane)
+  const int kg = (int)rank * kComps + kl;        // global component
+  float4 kc = make_float4(-1e30f, 0.f, -1e30f, 0.f);
+  if (warp < kIsoEpiWarps) kc = p.consts[kg];
+  const int xa = x_scale_exp<false>(__int_as_float(*p.xscale));  // x' = (x - c) 2^-xa
+
+  // zero the stages once: padding features of a partial last chunk stay 0
+  for (int i = threadIdx.x; i < NS * stage_bytes / 16; i += kIsoThreads)
+    reinterpret_cast<uint4*>(xs)[i] = make_uint4(0u, 0u, 0u, 0u);
+  fence_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = ctl->tmem_base;
+
+  // W rows into TMEM (A operand of the distance GEMM), lane = component
+  if (warp < 4) {
+    const uint4* wh = reinterpret_cast<const uint4*>(p.Whi + (size_t)kg * p.nfeat);
+    const uint4* wl = reinterpret_cast<const uint4*>(p.Wlo + (size_t)kg * p.nfeat);
+    const uint32_t lb = (uint32_t)(q * 32) << 16;
+    for (int s = 0; s < p.nfeat / 16; ++s) {
+      uint32_t v[8];
+      uint4 a = wh[2 * s], c = wh[2 * s + 1];
+      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = c.x; v[5] = c.y; v[6] = c.z; v[7] = c.w;
+      tmem_st8(tmem + lb + kIsoColW + 8 * s, v);
+      a = wl[2 * s];
+      c = wl[2 * s + 1];
+      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = c.x; v[5] = c.y; v[6] = c.z; v[7] = c.w;
+      tmem_st8(tmem + lb + kIsoColW + 64 + 8 * s, v);
+    }
+    tmem_wait_st();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // peers' barriers are initialised before any remote arrive
+  tc_fence_after();
+
+  if (warp == kIsoMmaWarp) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t id_dist = idesc_f16(kIsoRows, false);
+      const uint32_t id_stat = idesc_f16(64 * p.nch, true);
+      const int ksd = p.nfeat / 16;
+      const uint32_t lo_off = (uint32_t)(p.nch * kIsoRows * 128);
+      auto issue_stats = [&](int jj) {
+        const uint32_t xhi = smem_u32(xs + (jj % NS) * stage_bytes), xlo = xhi + lo_off;
+        const uint32_t rcol = kIsoColS + 128u * (uint32_t)(jj & 1);
+        // terms r_lo x_hi, r_hi x_lo, r_hi x_hi; K-step s = rows 16s..16s+15 =
+        // row block s/2, columns 8 (s & 1) of its hi (+0) / lo (+16) words
+        for (int t = 0; t < 3; ++t) {
+          const uint32_t aoff = t == 0 ? 16u : 0u;
+          const uint32_t bb = t == 1 ? xlo : xhi;
+#pragma unroll
+          for (int s = 0; s < kIsoRows / 16; ++s)
+            mma_ts(tmem + kIsoColT, tmem + rcol + 32 * (s >> 1) + 8 * (s & 1) + aoff,
+                   desc_mnmajor(bb + s * 2048, kIsoRows * 128), id_stat,
+                   (jj == 0 && t == 0 && s == 0) ? 0u : 1u);
+        }
+        tc_commit(&ctl->xempty[jj % NS]);
+      };
+      bool ok = true;
+      for (int j = 0; j < ntiles; ++j) {
+        const int st = j % NS;
+        if (!iso_wait(&ctl->xfull[st], (j / NS) & 1, ctl, p.err, 1)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t xhi = smem_u32(xs + st * stage_bytes), xlo = xhi + lo_off;
+        const uint32_t scol = kIsoColS + 128u * (uint32_t)(j & 1);
+        // terms W_lo x_hi, W_hi x_lo, W_hi x_hi (smallest magnitudes first)
+        for (int t = 0; t < 3; ++t) {
+          const uint32_t acol = kIsoColW + (t == 0 ? 64u : 0u);
+          const uint32_t bb = t == 1 ? xlo : xhi;
+          for (int s = 0; s < ksd; ++s)
+            mma_ts(tmem + scol, tmem + acol + 8 * s,
+                   desc_kmajor(bb + (s >> 2) * (kIsoRows * 128) + (s & 3) * 32), id_dist,
+                   (t == 0 && s == 0) ? 0u : 1u);
+        }
+        tc_commit(&ctl->s_full[j & 1]);
+        if (j >= 1) {
+          if (!iso_wait(&ctl->r_full[(j - 1) & 1], ((j - 1) >> 1) & 1, ctl, p.err, 4)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_stats(j - 1);
+        }
+      }
+      if (ok && ntiles >= 1 &&
+          iso_wait(&ctl->r_full[(ntiles - 1) & 1], ((ntiles - 1) >> 1) & 1, ctl, p.err, 4)) {
+        tc_fence_after();
+        issue_stats(ntiles - 1);
+        tc_commit(&ctl->t_done);
+      }
+    }
+    __syncwarp();
+  } else if (warp == kIsoLoadWarp) {
+    // ------------------------------------------------------------ row-tile loader
+    if (lane == 0) {
+      const uint32_t tx = (uint32_t)stage_bytes + kIsoRows * 4u;
+      for (int j = 0; j < ntiles; ++j) {
+        const int st = j % NS;
+        const int64_t tile = cluster_id + (int64_t)j * num_clusters;
+        if (!iso_wait(&ctl->xempty[st], ((j / NS) & 1) ^ 1, ctl, p.err, 8)) break;
+        mbar_arrive_expect_tx(&ctl->xfull[st], tx);
+        bulk_g2s(smem_u32(xs + st * stage_bytes), p.xsplit + tile * stage_bytes,
+                 (uint32_t)stage_bytes, &ctl->xfull[st]);
+        bulk_g2s(smem_u32(xsq + st * kIsoRows), p.xsq + tile * kIsoRows, kIsoRows * 4u,
+                 &ctl->xfull[st]);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------- epilogue
+    const float c0p = kc.x, ish = kc.y, c0 = kc.z;
+    const float sck = ldexpf(1.0f, xa + (int)kc.w);  // ll = S' 2^(a + s_k) + ...
+    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    float nk_acc = 0.f, rll_acc = 0.f;
+    const int g = lane >> 3;            // phase B: lane quadrant / peer group
+    const int rr = 8 * q + (lane & 7);  // phase B: row of the block this lane combines
+    float2* rq = red + cb * 128;        // [4 q][32 rows] quadrant (max, fixed-point sum)
+    auto sync_block = [&](int e, int j, int code) -> bool {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ctl->e_bar[e][cb]);
+      return iso_wait(&ctl->e_bar[e][cb], j & 1, ctl, p.err, code);
+    };
+    for (int j = 0; j < ntiles; ++j) {
+      const int b = j & 1, st = j % NS, slot = j & 1;
+      const int64_t row0 = (int64_t)(cluster_id + (int64_t)j * num_clusters) * kIsoRows;
+      const uint32_t scol = tmem + lane_base + kIsoColS + 128u * (uint32_t)b + 32u * (uint32_t)cb;
+      const float* xq = xsq + st * kIsoRows + 32 * cb;
+      const int xrow = 32 * cb + rr;
+      if (!iso_wait(&ctl->s_full[b], (j >> 1) & 1, ctl, p.err, 16)) break;
+      if (!iso_wait(&ctl->xfull[st], (j / NS) & 1, ctl, p.err, 4096)) break;
+      tc_fence_after();
+      // ---- A: per row, the quadrant's max m, p = 2^(ll - m) and the sum of p
+      // (fixed point); lane 0 records (m, sum bits)
+      {
+        uint32_t sv[32];
+        tmem_ld32(scol, sv);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) {
+          const float4 s4 = *reinterpret_cast<const float4*>(xq + i);
+          const float xv[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            const float ll = fmaf(__uint_as_float(sv[i + t]), sck, fmaf(-ish, xv[t], c0p));
+            const float m = redux_max(ll);
+            const uint32_t su =
+                redux_add_u32(__float_as_uint(fmaf(ex2(ll - m), kFixScale, kFixBias)));
+            if (lane == 0) rq[q * 32 + i + t] = make_float2(m, __uint_as_float(su));
+          }
+        }
+      }
+      __syncwarp();
+      const float mq = rq[q * 32 + lane].x;  // this quadrant's max of row `lane`
+      if (!sync_block(0, j, 256)) break;
+      // ---- B: row rr (lane group g = quadrant): the CTA's (max, sum) to every
+      // CTA of the cluster (group g sends to peers g and g + 4); the peers'
+      // pairs -> the row's log2-normaliser lz2 and logZ
+      {
+        const float2 e = rq[g * 32 + rr];
+        const float mg = e.x;
+        const float sg = (float)(__float_as_uint(e.y) - kFixBits32) * (1.0f / kFixScale);
+        float M = fmaxf(mg, __shfl_xor_sync(0xffffffffu, mg, 8));
+        M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, 16));
+        float L = sg * ex2(mg - M);
+        L += __shfl_xor_sync(0xffffffffu, L, 8);
+        L += __shfl_xor_sync(0xffffffffu, L, 16);
+        float2* xb = xchg + slot * kIsoCluster * kIsoRows;
+        const uint32_t my_slot = smem_u32(&xb[rank * kIsoRows + xrow]);
+        const uint32_t my_bar = smem_u32(&ctl->xchg_full[slot][cb]);
+        if (q == 0 && lane == 0)
+          mbar_arrive_expect_tx(&ctl->xchg_full[slot][cb], (uint32_t)(p.C * 32 * 8));
+#pragma unroll
+        for (int jj = 0; jj < 2; ++jj)
+          if (g + 4 * jj < p.C)
+            st_async_f2(map_to_cta(my_slot, g + 4 * jj), M, L, map_to_cta(my_bar, g + 4 * jj));
+        if (!mbar_wait_flag<true>(&ctl->xchg_full[slot][cb], (j >> 1) & 1, &ctl->abort_flag,
+                                  p.err, 32))
+          break;
+        const float2 e0 = g < p.C ? xb[g * kIsoRows + xrow] : make_float2(-3e38f, 0.f);
+        const float2 e1 = g + 4 < p.C ? xb[(g + 4) * kIsoRows + xrow] : make_float2(-3e38f, 0.f);
+        float GM = fmaxf(e0.x, e1.x);
+        GM = fmaxf(GM, __shfl_xor_sync(0xffffffffu, GM, 8));
+        GM = fmaxf(GM, __shfl_xor_sync(0xffffffffu, GM, 16));
+        float GL = e0.y * ex2(e0.x - GM) + e1.y * ex2(e1.x - GM);
+        GL += __shfl_xor_sync(0xffffffffu, GL, 8);
+        GL += __shfl_xor_sync(0xffffffffu, GL, 16);
+        const float lz2 = GM + lg2(GL);
+        const bool valid = row0 + xrow < p.N;
+        if (valid && rank == 0 && g == 0) p.logZ[row0 + xrow] = lz2 * 0.6931471805599453f;
+        if (g == 0) zrow[cb * 32 + rr] = valid ? lz2 : __int_as_float(0x7f800000);  // +inf: r = 0
+      }
+      if (!sync_block(1, j, 512)) break;
+
+      // ---- C: responsibilities of the rows this quadrant takes part in;
+      // R^T (fp16 hi | lo) over the block's own S columns, zeros elsewhere
+      {
+        const float lz = zrow[cb * 32 + lane];
+        const uint32_t need = __ballot_sync(0xffffffffu, mq >= lz - kRespCut);
+        const uint32_t pairs = (need | (need >> 1)) & 0x55555555u;
+        float nk_t = 0.f, rll_t = 0.f;
+        auto resp = [&](int i, float s) {
+          const float ll = fmaf(s, sck, fmaf(-ish, xq[i], c0p));
+          const float r = ex2(ll - __shfl_sync(0xffffffffu, lz, i));
+          nk_t += r;
+          rll_t = fmaf(r, ll, rll_t);
+          return r;
+        };
+        if (__popc(pairs) <= 2) {
+          // at most two column pairs: read their distances, zero the block's
+          // words (R^T replaces S in place), then write the pairs' words
+          int i0[2];
+          uint32_t v[4];
+          uint32_t pm = pairs;
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            i0[u] = pm ? __ffs(pm) - 1 : -1;
+            pm &= pm - 1;
+            const uint32_t c = i0[u] >= 0 ? (uint32_t)i0[u] : 0u;
+            v[2 * u] = tmem_ld1(scol + c);
+            v[2 * u + 1] = tmem_ld1(scol + c + 1u);
+          }
+          tmem_wait_ld();
+          const uint32_t z = 0u;
+          const uint32_t zv[16] = {z, z, z, z, z, z, z, z, z, z, z, z, z, z, z, z};
+          tmem_st16(scol, zv);
+          tmem_st16(scol + 16, zv);
+          if (pairs) {
+            tmem_wait_st();  // the zeros land before the words that replace them
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              if (i0[u] < 0) continue;
+              const int i = i0[u];
+              const float r0 = ((need >> i) & 1u) ? resp(i, __uint_as_float(v[2 * u])) : 0.f;
+              const float r1 =
+                  ((need >> (i + 1)) & 1u) ? resp(i + 1, __uint_as_float(v[2 * u + 1])) : 0.f;
+              uint32_t h, l;
+              split2(r0, r1, h, l);
+              tmem_st1(scol + (uint32_t)(i >> 1), h);
+              tmem_st1(scol + 16u + (uint32_t)(i >> 1), l);
+            }
+          }
+        } else {
+          uint32_t sv[32];
+          tmem_ld32(scol, sv);
+          tmem_wait_ld();
+          uint32_t hv[16], lv[16];
+#pragma unroll
+          for (int c = 0; c < 16; ++c) {
+            const float r0 = ((need >> (2 * c)) & 1u) ? resp(2 * c, __uint_as_float(sv[2 * c])) : 0.f;
+            const float r1 =
+                ((need >> (2 * c + 1)) & 1u) ? resp(2 * c + 1, __uint_as_float(sv[2 * c + 1])) : 0.f;
+            split2(r0, r1, hv[c], lv[c]);
+          }
+          tmem_st16(scol, hv);
+          tmem_st16(scol + 16, lv);
+        }
+        nk_acc += nk_t;
+        rll_acc += rll_t;
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ctl->r_full[b]);
+    }
+
+    // End: statistics accumulator -> per-cluster partials {Nk, sig, T 2^a}.
+    fin[cb * kComps + kl] = nk_acc;
+    fin[(4 + cb) * kComps + kl] = rll_acc;
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&ctl->e_end);
+    const bool ok = !ctl->abort_flag && ntiles >= 1 &&
+                    iso_wait(&ctl->e_end, 0, ctl, p.err, 1024) &&
+                    iso_wait(&ctl->t_done, 0, ctl, p.err, 128);
+    float* out = p.part + ((size_t)cluster_id * p.C * kComps + kg) * p.plen;
+    if (ok) {
+      tc_fence_after();
+      if (32 * cb < 64 * p.nch) {
+        uint32_t tv[32];
+        tmem_ld32(tmem + lane_base + kIsoColT + 32 * cb, tv);
+        tmem_wait_ld();
+        for (int i = 0; i < 32; ++i) {
+          const int f = 32 * cb + i;
+          if (f < p.D) out[2 + f] = ldexpf(__uint_as_float(tv[i]), xa);  // T = T' 2^a
+        }
+      }
+      if (cb == 0) {
+        const float nk = fin[kl] + fin[kComps + kl] + fin[2 * kComps + kl] + fin[3 * kComps + kl];
+        const float rl = fin[4 * kComps + kl] + fin[5 * kComps + kl] + fin[6 * kComps + kl] +
+                         fin[7 * kComps + kl];
+        out[0] = nk;
+        out[1] = ish > 0.f ? (c0 * nk - rl) / ish : 0.f;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
+  }
+  cluster_sync_all();
+}

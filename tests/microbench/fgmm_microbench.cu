@@ -288,7 +288,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(128, 1)
 
 // Issue-rate kernel: every thread runs `iters` rounds of 8 independent
 // operations of kind `op` (0 ex2.approx.ftz.f32, 1 ex2.approx.f16x2,
-// 2 fma.rn.f32, 3 one ex2.f32 per 4 FFMA).  out[cta] = cycles.
+// 2 fma.rn.f32, 3 two ex2.f32 and six FFMA, 4 redux.sync.add.u32,
+// 5 redux.sync.max.f32, 6 shfl.sync.bfly).  out[cta] = cycles.
 __global__ void __launch_bounds__(1024, 1) issue_rate_kernel(int iters, int op, long long* out,
                                                              float* sink) {
   float v[8];
@@ -312,6 +313,21 @@ __global__ void __launch_bounds__(1024, 1) issue_rate_kernel(int iters, int op, 
 #pragma unroll
       for (int i = 0; i < 8; ++i)
         asm volatile("fma.rn.f32 %0, %0, 0f3F7FF000, 0f3A800000;" : "+f"(v[i]));
+  } else if (op == 4) {
+    for (int it = 0; it < iters; ++it)
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        asm volatile("redux.sync.add.u32 %0, %0, 0xffffffff;" : "+r"(h[i]));
+  } else if (op == 5) {
+    for (int it = 0; it < iters; ++it)
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        asm volatile("redux.sync.max.f32 %0, %0, 0xffffffff;" : "+f"(v[i]));
+  } else if (op == 6) {
+    for (int it = 0; it < iters; ++it)
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        asm volatile("shfl.sync.bfly.b32 %0, %0, 16, 0x1f, 0xffffffff;" : "+r"(h[i]));
   } else {
     for (int it = 0; it < iters; ++it) {
 #pragma unroll
