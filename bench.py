@@ -19,12 +19,14 @@ reference's headline shape N=1M, K=1024, D=128.
   chunks with FGMM_FLAG_ACCUMULATE, then one all-reduce.
 * ``--impl reference``: the reference's algorithm on the host cores -- the
   CPU restatement in oracle/ (the reference itself is Triton-only and has no
-  CPU implementation of the path), fp32 torch-CPU, chunked, all threads, on a
-  bounded sample of rows per step.  Rank 0 runs it; other ranks exit.
+  CPU implementation of the path), fp32 torch-CPU, chunked, all physical
+  cores, the workload's full row count per step (C2: 1M rows).  Rank 0 runs
+  it; other ranks exit.
 
 Timing: W untimed warm-up steps, then K steps between a barrier +
 cuda.synchronize on both sides, CUDA events on the launching stream (one
-pair per step), max over ranks.  Inputs of C2/C3/C5 (384-512 MB of X per
+pair per step); ms_per_step is the median step (the mean is reported too),
+max over ranks.  Inputs of C2/C3/C5 (384-512 MB of X per
 rank) exceed the 126 MB L2; for C4 (64 MB) a 256 MB buffer is rewritten
 between the timed steps.
 """
@@ -59,7 +61,7 @@ SEED = 1234
 WORKLOADS = {
     "c2": dict(kind="iso", rows=1_000_000, K=1024, D=128, scaling="weak",
                title="C2 isotropic E-step N=1M K=1024 D=128 per GPU",
-               profile="tc_fused_iso_c2.txt", kernel="tc_fused_kernel<iso> "
+               profile="tc_iso_c2.txt", kernel="tc_iso_kernel "
                "(fused distance/LSE/statistics, tcgen05)"),
     "c3": dict(kind="diag", rows=1_000_000, K=1024, D=96, scaling="weak",
                title="C3 diagonal-covariance E-step N=1M K=1024 D=96 per GPU",
@@ -71,7 +73,7 @@ WORKLOADS = {
                "full_stats_kernel (the two tensor-core passes and the responsibilities between)"),
     "c5": dict(kind="iso", rows=ROWS_C5, K=1024, D=128, scaling="strong",
                title="C5 streaming isotropic E-step N=100M K=1024 D=128 total",
-               profile="tc_fused_iso_c2.txt", kernel="tc_fused_kernel<iso> "
+               profile="tc_iso_c2.txt", kernel="tc_iso_kernel "
                "(fused distance/LSE/statistics, tcgen05), the last row chunk of a step"),
 }
 
@@ -91,6 +93,25 @@ def load_peaks():
     except Exception:
         return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
                 "source": "fallback"}
+
+
+def measured_tf32_tflops():
+    """Dense TF32 matmul rate measured on this pool's B200 by
+    tests/microbench/microbench.py (committed summary profiles/mma_cost.txt),
+    or None."""
+    v = profile_traffic("mma_cost.txt", "tf32_tflops")
+    return v if v and v > 0 else None
+
+
+def host_cores():
+    """(physical, logical) host cores."""
+    logical = os.cpu_count() or 1
+    try:
+        import psutil
+        phys = psutil.cpu_count(logical=False) or logical
+    except Exception:
+        phys = logical
+    return phys, logical
 
 
 def profile_traffic(profile: str, name: str = "dram_bytes_per_launch"):
@@ -185,11 +206,12 @@ def cpu_port(kind: str):
     return getattr(O, CPU_PORT[kind])
 
 
-def cpu_reference_rate(kind, X, mu, cov, lpi, budget_s: float, chunk: int = 16384):
+def cpu_reference_rate(kind, X, mu, cov, lpi, budget_s: float, chunk: int = 16384,
+                       threads: int = 0):
     """Pairs/s of the CPU restatement (fp32 torch-CPU) over a bounded sample."""
     import torch
     fn = cpu_port(kind)
-    torch.set_num_threads(os.cpu_count() or 1)
+    torch.set_num_threads(threads or os.cpu_count() or 1)
     n_done = 0
     t0 = time.perf_counter()
     start = 0
@@ -215,39 +237,46 @@ def host_sample(w: dict, rows: int):
 
 
 def run_reference(args):
+    """The reference arm: the reference's algorithm on the host cores (the
+    reference is Triton-only), the full workload of --workload per step (C2:
+    all 1M rows), all physical cores.  Warm-up steps run on a 16K-row slice
+    (they only load the code paths); the K timed steps are full."""
     world, rank, _ = dist_setup()
     if rank != 0:
         return 0
     import torch
     w = WORKLOADS[args.workload]
     K = w["K"]
-    cores = os.cpu_count() or 1
-    torch.set_num_threads(cores)
-    rows = {"iso": 65536, "diag": 65536, "full": 8192}[w["kind"]]
-    X, mu, cov, lpi = host_sample(w, 4 * rows)
+    phys, logical = host_cores()
+    torch.set_num_threads(phys)
+    rows = w["rows"] if args.workload != "c5" else 1_000_000
+    X, mu, cov, lpi = host_sample(w, rows)
     fn = cpu_port(w["kind"])
     for _ in range(max(args.warmup, 0)):
-        fn(X[:rows], mu, cov, lpi)
+        fn(X[:16384], mu, cov, lpi)
     times = []
     for s in range(args.steps):
-        xs = X[(s % 4) * rows:(s % 4 + 1) * rows]
         t0 = time.perf_counter()
-        fn(xs, mu, cov, lpi)
+        fn(X, mu, cov, lpi)
         times.append(time.perf_counter() - t0)
-    sec = sum(times) / len(times)
+    sec = statistics.median(times)
     value = rows * K / sec
+    title = w["title"] if args.workload != "c5" else (
+        "C5 streaming isotropic E-step; the host runs 1M of its rows per step")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3,
+        "ms_per_step_mean": sum(times) / len(times) * 1e3,
         "higher_is_better": True, "scaling": w["scaling"], "vs_baseline": None, "dtype": "f32",
         "data": f"synthetic (seeded {args.workload.upper()} mixture rows on the host)",
-        "config": {"workload": f"{w['title']}; each step a {rows:,}-row sample on the host CPU",
-                   "K": K, "D": w["D"], "rows_per_step": rows},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
-                         "sample": f"{rows} rows x {K} components per step, torch-CPU fp32"},
+        "config": {"workload": title, "K": K, "D": w["D"], "rows_per_step": rows},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": phys, "cores_physical": phys,
+                         "cores_logical": logical, "kind": "port",
+                         "sample": f"all {rows:,} rows x {K} components per step, torch-CPU "
+                                   f"fp32, {phys} threads"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "the reference is Triton-only (GPU); this arm runs its algorithm's CPU "
-                "restatement from oracle/ on all host threads",
+                "restatement from oracle/ on the host's physical cores",
     }
     print(json.dumps(line), flush=True)
     return 0
@@ -373,14 +402,15 @@ def main():
         dist.barrier()
     clocks = sampler.stop() if sampler is not None else None
     launches = L.launch_count() - launches0
-    ms_total = sum(t0.elapsed_time(t1) for t0, t1 in step_ev)
+    step_ms = [t0.elapsed_time(t1) for t0, t1 in step_ev]
     kern_ms = [a.elapsed_time(b) for a, b in ev_pairs]
-    ms_step = ms_total / args.steps
-    kern_avg = sum(kern_ms) / len(kern_ms)
+    ms_mean = sum(step_ms) / args.steps
+    ms_step = statistics.median(step_ms)  # the median of the K timed steps
+    kern_avg = statistics.median(kern_ms)
     if world > 1:
-        t = torch.tensor([ms_step, kern_avg], device=dev)
+        t = torch.tensor([ms_step, kern_avg, ms_mean], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_step, kern_avg = float(t[0]), float(t[1])
+        ms_step, kern_avg, ms_mean = float(t[0]), float(t[1]), float(t[2])
 
     pairs_step = n_global * K
     value = pairs_step / (ms_step * 1e-3)
@@ -451,8 +481,13 @@ def main():
                 "kernel": w["kernel"],
                 "algorithmic_flops_per_launch": flops_launch,
                 "kernel_ms_per_launch": kern_launch_ms, "rows_per_launch": last_rows}
-    # north-star roofline: max(tensor time at TF32 peak = bf16/2, exp time at MUFU peak)
-    p_tf32 = peaks["bf16_tflops"] / 2
+    # north-star roofline: max(tensor time at the measured dense TF32 rate,
+    # exp time at the MUFU rate: 16 ex2 per clock per SM, measured by the
+    # microbenchmark, at the 1965 MHz maximum clock)
+    tf32 = measured_tf32_tflops()
+    p_tf32 = tf32 if tf32 else peaks["bf16_tflops"] / 2
+    tf32_basis = (f"TF32 {p_tf32:.1f} TFLOP/s measured (torch.matmul 8192^3, "
+                  "profiles/mma_cost.txt)" if tf32 else "TF32 = bf16/2 of measured")
     p_mufu = 148 * 16 * 1.965e9
     t_tc = fpp * pairs_step / world / (p_tf32 * 1e12)
     t_exp = pairs_step / world / p_mufu
@@ -462,15 +497,19 @@ def main():
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         ncpu = min(n_local, 262144)
         Xc, muc, covc, lpic = X[:ncpu].cpu(), mu.cpu(), cov.cpu(), lpi.cpu()
+        phys, logical = host_cores()
         rate, nrows, secs = cpu_reference_rate(kind, Xc, muc, covc, lpic, budget_s=12.0,
-                                               chunk=16384 if kind != "full" else 4096)
-        cpu = {"value": rate, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+                                               chunk=16384 if kind != "full" else 4096,
+                                               threads=phys)
+        cpu = {"value": rate, "unit": UNIT, "cores": phys, "cores_physical": phys,
+               "cores_logical": logical, "kind": "port",
                "sample": f"{nrows} rows x {K} components of the same workload in {secs:.1f} s, "
-                         "torch-CPU fp32 restatement (oracle/)"}
+                         f"torch-CPU fp32 restatement (oracle/), {phys} threads"}
 
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+        "warmup": args.warmup, "ms_per_step": ms_step, "ms_per_step_mean": ms_mean,
+        "higher_is_better": True,
         "scaling": w["scaling"], "vs_baseline": None, "dtype": "f32",
         "data": data,
         "config": {"workload": w["title"], "N_global": n_global, "N_per_rank": n_local, "K": K,
@@ -483,7 +522,10 @@ def main():
         "roofline": roofline,
         "north_star_roofline": {"t_tensor_ms": t_tc * 1e3, "t_exp_ms": t_exp * 1e3,
                                 "t_roof_ms": t_roof * 1e3, "frac": t_roof / (ms_step * 1e-3),
-                                "basis": "TF32 = bf16/2 of measured, MUFU 148x16/clk @1965 MHz"},
+                                "basis": tf32_basis + ", MUFU 148x16/clk @1965 MHz",
+                                "frac_bf16_half_basis": (max(fpp * pairs_step / world /
+                                                             (peaks["bf16_tflops"] / 2 * 1e12),
+                                                             t_exp) / (ms_step * 1e-3))},
         "clocks": clocks,
         "e2e": e2e,
         "gpu_launches": launches,

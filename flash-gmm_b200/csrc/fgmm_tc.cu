@@ -172,6 +172,9 @@ struct TcParams {
   const __half* Wlo;
   const float4* consts;      // [C*128] {c0', ish (iso), c0 (iso), s_k}
   const int* xscale;         // [0] = max|mu| (or max|mu - c|) bits -> a
+  // isotropic: nonzero when the components' variances differ (null: treat
+  // them as different); written by tc_prep_kernel
+  const int* nonuniform = nullptr;
   // Mode 0 (single pass): logZ[row] out, natural log.  Component blocks of
   // more than 1024 components (K > 1024) run in two phases: mode 1 writes
   // each row's log-sum-exp over this launch's components to logZ[row] in
@@ -218,9 +221,12 @@ inline int prep_threads(int Dp) { return Dp > 128 ? 256 : 128; }
 __global__ void __launch_bounds__(256) tc_prep_kernel(
     const float* __restrict__ mu, int64_t smk, int64_t smd, const float* __restrict__ lss,
     const float* __restrict__ lpi, const float* __restrict__ cvec, int K, int D, int Dp,
-    __half* __restrict__ Whi, __half* __restrict__ Wlo, float4* __restrict__ consts) {
+    __half* __restrict__ Whi, __half* __restrict__ Wlo, float4* __restrict__ consts,
+    int* __restrict__ nonuniform) {
   const int k = blockIdx.x;
   const bool valid = k < K;
+  if (nonuniform != nullptr && threadIdx.x == 0 && valid && lss[k] != lss[0])
+    atomicOr(nonuniform, 1);
   double ish = 0.0, c0 = -1e30;
   if (valid) {
     const double l = (double)lss[k];
@@ -1337,7 +1343,7 @@ cudaError_t tc_estep_blocks(int variant, const EstepArgs& a) {
     else
       tc_prep_kernel<<<m.pl[b].Kpad, prep_threads(p0.Dp), 0, st>>>(
           mub, a.smk, a.smd, a.cov + k0, a.lpi + k0, m.cvec, m.Kb[b], a.D, p0.Dp, m.Whi[b],
-          m.Wlo[b], m.consts[b]);
+          m.Wlo[b], m.consts[b], nullptr);
     ++launches;
   }
   const int vec_ok = a.x_vec_ok();
@@ -1536,7 +1542,8 @@ cudaError_t tc_estep(int variant, const EstepArgs& a) {
 
   // err[0]: device error word, err[1]: max|mu - c| (float bits, for the X
   // scale), written by the centre kernel
-  e = cudaMemsetAsync(err, 0, 2 * sizeof(int), hi);
+  // err[2]: the components' variances differ (isotropic prep)
+  e = cudaMemsetAsync(err, 0, 3 * sizeof(int), hi);
   if (e != cudaSuccess) return e;
   int launches = 0;
   centre_kernel<<<pl.Dp, 256, 0, hi>>>(a.mu, a.smk, a.smd, a.K, a.D, cvec, err + 1);
@@ -1549,7 +1556,7 @@ cudaError_t tc_estep(int variant, const EstepArgs& a) {
                                                  a.K, a.D, pl.Dp, Whi, Wlo, consts);
   else
     tc_prep_kernel<<<pl.Kpad, prep_threads(pl.Dp), 0, hi>>>(a.mu, a.smk, a.smd, a.cov, a.lpi, cvec, a.K, a.D,
-                                            pl.Dp, Whi, Wlo, consts);
+                                            pl.Dp, Whi, Wlo, consts, err + 2);
   launches += 2;
   const int vec_ok = a.x_vec_ok();
 
@@ -1592,6 +1599,7 @@ cudaError_t tc_estep(int variant, const EstepArgs& a) {
   p.Wlo = Wlo;
   p.consts = consts;
   p.xscale = err + 1;
+  p.nonuniform = pl.diag ? nullptr : err + 2;
   p.plen = pl.plen;
   p.err = err;
   int part_clusters = 0, presummed = 0;

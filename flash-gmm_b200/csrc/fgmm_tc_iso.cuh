@@ -14,9 +14,8 @@
 // quadrant of 32 components (one epilogue warp; lane = component):
 //   MMA dist(j):  S[b] = W_lo X_hi + W_hi X_lo + W_hi X_hi   (24 MMAs, N = 128)
 //   A   ll = S 2^(a+s_k) + c0' - ish |x-c|^2 (log2 units) for the block's 32
-//       rows; per row the quadrant's max m (redux.sync.max) and the sum of
-//       p = 2^(ll - m) as fixed point (p 2^22 rounded, added with
-//       redux.sync.add.u32: at most 2^-18 relative error in the sum);
+//       rows; per row the quadrant's max m (redux.sync.max) and the fp32 sum
+//       of p = 2^(ll - m) (transpose-reduce over shuffles);
 //   B   the four quadrants' pairs (shared memory) -> the CTA's (max, sum)
 //       per row, sent to every CTA of the cluster (st.async); each CTA forms
 //       the row's log2-normaliser lz2 = M + log2 S;
@@ -59,9 +58,6 @@ constexpr int kIsoRows = 128;
 constexpr int kIsoMaxD = 128;
 constexpr int kIsoCluster = 8;
 constexpr uint32_t kIsoColW = 0, kIsoColT = 128, kIsoColS = 256;
-// fixed-point row sums: q = round(p 2^22) read from the bits of p 2^22 + 2^23
-constexpr float kFixScale = 4194304.0f, kFixBias = 8388608.0f;
-constexpr uint32_t kFixBits32 = 32u * 0x4B000000u;  // 32 biases, mod 2^32
 constexpr float kRespCut = 25.f;  // C: quadrant max below lz2 - 25: r = 0
 
 struct __align__(8) IsoCtl {
@@ -258,6 +254,12 @@ __global__ void __launch_bounds__(kIsoThreads, 1) tc_iso_kernel(const TcParams p
     // ------------------------------------------------------------- epilogue
     const float c0p = kc.x, ish = kc.y, c0 = kc.z;
     const float sck = ldexpf(1.0f, xa + (int)kc.w);  // ll = S' 2^(a + s_k) + ...
+    // Equal variances: every component's ll has the same row term
+    // -ish |x-c|^2, which a row's log-sum-exp carries through unchanged, so
+    // the reductions run on ll' = S' 2^(a+s_k) + c0' (one FFMA per pair) and
+    // the term is applied once per row (lz2 = lz2' - ish |x-c|^2).
+    const bool uni = p.nonuniform != nullptr && *p.nonuniform == 0;
+    const float ish_row = uni ? p.consts[0].y : 0.f;
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
     float nk_acc = 0.f, rll_acc = 0.f;
     const int g = lane >> 3;            // phase B: lane quadrant / peer group
@@ -277,25 +279,51 @@ __global__ void __launch_bounds__(kIsoThreads, 1) tc_iso_kernel(const TcParams p
       if (!iso_wait(&ctl->s_full[b], (j >> 1) & 1, ctl, p.err, 16)) break;
       if (!iso_wait(&ctl->xfull[st], (j / NS) & 1, ctl, p.err, 4096)) break;
       tc_fence_after();
-      // ---- A: per row, the quadrant's max m, p = 2^(ll - m) and the sum of p
-      // (fixed point); lane 0 records (m, sum bits)
+      // ---- A: per row, the quadrant's max m (redux.sync.max; lane 0 records
+      // it) and p = 2^(ll - m); the quadrant's sums of p by an fp32
+      // transpose-reduce over shuffles (five rounds, each halving the rows a
+      // lane carries: lane r ends with row r's sum, which it records)
       {
-        uint32_t sv[32];
-        tmem_ld32(scol, sv);
-        tmem_wait_ld();
+        float pv[32];
+        {
+          uint32_t sv[32];
+          tmem_ld32(scol, sv);
+          tmem_wait_ld();
+          if (uni) {
 #pragma unroll
-        for (int i = 0; i < 32; i += 4) {
-          const float4 s4 = *reinterpret_cast<const float4*>(xq + i);
-          const float xv[4] = {s4.x, s4.y, s4.z, s4.w};
+            for (int i = 0; i < 32; ++i) {
+              const float ll = fmaf(__uint_as_float(sv[i]), sck, c0p);
+              const float m = redux_max(ll);
+              pv[i] = ex2(ll - m);
+              if (lane == 0) rq[q * 32 + i].x = m;
+            }
+          } else {
 #pragma unroll
-          for (int t = 0; t < 4; ++t) {
-            const float ll = fmaf(__uint_as_float(sv[i + t]), sck, fmaf(-ish, xv[t], c0p));
-            const float m = redux_max(ll);
-            const uint32_t su =
-                redux_add_u32(__float_as_uint(fmaf(ex2(ll - m), kFixScale, kFixBias)));
-            if (lane == 0) rq[q * 32 + i + t] = make_float2(m, __uint_as_float(su));
+            for (int i = 0; i < 32; i += 4) {
+              const float4 s4 = *reinterpret_cast<const float4*>(xq + i);
+              const float xv[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+              for (int t = 0; t < 4; ++t) {
+                const float ll =
+                    fmaf(__uint_as_float(sv[i + t]), sck, fmaf(-ish, xv[t], c0p));
+                const float m = redux_max(ll);
+                pv[i + t] = ex2(ll - m);
+                if (lane == 0) rq[q * 32 + i + t].x = m;
+              }
+            }
           }
         }
+#pragma unroll
+        for (int h = 16; h >= 1; h >>= 1) {
+          const bool up = (lane & h) != 0;
+#pragma unroll
+          for (int i = 0; i < h; ++i) {
+            const float send = up ? pv[i] : pv[i + h];
+            const float keep = up ? pv[i + h] : pv[i];
+            pv[i] = keep + __shfl_xor_sync(0xffffffffu, send, h);
+          }
+        }
+        rq[q * 32 + lane].y = pv[0];
       }
       __syncwarp();
       const float mq = rq[q * 32 + lane].x;  // this quadrant's max of row `lane`
@@ -305,8 +333,7 @@ __global__ void __launch_bounds__(kIsoThreads, 1) tc_iso_kernel(const TcParams p
       // pairs -> the row's log2-normaliser lz2 and logZ
       {
         const float2 e = rq[g * 32 + rr];
-        const float mg = e.x;
-        const float sg = (float)(__float_as_uint(e.y) - kFixBits32) * (1.0f / kFixScale);
+        const float mg = e.x, sg = e.y;
         float M = fmaxf(mg, __shfl_xor_sync(0xffffffffu, mg, 8));
         M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, 16));
         float L = sg * ex2(mg - M);
@@ -332,9 +359,10 @@ __global__ void __launch_bounds__(kIsoThreads, 1) tc_iso_kernel(const TcParams p
         float GL = e0.y * ex2(e0.x - GM) + e1.y * ex2(e1.x - GM);
         GL += __shfl_xor_sync(0xffffffffu, GL, 8);
         GL += __shfl_xor_sync(0xffffffffu, GL, 16);
-        const float lz2 = GM + lg2(GL);
+        const float lz2 = GM + lg2(GL);  // in the reductions' units (ll' when uni)
         const bool valid = row0 + xrow < p.N;
-        if (valid && rank == 0 && g == 0) p.logZ[row0 + xrow] = lz2 * 0.6931471805599453f;
+        if (valid && rank == 0 && g == 0)
+          p.logZ[row0 + xrow] = fmaf(-ish_row, xq[rr], lz2) * 0.6931471805599453f;
         if (g == 0) zrow[cb * 32 + rr] = valid ? lz2 : __int_as_float(0x7f800000);  // +inf: r = 0
       }
       if (!sync_block(1, j, 512)) break;
@@ -346,11 +374,14 @@ __global__ void __launch_bounds__(kIsoThreads, 1) tc_iso_kernel(const TcParams p
         const uint32_t need = __ballot_sync(0xffffffffu, mq >= lz - kRespCut);
         const uint32_t pairs = (need | (need >> 1)) & 0x55555555u;
         float nk_t = 0.f, rll_t = 0.f;
+        // r of row i from this lane's distance s (ll in the reductions'
+        // units; sum r ll in true units)
         auto resp = [&](int i, float s) {
-          const float ll = fmaf(s, sck, fmaf(-ish, xq[i], c0p));
+          const float x = xq[i];
+          const float ll = uni ? fmaf(s, sck, c0p) : fmaf(s, sck, fmaf(-ish, x, c0p));
           const float r = ex2(ll - __shfl_sync(0xffffffffu, lz, i));
           nk_t += r;
-          rll_t = fmaf(r, ll, rll_t);
+          rll_t = fmaf(r, uni ? fmaf(-ish, x, ll) : ll, rll_t);
           return r;
         };
         if (__popc(pairs) <= 2) {
@@ -368,6 +399,16 @@ __global__ void __launch_bounds__(kIsoThreads, 1) tc_iso_kernel(const TcParams p
             v[2 * u + 1] = tmem_ld1(scol + c + 1u);
           }
           tmem_wait_ld();
+          uint32_t h[2] = {0u, 0u}, l[2] = {0u, 0u};
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            if (i0[u] < 0) continue;
+            const int i = i0[u];
+            const float r0 = ((need >> i) & 1u) ? resp(i, __uint_as_float(v[2 * u])) : 0.f;
+            const float r1 =
+                ((need >> (i + 1)) & 1u) ? resp(i + 1, __uint_as_float(v[2 * u + 1])) : 0.f;
+            split2(r0, r1, h[u], l[u]);
+          }
           const uint32_t z = 0u;
           const uint32_t zv[16] = {z, z, z, z, z, z, z, z, z, z, z, z, z, z, z, z};
           tmem_st16(scol, zv);
@@ -377,14 +418,8 @@ __global__ void __launch_bounds__(kIsoThreads, 1) tc_iso_kernel(const TcParams p
 #pragma unroll
             for (int u = 0; u < 2; ++u) {
               if (i0[u] < 0) continue;
-              const int i = i0[u];
-              const float r0 = ((need >> i) & 1u) ? resp(i, __uint_as_float(v[2 * u])) : 0.f;
-              const float r1 =
-                  ((need >> (i + 1)) & 1u) ? resp(i + 1, __uint_as_float(v[2 * u + 1])) : 0.f;
-              uint32_t h, l;
-              split2(r0, r1, h, l);
-              tmem_st1(scol + (uint32_t)(i >> 1), h);
-              tmem_st1(scol + 16u + (uint32_t)(i >> 1), l);
+              tmem_st1(scol + (uint32_t)(i0[u] >> 1), h[u]);
+              tmem_st1(scol + 16u + (uint32_t)(i0[u] >> 1), l[u]);
             }
           }
         } else {

@@ -139,7 +139,7 @@ def matmul_tflops(dtype, tf32=False, n=8192, reps=10):
 def run_all(quick: bool = False):
     lib = _lib()
     rows = []
-    Ns = [64, 128, 256] if quick else [32, 64, 128, 192, 256]
+    Ns = [64, 128, 256] if quick else [32, 64, 80, 96, 112, 128, 192, 256]
     for N in Ns:
         rows.append(mma_rate(lib, 0, 128, N))
     for N in Ns:
