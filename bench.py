@@ -250,6 +250,8 @@ def run_reference(args):
     phys, logical = host_cores()
     torch.set_num_threads(phys)
     rows = w["rows"] if args.workload != "c5" else 1_000_000
+    if args.ref_rows > 0:
+        rows = min(rows, args.ref_rows)
     X, mu, cov, lpi = host_sample(w, rows)
     fn = cpu_port(w["kind"])
     for _ in range(max(args.warmup, 0)):
@@ -291,6 +293,8 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="c2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--ref-rows", type=int, default=0,
+                    help="reference arm only: rows per step (default: the full workload)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":

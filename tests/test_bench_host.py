@@ -26,7 +26,8 @@ def _run_bench(*args, env_extra=None):
 
 
 def test_reference_arm_prints_one_contract_line():
-    r = _run_bench("--impl", "reference", "--workload", "c4", "--steps", "2", "--warmup", "0")
+    r = _run_bench("--impl", "reference", "--workload", "c4", "--steps", "2", "--warmup", "0",
+                   "--ref-rows", "8192")
     assert r.returncode == 0, r.stderr
     lines = [ln for ln in r.stdout.splitlines() if ln.strip()]
     assert len(lines) == 1
