@@ -129,6 +129,28 @@ __device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_
       "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// The same MMA with the B descriptor given as its two 32-bit words: callers
+// keep the constant high word and add byte offsets >> 4 to the low word (the
+// start-address field, bits 0-13, does not carry for shared-memory offsets),
+// so each MMA of an unrolled sequence costs one integer add to set up.
+__device__ __forceinline__ void mma_ts2(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_lo,
+                                        uint32_t b_hi, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b64 bd;\n\t"
+      "setp.ne.b32 p, %5, 0;\n\t"
+      "mov.b64 bd, {%2, %3};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], bd, %4, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// True on exactly one active lane of the warp (all 32 lanes must call it).
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\telect.sync _|P, 0xffffffff;\n\tselp.u32 %0, 1, 0, P;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
 // D[tmem] (+)= A[smem desc] * B[smem desc]; kind::f16 with fp16 inputs, fp32 accum.
 __device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
                                        uint32_t idesc, uint32_t accumulate) {
@@ -237,6 +259,15 @@ __device__ __forceinline__ uint64_t desc_kmajor(uint32_t addr) {
   return (uint64_t)((addr >> 4) & 0x3FFF) | (1ull << 16) | (64ull << 32) | (1ull << 46) |
          (2ull << 61);
 }
+// Words of desc_kmajor / desc_mnmajor: low word for a shared-memory address,
+// and the constant high word (SBO = 1024 B, version 1, 128B swizzle).
+__device__ __forceinline__ uint32_t desc_lo_kmajor(uint32_t addr) {
+  return ((addr >> 4) & 0x3FFFu) | (1u << 16);
+}
+__device__ __forceinline__ uint32_t desc_lo_mnmajor(uint32_t addr, uint32_t chunk_bytes) {
+  return ((addr >> 4) & 0x3FFFu) | ((chunk_bytes >> 4) << 16);
+}
+constexpr uint32_t kDescHi = 64u | (1u << 14) | (2u << 29);
 // MN-major: LBO = byte stride between 64-element chunks along N.
 __device__ __forceinline__ uint64_t desc_mnmajor(uint32_t addr, uint32_t chunk_bytes) {
   return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)(chunk_bytes >> 4) << 16) |

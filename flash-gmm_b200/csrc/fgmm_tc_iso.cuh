@@ -14,11 +14,13 @@
 // quadrant of 32 components (one epilogue warp; lane = component):
 //   MMA dist(j):  S[b] = W_lo X_hi + W_hi X_lo + W_hi X_hi   (24 MMAs, N = 128)
 //   A   ll = S 2^(a+s_k) + c0' - ish |x-c|^2 (log2 units) for the block's 32
-//       rows; per row the quadrant's max m (redux.sync.max) and the fp32 sum
-//       of p = 2^(ll - m) (transpose-reduce over shuffles);
-//   B   the four quadrants' pairs (shared memory) -> the CTA's (max, sum)
-//       per row, sent to every CTA of the cluster (st.async); each CTA forms
-//       the row's log2-normaliser lz2 = M + log2 S;
+//       rows; per row the quadrant's max m (redux.sync.max) and the sum of
+//       p = 2^(ll - m) as a 23-bit fixed-point integer (redux.sync.add.u32,
+//       exact and independent of the order of the lanes);
+//   B   (lane = row; each of the block's four warps) the four quadrants'
+//       pairs (shared memory) -> the CTA's (max, sum) per row, sent to the
+//       cluster's CTAs (st.async; warp q serves peers q and q + 4); every
+//       CTA's pair -> the row's log2-normaliser lz2 = M + log2 S;
 //   C   rows where the quadrant's max is within 2^25 of lz2:
 //       r = 2^(ll - lz2), split into fp16 hi/lo words and written to TMEM
 //       over the block's own S columns (hi in the first 16, lo in the next
@@ -78,9 +80,11 @@ struct IsoSmem {
   static constexpr int kStageMax = 2 * 2 * kIsoRows * 128;           // 64 KB
   static constexpr int kXs = 0;
   static constexpr int kXsq = kXs + kIsoStages * kStageMax;          // [NS][128] f32
-  static constexpr int kRed = kXsq + kIsoStages * kIsoRows * 4;      // [4 blk][4 q][32] f2
-  static constexpr int kZ = kRed + 16 * 32 * 8;                      // [4 blk][32] f32 lz2
-  static constexpr int kFin = kZ + 4 * 32 * 4;                       // [8][128] f32
+  // per tile parity, row block, quadrant and row: the quadrant's max (f32)
+  // and its fixed-point sum of 2^(ll - max) (u32, 23 fraction bits)
+  static constexpr int kQMax = kXsq + kIsoStages * kIsoRows * 4;     // [2][4 blk][4 q][32]
+  static constexpr int kQSum = kQMax + 2 * 16 * 32 * 4;              // [2][4 blk][4 q][32]
+  static constexpr int kFin = kQSum + 2 * 16 * 32 * 4;               // [8][128] f32
   static constexpr int kXchg = kFin + 8 * kComps * 4;                // [2][8][128] f2
   static constexpr int kCtl = kXchg + 2 * kIsoCluster * kIsoRows * 8;
   static constexpr int kBytes = kCtl + (int)sizeof(IsoCtl);
@@ -101,8 +105,8 @@ __global__ void __launch_bounds__(kIsoThreads, 1) tc_iso_kernel(const TcParams p
   const int stage_bytes = 2 * p.nch * kIsoRows * 128;  // hi + lo
   uint8_t* xs = smem + IsoSmem::kXs;
   float* xsq = reinterpret_cast<float*>(smem + IsoSmem::kXsq);
-  float2* red = reinterpret_cast<float2*>(smem + IsoSmem::kRed);
-  float* zrow = reinterpret_cast<float*>(smem + IsoSmem::kZ);
+  float* qmax = reinterpret_cast<float*>(smem + IsoSmem::kQMax);
+  uint32_t* qsum = reinterpret_cast<uint32_t*>(smem + IsoSmem::kQSum);
   float* fin = reinterpret_cast<float*>(smem + IsoSmem::kFin);
   float2* xchg = reinterpret_cast<float2*>(smem + IsoSmem::kXchg);  // [slot][CTA][row]
   IsoCtl* ctl = reinterpret_cast<IsoCtl*>(smem + IsoSmem::kCtl);
@@ -179,61 +183,86 @@ __global__ void __launch_bounds__(kIsoThreads, 1) tc_iso_kernel(const TcParams p
 
   if (warp == kIsoMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      const uint32_t id_dist = idesc_f16(kIsoRows, false);
-      const uint32_t id_stat = idesc_f16(64 * p.nch, true);
-      const int ksd = p.nfeat / 16;
-      const uint32_t lo_off = (uint32_t)(p.nch * kIsoRows * 128);
-      auto issue_stats = [&](int jj) {
-        const uint32_t xhi = smem_u32(xs + (jj % NS) * stage_bytes), xlo = xhi + lo_off;
-        const uint32_t rcol = kIsoColS + 128u * (uint32_t)(jj & 1);
+    // The whole warp runs the loop (waits, addresses: warp-uniform values);
+    // one elected lane issues each batch of MMAs.  Descriptors are formed
+    // once per stage and advanced by constant offsets, so an MMA costs about
+    // one integer add to set up: the issuing warp shares its sub-partition
+    // with four epilogue warps, and a longer setup left the tensor pipe idle
+    // between MMAs.
+    const uint32_t id_dist = idesc_f16(kIsoRows, false);
+    const uint32_t id_stat = idesc_f16(64 * p.nch, true);
+    const int ksd = p.nfeat / 16;
+    const uint32_t lo_off = (uint32_t)(p.nch * kIsoRows * 128);
+    const uint32_t xs0 = smem_u32(xs);
+    constexpr uint32_t kChunkBytes = kIsoRows * 128;  // one 64-feature chunk of a stage
+    auto issue_stats = [&](int jj) {
+      const uint32_t xhi = xs0 + (uint32_t)((jj % NS) * stage_bytes);
+      const uint32_t dhi = desc_lo_mnmajor(xhi, kChunkBytes);
+      const uint32_t dlo = desc_lo_mnmajor(xhi + lo_off, kChunkBytes);
+      const uint32_t rcol = tmem + kIsoColS + 128u * (uint32_t)(jj & 1);
+      const uint32_t tcol = tmem + kIsoColT;
+      if (elect_one()) {
         // terms r_lo x_hi, r_hi x_lo, r_hi x_hi; K-step s = rows 16s..16s+15 =
-        // row block s/2, columns 8 (s & 1) of its hi (+0) / lo (+16) words
+        // row block s/2, columns 8 (s & 1) of its hi (+0) / lo (+16) words;
+        // B advances 16 rows = 2048 bytes per K-step
+#pragma unroll
         for (int t = 0; t < 3; ++t) {
           const uint32_t aoff = t == 0 ? 16u : 0u;
-          const uint32_t bb = t == 1 ? xlo : xhi;
+          const uint32_t bd = t == 1 ? dlo : dhi;
 #pragma unroll
           for (int s = 0; s < kIsoRows / 16; ++s)
-            mma_ts(tmem + kIsoColT, tmem + rcol + 32 * (s >> 1) + 8 * (s & 1) + aoff,
-                   desc_mnmajor(bb + s * 2048, kIsoRows * 128), id_stat,
-                   (jj == 0 && t == 0 && s == 0) ? 0u : 1u);
+            mma_ts2(tcol, rcol + 32u * (uint32_t)(s >> 1) + 8u * (uint32_t)(s & 1) + aoff,
+                    bd + (uint32_t)(s * (2048 >> 4)), kDescHi, id_stat,
+                    (jj == 0 && t == 0 && s == 0) ? 0u : 1u);
         }
         tc_commit(&ctl->xempty[jj % NS]);
-      };
-      bool ok = true;
-      for (int j = 0; j < ntiles; ++j) {
-        const int st = j % NS;
-        if (!iso_wait(&ctl->xfull[st], (j / NS) & 1, ctl, p.err, 1)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t xhi = smem_u32(xs + st * stage_bytes), xlo = xhi + lo_off;
-        const uint32_t scol = kIsoColS + 128u * (uint32_t)(j & 1);
-        // terms W_lo x_hi, W_hi x_lo, W_hi x_hi (smallest magnitudes first)
+      }
+      __syncwarp();
+    };
+    // warp-uniform outcome of a bounded wait (elect_one needs every lane)
+    auto wait_all = [&](uint64_t* bar, uint32_t parity, int code) {
+      return __all_sync(0xffffffffu, iso_wait(bar, parity, ctl, p.err, code));
+    };
+    bool ok = true;
+    for (int j = 0; j < ntiles; ++j) {
+      const int st = j % NS;
+      if (!wait_all(&ctl->xfull[st], (j / NS) & 1, 1)) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t xhi = xs0 + (uint32_t)(st * stage_bytes);
+      const uint32_t dhi = desc_lo_kmajor(xhi), dlo = desc_lo_kmajor(xhi + lo_off);
+      const uint32_t scol = tmem + kIsoColS + 128u * (uint32_t)(j & 1);
+      if (elect_one()) {
+        // terms W_lo x_hi, W_hi x_lo, W_hi x_hi (smallest magnitudes first);
+        // K-step s: chunk s/4 (kChunkBytes apart), 32 bytes within the row
+#pragma unroll
         for (int t = 0; t < 3; ++t) {
-          const uint32_t acol = kIsoColW + (t == 0 ? 64u : 0u);
-          const uint32_t bb = t == 1 ? xlo : xhi;
-          for (int s = 0; s < ksd; ++s)
-            mma_ts(tmem + scol, tmem + acol + 8 * s,
-                   desc_kmajor(bb + (s >> 2) * (kIsoRows * 128) + (s & 3) * 32), id_dist,
-                   (t == 0 && s == 0) ? 0u : 1u);
+          const uint32_t acol = tmem + kIsoColW + (t == 0 ? 64u : 0u);
+          const uint32_t bd = t == 1 ? dlo : dhi;
+#pragma unroll
+          for (int s = 0; s < kIsoMaxD / 16; ++s)
+            if (s < ksd)
+              mma_ts2(scol, acol + 8u * (uint32_t)s,
+                      bd + (uint32_t)(((s >> 2) * kChunkBytes + (s & 3) * 32) >> 4), kDescHi,
+                      id_dist, (t == 0 && s == 0) ? 0u : 1u);
         }
         tc_commit(&ctl->s_full[j & 1]);
-        if (j >= 1) {
-          if (!iso_wait(&ctl->r_full[(j - 1) & 1], ((j - 1) >> 1) & 1, ctl, p.err, 4)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          issue_stats(j - 1);
-        }
       }
-      if (ok && ntiles >= 1 &&
-          iso_wait(&ctl->r_full[(ntiles - 1) & 1], ((ntiles - 1) >> 1) & 1, ctl, p.err, 4)) {
+      __syncwarp();
+      if (j >= 1) {
+        if (!wait_all(&ctl->r_full[(j - 1) & 1], ((j - 1) >> 1) & 1, 4)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
-        issue_stats(ntiles - 1);
-        tc_commit(&ctl->t_done);
+        issue_stats(j - 1);
       }
     }
-    __syncwarp();
+    if (ok && ntiles >= 1 && wait_all(&ctl->r_full[(ntiles - 1) & 1], ((ntiles - 1) >> 1) & 1, 4)) {
+      tc_fence_after();
+      issue_stats(ntiles - 1);
+      if (elect_one()) tc_commit(&ctl->t_done);
+      __syncwarp();
+    }
   } else if (warp == kIsoLoadWarp) {
     // ------------------------------------------------------------ row-tile loader
     if (lane == 0) {
@@ -262,83 +291,75 @@ __global__ void __launch_bounds__(kIsoThreads, 1) tc_iso_kernel(const TcParams p
     const float ish_row = uni ? p.consts[0].y : 0.f;
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
     float nk_acc = 0.f, rll_acc = 0.f;
-    const int g = lane >> 3;            // phase B: lane quadrant / peer group
-    const int rr = 8 * q + (lane & 7);  // phase B: row of the block this lane combines
-    float2* rq = red + cb * 128;        // [4 q][32 rows] quadrant (max, fixed-point sum)
     auto sync_block = [&](int e, int j, int code) -> bool {
       __syncwarp();
       if (lane == 0) mbar_arrive(&ctl->e_bar[e][cb]);
       return iso_wait(&ctl->e_bar[e][cb], j & 1, ctl, p.err, code);
     };
+    // peers' pair slots for this lane's row and the barrier words, per slot
+    const int xrow = 32 * cb + lane;
     for (int j = 0; j < ntiles; ++j) {
       const int b = j & 1, st = j % NS, slot = j & 1;
       const int64_t row0 = (int64_t)(cluster_id + (int64_t)j * num_clusters) * kIsoRows;
       const uint32_t scol = tmem + lane_base + kIsoColS + 128u * (uint32_t)b + 32u * (uint32_t)cb;
       const float* xq = xsq + st * kIsoRows + 32 * cb;
-      const int xrow = 32 * cb + rr;
+      float* qm = qmax + (slot * 4 + cb) * 128;     // [4 q][32 rows] of this row block
+      uint32_t* qs = qsum + (slot * 4 + cb) * 128;
       if (!iso_wait(&ctl->s_full[b], (j >> 1) & 1, ctl, p.err, 16)) break;
       if (!iso_wait(&ctl->xfull[st], (j / NS) & 1, ctl, p.err, 4096)) break;
       tc_fence_after();
-      // ---- A: per row, the quadrant's max m (redux.sync.max; lane 0 records
-      // it) and p = 2^(ll - m); the quadrant's sums of p by an fp32
-      // transpose-reduce over shuffles (five rounds, each halving the rows a
-      // lane carries: lane r ends with row r's sum, which it records)
+      // ---- A: per row, the quadrant's max m (redux.sync.max) and the sum of
+      // p = 2^(ll - m) over the quadrant's 32 components: each p in [0, 1] is
+      // rounded to a 23-bit fixed-point integer (p 2^23 + 2^23 leaves it in
+      // the low mantissa bits) and summed exactly by redux.sync.add.u32 (the
+      // 32 copies of 2^23's bits, 0x60000000 mod 2^32, come off when read).
+      // Lane 0 records both per row; the register holding a row's value is
+      // fixed, so no transposition is needed.
       {
-        float pv[32];
-        {
-          uint32_t sv[32];
-          tmem_ld32(scol, sv);
-          tmem_wait_ld();
-          if (uni) {
+        uint32_t sv[32];
+        tmem_ld32(scol, sv);
+        tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const float ll = fmaf(__uint_as_float(sv[i]), sck, c0p);
-              const float m = redux_max(ll);
-              pv[i] = ex2(ll - m);
-              if (lane == 0) rq[q * 32 + i].x = m;
-            }
-          } else {
+        for (int i = 0; i < 32; i += 4) {
+          float xv[4] = {0.f, 0.f, 0.f, 0.f};
+          if (!uni) {
+            const float4 s4 = *reinterpret_cast<const float4*>(xq + i);
+            xv[0] = s4.x; xv[1] = s4.y; xv[2] = s4.z; xv[3] = s4.w;
+          }
+          float mv[4];
+          uint32_t uv[4];
 #pragma unroll
-            for (int i = 0; i < 32; i += 4) {
-              const float4 s4 = *reinterpret_cast<const float4*>(xq + i);
-              const float xv[4] = {s4.x, s4.y, s4.z, s4.w};
-#pragma unroll
-              for (int t = 0; t < 4; ++t) {
-                const float ll =
-                    fmaf(__uint_as_float(sv[i + t]), sck, fmaf(-ish, xv[t], c0p));
-                const float m = redux_max(ll);
-                pv[i + t] = ex2(ll - m);
-                if (lane == 0) rq[q * 32 + i + t].x = m;
-              }
-            }
+          for (int t = 0; t < 4; ++t) {
+            const float base = uni ? c0p : fmaf(-ish, xv[t], c0p);
+            const float ll = fmaf(__uint_as_float(sv[i + t]), sck, base);
+            mv[t] = redux_max(ll);
+            const float pe = ex2(ll - mv[t]);
+            uv[t] = redux_add_u32(__float_as_uint(fmaf(pe, 8388608.f, 8388608.f)));
+          }
+          if (lane == 0) {
+            *reinterpret_cast<float4*>(qm + q * 32 + i) = make_float4(mv[0], mv[1], mv[2], mv[3]);
+            *reinterpret_cast<uint4*>(qs + q * 32 + i) = make_uint4(uv[0], uv[1], uv[2], uv[3]);
           }
         }
-#pragma unroll
-        for (int h = 16; h >= 1; h >>= 1) {
-          const bool up = (lane & h) != 0;
-#pragma unroll
-          for (int i = 0; i < h; ++i) {
-            const float send = up ? pv[i] : pv[i + h];
-            const float keep = up ? pv[i + h] : pv[i];
-            pv[i] = keep + __shfl_xor_sync(0xffffffffu, send, h);
-          }
-        }
-        rq[q * 32 + lane].y = pv[0];
       }
-      __syncwarp();
-      const float mq = rq[q * 32 + lane].x;  // this quadrant's max of row `lane`
       if (!sync_block(0, j, 256)) break;
-      // ---- B: row rr (lane group g = quadrant): the CTA's (max, sum) to every
-      // CTA of the cluster (group g sends to peers g and g + 4); the peers'
-      // pairs -> the row's log2-normaliser lz2 and logZ
+      // ---- B (lane = row of the block; each of the block's four warps does
+      // this for all 32 rows, so no second block-wide sync is needed): the
+      // CTA's (max, sum) from the four quadrants, sent to peers q and q + 4;
+      // then every CTA's pair -> the row's log2-normaliser lz2
+      float mq, lz;
       {
-        const float2 e = rq[g * 32 + rr];
-        const float mg = e.x, sg = e.y;
-        float M = fmaxf(mg, __shfl_xor_sync(0xffffffffu, mg, 8));
-        M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, 16));
-        float L = sg * ex2(mg - M);
-        L += __shfl_xor_sync(0xffffffffu, L, 8);
-        L += __shfl_xor_sync(0xffffffffu, L, 16);
+        float mqq[4], sqq[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          mqq[u] = qm[u * 32 + lane];
+          sqq[u] = (float)(qs[u * 32 + lane] - 0x60000000u) * 1.1920928955078125e-7f;  // 2^-23
+        }
+        mq = q == 0 ? mqq[0] : q == 1 ? mqq[1] : q == 2 ? mqq[2] : mqq[3];
+        const float M = fmaxf(fmaxf(mqq[0], mqq[1]), fmaxf(mqq[2], mqq[3]));
+        float L = 0.f;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) L = fmaf(sqq[u], ex2(mqq[u] - M), L);
         float2* xb = xchg + slot * kIsoCluster * kIsoRows;
         const uint32_t my_slot = smem_u32(&xb[rank * kIsoRows + xrow]);
         const uint32_t my_bar = smem_u32(&ctl->xchg_full[slot][cb]);
@@ -346,31 +367,32 @@ __global__ void __launch_bounds__(kIsoThreads, 1) tc_iso_kernel(const TcParams p
           mbar_arrive_expect_tx(&ctl->xchg_full[slot][cb], (uint32_t)(p.C * 32 * 8));
 #pragma unroll
         for (int jj = 0; jj < 2; ++jj)
-          if (g + 4 * jj < p.C)
-            st_async_f2(map_to_cta(my_slot, g + 4 * jj), M, L, map_to_cta(my_bar, g + 4 * jj));
+          if (q + 4 * jj < p.C)
+            st_async_f2(map_to_cta(my_slot, q + 4 * jj), M, L, map_to_cta(my_bar, q + 4 * jj));
         if (!mbar_wait_flag<true>(&ctl->xchg_full[slot][cb], (j >> 1) & 1, &ctl->abort_flag,
                                   p.err, 32))
           break;
-        const float2 e0 = g < p.C ? xb[g * kIsoRows + xrow] : make_float2(-3e38f, 0.f);
-        const float2 e1 = g + 4 < p.C ? xb[(g + 4) * kIsoRows + xrow] : make_float2(-3e38f, 0.f);
-        float GM = fmaxf(e0.x, e1.x);
-        GM = fmaxf(GM, __shfl_xor_sync(0xffffffffu, GM, 8));
-        GM = fmaxf(GM, __shfl_xor_sync(0xffffffffu, GM, 16));
-        float GL = e0.y * ex2(e0.x - GM) + e1.y * ex2(e1.x - GM);
-        GL += __shfl_xor_sync(0xffffffffu, GL, 8);
-        GL += __shfl_xor_sync(0xffffffffu, GL, 16);
+        float2 e[kIsoCluster];
+        float GM = -3e38f;
+#pragma unroll
+        for (int c = 0; c < kIsoCluster; ++c) {
+          e[c] = c < p.C ? xb[c * kIsoRows + xrow] : make_float2(-3e38f, 0.f);
+          GM = fmaxf(GM, e[c].x);
+        }
+        float GL = 0.f;
+#pragma unroll
+        for (int c = 0; c < kIsoCluster; ++c)
+          if (c < p.C) GL = fmaf(e[c].y, ex2(e[c].x - GM), GL);
         const float lz2 = GM + lg2(GL);  // in the reductions' units (ll' when uni)
         const bool valid = row0 + xrow < p.N;
-        if (valid && rank == 0 && g == 0)
-          p.logZ[row0 + xrow] = fmaf(-ish_row, xq[rr], lz2) * 0.6931471805599453f;
-        if (g == 0) zrow[cb * 32 + rr] = valid ? lz2 : __int_as_float(0x7f800000);  // +inf: r = 0
+        if (valid && rank == 0 && q == 0)
+          p.logZ[row0 + xrow] = fmaf(-ish_row, xq[lane], lz2) * 0.6931471805599453f;
+        lz = valid ? lz2 : __int_as_float(0x7f800000);  // +inf: r = 0
       }
-      if (!sync_block(1, j, 512)) break;
 
       // ---- C: responsibilities of the rows this quadrant takes part in;
       // R^T (fp16 hi | lo) over the block's own S columns, zeros elsewhere
       {
-        const float lz = zrow[cb * 32 + lane];
         const uint32_t need = __ballot_sync(0xffffffffu, mq >= lz - kRespCut);
         const uint32_t pairs = (need | (need >> 1)) & 0x55555555u;
         float nk_t = 0.f, rll_t = 0.f;
