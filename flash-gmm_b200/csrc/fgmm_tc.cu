@@ -57,6 +57,7 @@
 #include <math.h>
 
 #include <algorithm>
+#include <climits>
 #include <atomic>
 #include <mutex>
 #include <type_traits>
@@ -184,6 +185,14 @@ struct TcParams {
   float* part;               // [clusters][C*128][plen]
   int plen;
   int* err;
+  // isotropic single-pass kernel: (row, component) pairs whose expanded
+  // distance may carry more error than logZ's tolerance allows are appended
+  // here (null: none) for tc_refine_iso_kernel; mc[k] = |mu_k - c|
+  const float* mc = nullptr;
+  int4* refine = nullptr;     // {row of the call, component, r bits, ll (log2) bits}
+  int* refine_count = nullptr;
+  int refine_cap = 0;
+  int row_base = 0;           // first row of this launch within the call
 };
 
 struct __align__(8) SmemCtl {
@@ -222,7 +231,7 @@ __global__ void __launch_bounds__(256) tc_prep_kernel(
     const float* __restrict__ mu, int64_t smk, int64_t smd, const float* __restrict__ lss,
     const float* __restrict__ lpi, const float* __restrict__ cvec, int K, int D, int Dp,
     __half* __restrict__ Whi, __half* __restrict__ Wlo, float4* __restrict__ consts,
-    int* __restrict__ nonuniform) {
+    int* __restrict__ nonuniform, float* __restrict__ mc = nullptr) {
   const int k = blockIdx.x;
   const bool valid = k < K;
   if (nonuniform != nullptr && threadIdx.x == 0 && valid && lss[k] != lss[0])
@@ -269,6 +278,7 @@ __global__ void __launch_bounds__(256) tc_prep_kernel(
     if (!(c0 > -1e30)) { c0 = -1e30; c0p = -1e30; }
     if (c0p < -1e30) c0p = -1e30;
     consts[k] = make_float4((float)c0p, (float)ish, (float)c0, (float)sk);
+    if (mc != nullptr) mc[k] = (float)sqrt(musq);
   }
 }
 
@@ -1055,6 +1065,53 @@ __global__ void tc_lse_combine_kernel(const float* __restrict__ lse_part, int nb
   }
 }
 
+// Exact refinement of logZ for the (row, component) pairs listed by
+// tc_iso_kernel (isotropic, log2 units): one warp per pair forms
+// |x - mu_k|^2 from the inputs with exact differences (lanes over features,
+// a fixed shuffle order), ll = c0_k - ish_k |x - mu_k|^2, and adds
+// r (2^(ll - ll_used) - 1) -- the relative change of the row's sum of
+// 2^ll -- to corr[row] as a 2^-40 fixed-point integer (integer adds: the
+// result does not depend on the order of the pairs).
+constexpr double kCorrScale = 1099511627776.0;  // 2^40
+template <class TX>
+__global__ void __launch_bounds__(256) tc_refine_iso_kernel(
+    const int4* __restrict__ pairs, const int* __restrict__ count, int cap,
+    const TX* __restrict__ X, int64_t sxn, int64_t sxd, const float* __restrict__ mu,
+    int64_t smk, int64_t smd, int D, const float4* __restrict__ consts,
+    unsigned long long* __restrict__ corr) {
+  const int n = min(*count, cap);
+  const int lane = threadIdx.x & 31;
+  for (int e = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; e < n;
+       e += (gridDim.x * blockDim.x) >> 5) {
+    const int4 en = pairs[e];
+    const int64_t row = en.x;
+    const int k = en.y;
+    float d2 = 0.f;
+    for (int d = lane; d < D; d += 32) {
+      const float diff = ldx(X + row * sxn + (int64_t)d * sxd) - __ldg(mu + (int64_t)k * smk +
+                                                                         (int64_t)d * smd);
+      d2 = fmaf(diff, diff, d2);
+    }
+    for (int o = 16; o > 0; o >>= 1) d2 += __shfl_xor_sync(0xffffffffu, d2, o);
+    if (lane == 0) {
+      const float4 kc = consts[k];  // {c0', ish, c0, s_k}
+      const float delta = fmaf(-kc.y, d2, kc.z) - __int_as_float(en.w);
+      const double v = (double)__int_as_float(en.z) * ((double)exp2f(delta) - 1.0);
+      atomicAdd(corr + row, (unsigned long long)__double2ll_rn(v * kCorrScale));
+    }
+  }
+}
+
+// logZ += ln(1 + corr 2^-40) for rows with a correction.
+__global__ void __launch_bounds__(256) tc_apply_refine_kernel(
+    const unsigned long long* __restrict__ corr, int64_t N, float* __restrict__ logZ) {
+  for (int64_t n = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; n < N;
+       n += (int64_t)gridDim.x * blockDim.x) {
+    const long long v = (long long)corr[n];
+    if (v != 0) logZ[n] += (float)log1p((double)v / kCorrScale);
+  }
+}
+
 struct TcPlan {
   bool diag;
   bool iso = false;  // isotropic, K <= 1024, D <= 128: tc_iso_kernel
@@ -1481,6 +1538,10 @@ bool tc_supported(int variant, const EstepArgs& a, std::string* why) {
   return true;
 }
 
+// Room for pairs to refine: two per row on average (a row has at most 256
+// pairs with r >= 2^-8; pairs beyond the room keep the tensor-core value).
+inline int64_t refine_cap(int64_t N) { return std::min<int64_t>(2 * N + 4096, INT32_MAX); }
+
 size_t tc_workspace_bytes(int variant, int64_t N, int K, int D) {
   if (variant == kFull) return full_tc_workspace_bytes(N, K, D);
   EstepArgs probe{};
@@ -1503,6 +1564,11 @@ size_t tc_workspace_bytes(int variant, int64_t N, int K, int D) {
   w.take<float>((size_t)plan_chunks(pl) * (kSms / pl.C) * pl.Kpad * pl.plen);
   w.take<uint8_t>((size_t)pl.num_tiles * pl.stage_bytes);             // split features
   if (!pl.diag) w.take<float>((size_t)pl.num_tiles * pl.rows);         // |x|^2
+  if (pl.iso) {                                                        // logZ refinement
+    w.take<float>(pl.Kpad);
+    w.take<unsigned long long>((size_t)N);
+    w.take<int4>((size_t)refine_cap(N));
+  }
   return std::max(w.used + 256, blocked);
 }
 
@@ -1526,6 +1592,15 @@ cudaError_t tc_estep(int variant, const EstepArgs& a) {
   float* part = w.take<float>((size_t)nchunks * (kSms / pl.C) * pl.Kpad * pl.plen);
   uint8_t* xsplit = w.take<uint8_t>((size_t)pl.num_tiles * pl.stage_bytes);
   float* xsq = pl.diag ? nullptr : w.take<float>((size_t)pl.num_tiles * pl.rows);
+  float* mc = nullptr;
+  unsigned long long* corr = nullptr;
+  int4* refine = nullptr;
+  const bool refine_on = pl.iso && a.N <= INT32_MAX;  // pairs store 32-bit row numbers
+  if (pl.iso) {
+    mc = w.take<float>(pl.Kpad);
+    corr = w.take<unsigned long long>((size_t)a.N);
+    refine = w.take<int4>((size_t)refine_cap(a.N));
+  }
 
   SideStreams* ss = nchunks > 1 ? side_streams() : nullptr;
   if (ss == nullptr) nchunks = 1;
@@ -1543,8 +1618,12 @@ cudaError_t tc_estep(int variant, const EstepArgs& a) {
   // err[0]: device error word, err[1]: max|mu - c| (float bits, for the X
   // scale), written by the centre kernel
   // err[2]: the components' variances differ (isotropic prep)
-  e = cudaMemsetAsync(err, 0, 3 * sizeof(int), hi);
+  // err[3]: pairs listed for the logZ refinement (tc_iso_kernel)
+  e = cudaMemsetAsync(err, 0, 4 * sizeof(int), hi);
   if (e != cudaSuccess) return e;
+  if (refine_on && (e = cudaMemsetAsync(corr, 0, (size_t)a.N * sizeof(*corr), hi)) !=
+                       cudaSuccess)
+    return e;
   int launches = 0;
   centre_kernel<<<pl.Dp, 256, 0, hi>>>(a.mu, a.smk, a.smd, a.K, a.D, cvec, err + 1);
   if (nchunks > 1) {  // the split passes need c and max|mu - c| only: they overlap the prep
@@ -1556,7 +1635,7 @@ cudaError_t tc_estep(int variant, const EstepArgs& a) {
                                                  a.K, a.D, pl.Dp, Whi, Wlo, consts);
   else
     tc_prep_kernel<<<pl.Kpad, prep_threads(pl.Dp), 0, hi>>>(a.mu, a.smk, a.smd, a.cov, a.lpi, cvec, a.K, a.D,
-                                            pl.Dp, Whi, Wlo, consts, err + 2);
+                                            pl.Dp, Whi, Wlo, consts, err + 2, mc);
   launches += 2;
   const int vec_ok = a.x_vec_ok();
 
@@ -1602,6 +1681,12 @@ cudaError_t tc_estep(int variant, const EstepArgs& a) {
   p.nonuniform = pl.diag ? nullptr : err + 2;
   p.plen = pl.plen;
   p.err = err;
+  if (refine_on) {
+    p.mc = mc;
+    p.refine = refine;
+    p.refine_count = err + 3;
+    p.refine_cap = (int)refine_cap(a.N);
+  }
   int part_clusters = 0, presummed = 0;
   for (int c = 0; c < nchunks; ++c) {
     const int t0 = chunk_begin(c, nchunks, pl.num_tiles);
@@ -1618,6 +1703,7 @@ cudaError_t tc_estep(int variant, const EstepArgs& a) {
     p.N = std::min<int64_t>(a.N, (int64_t)t1 * pl.rows) - row0;
     p.num_tiles = pc.num_tiles;
     p.logZ = a.logZ + row0;
+    p.row_base = (int)row0;
     p.part = part + (size_t)part_clusters * pl.Kpad * pl.plen;
     if (pl.iso)
       e = launch_iso(pc, p, hi);
@@ -1656,6 +1742,18 @@ cudaError_t tc_estep(int variant, const EstepArgs& a) {
                                           a.mu_acc, a.sig, accumulate);
   }
   ++launches;
+  if (refine_on) {
+    with_xtype(a.xtype, [&](auto tx) {
+      using TX = std::remove_const_t<std::remove_pointer_t<decltype(tx)>>;
+      tc_refine_iso_kernel<TX><<<2 * kSms, 256, 0, hi>>>(refine, err + 3, p.refine_cap, a.x<TX>(),
+                                                         a.sxn, a.sxd, a.mu, a.smk, a.smd, a.D,
+                                                         consts, corr);
+      return 0;
+    });
+    tc_apply_refine_kernel<<<(int)std::min<int64_t>((a.N + 255) / 256, 8 * kSms), 256, 0, hi>>>(
+        corr, a.N, a.logZ);
+    launches += 2;
+  }
   count_launches(launches);
   if (nchunks > 1) {
     if ((e = cudaEventRecord(ss->ev[2 + kChunks], hi)) != cudaSuccess) return e;

@@ -291,6 +291,15 @@ __global__ void __launch_bounds__(kIsoThreads, 1) tc_iso_kernel(const TcParams p
     const float ish_row = uni ? p.consts[0].y : 0.f;
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
     float nk_acc = 0.f, rll_acc = 0.f;
+    // Expanded-form accuracy: the distance comes out of an fp32 tensor-core
+    // accumulation whose error grows with ish |x - c| |mu_k - c| (up to ~14
+    // units of 2^-23 of it, measured), while logZ is held to 1e-5 of |logZ|.
+    // Pairs with r >= 2^-8 where 32 x 2^-23 of that magnitude exceeds the
+    // tolerance are listed for an exact recomputation of their distance from
+    // the inputs (tc_refine_iso_kernel), which corrects logZ.
+    const float mck = (p.refine != nullptr && warp < kIsoEpiWarps) ? p.mc[kg] : 0.f;
+    const float cmax = redux_max(ish * mck) * 3.814697265625e-06f;  // ish, mck >= 0
+    const float cgate = cmax * cmax;
     auto sync_block = [&](int e, int j, int code) -> bool {
       __syncwarp();
       if (lane == 0) mbar_arrive(&ctl->e_bar[e][cb]);
@@ -396,6 +405,36 @@ __global__ void __launch_bounds__(kIsoThreads, 1) tc_iso_kernel(const TcParams p
         const uint32_t need = __ballot_sync(0xffffffffu, mq >= lz - kRespCut);
         const uint32_t pairs = (need | (need >> 1)) & 0x55555555u;
         float nk_t = 0.f, rll_t = 0.f;
+        // Pairs for the exact refinement: r >= 2^-8 and
+        // 32 x 2^-23 ish |x - c| |mu_k - c| > 1e-5 max(1, |logZ|) (log2 units);
+        // only rows whose |x - c| / max(1, |logZ|) times the warp's largest
+        // ish |mu_k - c| could pass are scanned (on C2 about one in a hundred)
+        if (p.refine != nullptr) {
+          const float xl = xq[lane];  // lane = row; squared form of the test, no sqrt
+          const float tl = 1e-5f * fmaxf(1.44269504f, fabsf(uni ? fmaf(-ish_row, xl, lz) : lz));
+          const uint32_t cand = __ballot_sync(0xffffffffu, xl * cgate > tl * tl);
+          if (cand & need) {
+            for (uint32_t nm = cand & need; nm != 0u; nm &= nm - 1u) {
+              const int i = __ffs(nm) - 1;
+              const float sv1 = __uint_as_float(tmem_ld1(scol + (uint32_t)i));
+              tmem_wait_ld();
+              const float x = xq[i];
+              const float lzi = __shfl_sync(0xffffffffu, lz, i);
+              const float ll = uni ? fmaf(sv1, sck, c0p) : fmaf(sv1, sck, fmaf(-ish, x, c0p));
+              const float r = ex2(ll - lzi);
+              const float lzt = uni ? fmaf(-ish_row, x, lzi) : lzi;
+              const float tt = 1e-5f * fmaxf(1.44269504f, fabsf(lzt));
+              const float bk = ish * mck * 3.814697265625e-06f;
+              if (r >= 0.00390625f && x * bk * bk > tt * tt) {
+                const int at = atomicAdd(p.refine_count, 1);
+                if (at < p.refine_cap)
+                  p.refine[at] = make_int4(p.row_base + (int)row0 + 32 * cb + i, kg,
+                                           __float_as_int(r),
+                                           __float_as_int(uni ? fmaf(-ish, x, ll) : ll));
+              }
+            }
+          }
+        }
         // r of row i from this lane's distance s (ll in the reductions'
         // units; sum r ll in true units)
         auto resp = [&](int i, float s) {

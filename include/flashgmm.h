@@ -142,7 +142,7 @@ FGMM_API int fgmm_estep_x(int variant, int x_type, const void* X, int64_t x_stri
  * (a host runtime whose device memory belongs to another pool, or a loop
  * that must not call cudaMalloc).  No counterpart in the reference.
  *  - Shapes whose workspace exceeds the scratch return FGMM_ERR_WORKSPACE
- *    (about 110,000 rows at D = 128 on the tensor-core path; the general
+ *    (about 100,000 rows at D = 128 on the tensor-core path; the general
  *    kernels' scratch does not grow with N).
  *  - Nothing has to be zeroed beforehand.
  *  - The first call on a device does a one-time set-up (looks up the
