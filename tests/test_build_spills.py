@@ -1,7 +1,8 @@
 """Build check (CPU, needs nvcc): the fused E-step kernels that carry the
 benchmark shapes keep their epilogue in registers.  A register spill in the
-128-row isotropic kernel cost ~4% of the C2 E-step, so the single-pass
-(MODE 0) instantiations of the 8-CTA-cluster configurations must report no
+128-row isotropic kernel cost ~4% of the C2 E-step, so the isotropic
+K <= 1024 kernel (tc_iso_kernel) and the single-pass (MODE 0) instantiations
+of the other 8-CTA-cluster configurations (diagonal, wide) must report no
 spill stores or loads in ptxas's resource usage."""
 
 import os
@@ -49,7 +50,9 @@ def test_single_pass_fused_kernels_do_not_spill():
     checked = {}
     for name, spills in found.items():
         m = pat.search(name)
-        if m:
+        if m and not (m.group(1) == "128" and m.group(2) == "0"):  # iso: tc_iso_kernel below
             checked[f"rows={m.group(1)} diag={m.group(2)} feat={m.group(3)}"] = spills
+        if "tc_iso_kernel" in name:
+            checked["tc_iso_kernel"] = spills
     assert len(checked) == 4, sorted(found)
     assert all(v == (0, 0) for v in checked.values()), checked
