@@ -27,7 +27,9 @@ FGMM_X_F32 = 0
 FGMM_X_BF16 = 1
 
 _ERRORS = {1: "invalid argument", 2: "workspace", 3: "unsupported shape",
-           4: "CUDA error", 5: "unsupported device"}
+           4: "CUDA error", 5: "unsupported device", 6: "device-side failure"}
+FGMM_STATUS_RANGE = 0x10000
+ERR_DEVICE_STATUS = 6   # raised by estep(check=True); not a C ABI return code
 
 _lib = None
 _lock = threading.Lock()
@@ -123,12 +125,18 @@ def _f32(t: torch.Tensor, device) -> torch.Tensor:
 
 def estep(variant: int, X: torch.Tensor, mu: torch.Tensor, cov: torch.Tensor,
           log_pi: torch.Tensor, *, out=None, accumulate: bool = False,
-          force_general: bool = False):
+          force_general: bool = False, check: bool = False):
     """One E-step through the C ABI on torch's current stream.
 
     ``out`` may supply (logZ, Nk, mu_acc, sig) buffers (required when
     ``accumulate`` is set); otherwise fresh tensors are allocated, as the
     reference does on every call (flash_gmm_diag_h100.py:24-25).
+
+    ``check=True`` waits for the call and reads the workspace's device status
+    word (include/flashgmm.h): a device-side failure -- a scaled value of X
+    outside fp16's range, or a bounded wait that timed out, after which the
+    statistics are NaN -- raises FlashGMMError.  Without it the call stays
+    asynchronous and such a failure shows only as NaN statistics.
     """
     lib = load()
     dev = X.device
@@ -166,6 +174,12 @@ def estep(variant: int, X: torch.Tensor, mu: torch.Tensor, cov: torch.Tensor,
                   mu.stride(1), cov.data_ptr(), log_pi.data_ptr(), N, K, D,
                   logZ.data_ptr(), Nk.data_ptr(), mu_acc.data_ptr(), sig.data_ptr(),
                   ws.data_ptr(), ws.numel(), flags, stream))
+        if check:
+            status = int(ws[:4].view(torch.int32).item())  # synchronises with the stream
+            if status != 0:
+                what = ("a scaled value of X is outside fp16's range" if status == FGMM_STATUS_RANGE
+                        else f"device status word 0x{status:x} (a bounded wait timed out)")
+                raise FlashGMMError(ERR_DEVICE_STATUS, what + "; the statistics are NaN")
     return logZ, Nk, mu_acc, sig
 
 

@@ -499,6 +499,7 @@ GeneralPlan plan_general(int variant, int64_t N, int K, int D) {
 size_t general_workspace_bytes(int variant, int64_t N, int K, int D) {
   GeneralPlan p = plan_general(variant, N, K, D);
   WsCarve w(nullptr);
+  w.take<int>(64);                                     // device status word (stays 0)
   w.take<float>(K);                                    // cst
   w.take<float>(variant == kDiag ? (size_t)K * D : K); // inv
   w.take<float>((size_t)p.slabs * K * p.part_len);     // partials
@@ -510,11 +511,14 @@ cudaError_t general_estep(int variant, const EstepArgs& a) {
   const int K = a.K, D = a.D;
   GeneralPlan p = plan_general(variant, N, K, D);
   WsCarve w(a.ws);
+  int* status = w.take<int>(64);  // the workspace's first word: no device-side failure here
   float* cst = w.take<float>(K);
   float* inv = w.take<float>(variant == kDiag ? (size_t)K * D : K);
   float* part = w.take<float>((size_t)p.slabs * K * p.part_len);
   cudaStream_t st = a.stream;
 
+  cudaError_t e = cudaMemsetAsync(status, 0, sizeof(int), st);
+  if (e != cudaSuccess) return e;
   prep_kernel<<<(K + 127) / 128, 128, 0, st>>>(variant, a.cov, a.lpi, K, D, cst, inv);
   const unsigned row_blocks = (unsigned)((N + BR - 1) / BR);
   with_xtype(a.xtype, [&](auto tx) {

@@ -97,10 +97,12 @@ bool full_tc_supported(const EstepArgs& a);
 size_t full_tc_workspace_bytes(int64_t N, int K, int D);
 cudaError_t full_tc_estep(const EstepArgs& a);
 
-// c_d = mean_k mu_kd (0 for d >= D) and *amax |= max |mu_kd - c_d| (float
-// bits, atomicMax; *amax must start at 0).  Grid: Dp blocks of 256 threads.
-__global__ void centre_kernel(const float* __restrict__ mu, int64_t smk, int64_t smd, int K,
-                              int D, float* __restrict__ cvec, int* __restrict__ amax);
+// c_d = mean_k mu_kd (0 for d >= D) and *amax |= the largest |mu_kd - c_d|
+// and |x_nd - c_d| over an evenly spaced sample of kScaleSample rows (float
+// bits, atomicMax; *amax must start at 0): the X scale of the split passes.
+// One launch of Dp blocks on `stream`.
+constexpr int64_t kScaleSample = 4096;
+void launch_centre(const EstepArgs& a, int Dp, float* cvec, int* amax, cudaStream_t stream);
 
 // Row generator for the streaming configuration.
 cudaError_t generate_iso_rows(float* X, const int64_t* row_ids, int64_t row0,

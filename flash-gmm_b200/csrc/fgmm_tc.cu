@@ -1387,7 +1387,7 @@ cudaError_t tc_estep_blocks(int variant, const EstepArgs& a) {
   if (e != cudaSuccess) return e;
   int launches = 0;
   // one centre and X scale for all blocks
-  centre_kernel<<<p0.Dp, 256, 0, st>>>(a.mu, a.smk, a.smd, a.K, a.D, m.cvec, m.err + 1);
+  launch_centre(a, p0.Dp, m.cvec, m.err + 1, st);
   ++launches;
   for (int b = 0; b < m.nb; ++b) {
     const int64_t k0 = (int64_t)b * kBlockComps;
@@ -1476,14 +1476,18 @@ cudaError_t tc_estep_blocks(int variant, const EstepArgs& a) {
 
 // ---------------------------------------------------------------------------
 // Centre, one block per feature d (Dp blocks of 256 threads):
-// c_d = mean_k mu_kd (0 for padding features) and amax = max |mu_kd - c_d|.
+// c_d = mean_k mu_kd (0 for padding features) and amax = max of |mu_kd - c_d|
+// and of |x_nd - c_d| over a sample of rows (the X scale of the split passes).
 // Centring by one global vector leaves every x - mu_k unchanged and keeps
 // expanded forms (x^2 - 2 x mu + mu^2, x L - mu L, x x^T) away from
 // cancellation when the data sit far from the origin.
 // ---------------------------------------------------------------------------
+template <class TX>
 __global__ void __launch_bounds__(256) centre_kernel(const float* __restrict__ mu,
                                                              int64_t smk, int64_t smd, int K,
-                                                             int D, float* __restrict__ cvec,
+                                                             int D, const TX* __restrict__ X,
+                                                             int64_t sxn, int64_t sxd, int64_t N,
+                                                             float* __restrict__ cvec,
                                                              int* __restrict__ amax) {
   const int d = blockIdx.x;
   __shared__ double s_sum[8];
@@ -1510,6 +1514,14 @@ __global__ void __launch_bounds__(256) centre_kernel(const float* __restrict__ m
 #pragma unroll 4
     for (int k = threadIdx.x; k < K; k += 256)
       mx = fmaxf(mx, fabsf(mu[(int64_t)k * smk + (int64_t)d * smd] - c));
+    // and over an evenly spaced sample of up to kScaleSample rows of X, so the
+    // scale also covers the data when the means sit close together (K = 1,
+    // means near the global mean)
+    const int64_t ns = N < kScaleSample ? N : kScaleSample;
+    for (int64_t i = threadIdx.x; i < ns; i += 256) {
+      const int64_t n = i * N / ns;
+      mx = fmaxf(mx, fabsf(ldx(X + n * sxn + (int64_t)d * sxd) - c));
+    }
   }
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   if ((threadIdx.x & 31) == 0) s_max[threadIdx.x >> 5] = mx;
@@ -1519,6 +1531,15 @@ __global__ void __launch_bounds__(256) centre_kernel(const float* __restrict__ m
     for (int w = 0; w < 8; ++w) m = fmaxf(m, s_max[w]);
     atomicMax(amax, __float_as_int(m));
   }
+}
+
+void launch_centre(const EstepArgs& a, int Dp, float* cvec, int* amax, cudaStream_t stream) {
+  with_xtype(a.xtype, [&](auto tx) {
+    using TX = std::remove_const_t<std::remove_pointer_t<decltype(tx)>>;
+    centre_kernel<TX><<<Dp, 256, 0, stream>>>(a.mu, a.smk, a.smd, a.K, a.D, a.x<TX>(), a.sxn,
+                                              a.sxd, a.N, cvec, amax);
+    return 0;
+  });
 }
 
 
@@ -1625,7 +1646,7 @@ cudaError_t tc_estep(int variant, const EstepArgs& a) {
                        cudaSuccess)
     return e;
   int launches = 0;
-  centre_kernel<<<pl.Dp, 256, 0, hi>>>(a.mu, a.smk, a.smd, a.K, a.D, cvec, err + 1);
+  launch_centre(a, pl.Dp, cvec, err + 1, hi);
   if (nchunks > 1) {  // the split passes need c and max|mu - c| only: they overlap the prep
     if ((e = cudaEventRecord(ss->ev[1], hi)) != cudaSuccess) return e;
     if ((e = cudaStreamWaitEvent(lo, ss->ev[1], 0)) != cudaSuccess) return e;

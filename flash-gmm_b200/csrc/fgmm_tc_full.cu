@@ -970,7 +970,7 @@ cudaError_t full_tc_estep(const EstepArgs& a) {
   cudaError_t e = cudaMemsetAsync(ws.err, 0, 2 * sizeof(int), st);
   if (e != cudaSuccess) return e;
   int* amax = ws.err + 1;
-  centre_kernel<<<pl.Dp, 256, 0, st>>>(a.mu, a.smk, a.smd, a.K, a.D, ws.cvec, amax);
+  launch_centre(a, pl.Dp, ws.cvec, amax, st);
   full_prep_kernel<<<pl.Kpad, 64, 0, st>>>(a.mu, a.smk, a.smd, a.cov, a.lpi, ws.cvec, a.K, a.D,
                                            pl.Dp, ws.lgroups, ws.bvec, ws.kconst);
   const int vec_ok = a.x_vec_ok();

@@ -40,6 +40,19 @@
  *  - Return value: FGMM_OK (0) or one of the FGMM_ERR_* codes; no C++
  *    exception crosses the ABI.  fgmm_last_error() gives a message for the
  *    last failing call on the calling thread.
+ *  - Device-side failures cannot change the return value (the call has
+ *    returned before its kernels run).  The tensor-core kernels check on the
+ *    device that (a) every scaled value of X is finite and fits fp16's range -- X is scaled
+ *    by one power of two chosen from the means and an evenly spaced sample
+ *    of 4096 rows, which leaves room for rows about 2,000x (isotropic, full)
+ *    or 30x (diagonal, whose features include squares) farther from the
+ *    means' centre than any of those -- and (b) that every bounded wait
+ *    completed.  If either fails, logZ may be wrong and Nk, mu_acc and sig
+ *    are all NaN.  The first int32 of the workspace is the call's status
+ *    word: once the call's work on `stream` has completed it reads 0, or
+ *    FGMM_STATUS_RANGE for (a), or another nonzero value for (b).  The
+ *    no-workspace entry fgmm_estep_iso_noalloc signals them through the NaN
+ *    outputs only.
  */
 #ifndef FLASHGMM_H_
 #define FLASHGMM_H_
@@ -63,6 +76,9 @@ extern "C" {
 #define FGMM_ERR_UNSUPPORTED 3  /* shape outside what any kernel handles   */
 #define FGMM_ERR_CUDA 4         /* CUDA launch / runtime error             */
 #define FGMM_ERR_DEVICE 5       /* device is not sm_100                    */
+
+/* Bit of the workspace status word: a scaled value of X left fp16's range. */
+#define FGMM_STATUS_RANGE 0x10000
 
 #define FGMM_VARIANT_ISO 0
 #define FGMM_VARIANT_DIAG 1
