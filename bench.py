@@ -11,6 +11,10 @@ reference's headline shape N=1M, K=1024, D=128.
   global rows [r*1M, (r+1)*1M)), so per-GPU work is fixed as N grows
   ("scaling": "weak").  One step = the E-step on each rank + ONE NCCL
   all-reduce of the packed [Nk | mu_acc | sig_acc] statistics.
+  The same line carries ``c5``: the C5 strong-scaling step (100M rows in
+  total, each rank streaming its shard in 10M-row chunks, then the
+  all-reduce), timed the same way (``--no-c5`` skips it), and
+  ``allreduce_ms_per_step`` (N>1).
 * ``--workload c3`` / ``c4``: the diagonal (N=1M, K=1024, D=96) and full
   covariance (N=250K, K=256, D=64) configurations per rank, from the seeded
   recipes of ``gmm_data`` (weak scaling; the same rows on every rank).
@@ -293,6 +297,8 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="c2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-c5", action="store_true",
+                    help="c2 only: skip the C5 strong-scaling measurement on the same line")
     ap.add_argument("--ref-rows", type=int, default=0,
                     help="reference arm only: rows per step (default: the full workload)")
     args = ap.parse_args()
@@ -350,13 +356,19 @@ def main():
     buf, (Nk, mu_acc, sig) = GS.packed_stats(kind, K, D, dev)
     logZ = torch.empty(n_local, device=dev)
 
-    def step():
+    ar_ev = []   # (start, end) of each timed step's all-reduce
+
+    def step(ar_events=None):
         for s in range(0, n_local, chunk):
             e = min(n_local, s + chunk)
             L.estep(variant, X[s:e], mu, cov, lpi,
                     out=(logZ[s:e], Nk, mu_acc, sig), accumulate=s > 0)
         if world > 1:
+            if ar_events is not None:
+                ar_events[0].record(torch.cuda.current_stream(dev))
             dist.all_reduce(buf)
+            if ar_events is not None:
+                ar_events[1].record(torch.cuda.current_stream(dev))
 
     stream = torch.cuda.current_stream(dev)
     for _ in range(args.warmup):
@@ -396,8 +408,11 @@ def main():
         b.record(stream)  # materialise both events before handing them to the library
         t0.record(stream)
         L.set_profile_events(a, b)
-        step()
+        ar = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+        step(ar if world > 1 else None)
         L.set_profile_events(None, None)
+        if world > 1:
+            ar_ev.append(ar)
         t1.record(stream)
         ev_pairs.append((a, b))
         step_ev.append((t0, t1))
@@ -411,10 +426,11 @@ def main():
     ms_mean = sum(step_ms) / args.steps
     ms_step = statistics.median(step_ms)  # the median of the K timed steps
     kern_avg = statistics.median(kern_ms)
+    ar_ms = statistics.median([x.elapsed_time(y) for x, y in ar_ev]) if ar_ev else 0.0
     if world > 1:
-        t = torch.tensor([ms_step, kern_avg, ms_mean], device=dev)
+        t = torch.tensor([ms_step, kern_avg, ms_mean, ar_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_step, kern_avg, ms_mean = float(t[0]), float(t[1]), float(t[2])
+        ms_step, kern_avg, ms_mean, ar_ms = float(t[0]), float(t[1]), float(t[2]), float(t[3])
 
     pairs_step = n_global * K
     value = pairs_step / (ms_step * 1e-3)
@@ -468,6 +484,55 @@ def main():
                "path": f"pinned host X in {E2E_CHUNK}-row pieces -> device (copy stream, "
                        "overlapped) -> gmm_stream.stream_estep (the library E-step per piece, "
                        "statistics accumulated) -> logZ and statistics -> host"}
+
+    # ---- C5 strong scaling beside the C2 line: 100M rows in total, this rank's
+    # share streamed through the E-step in 10M-row chunks, then the all-reduce
+    c5 = None
+    if args.workload == "c2" and not args.no_c5:
+        lo5, hi5 = GS.shard_rows(ROWS_C5, rank, world)
+        n5 = hi5 - lo5
+        X5 = torch.empty(n5, D, device=dev, dtype=torch.float32)
+        for s0 in range(0, n5, C5_CHUNK):
+            GS.generate_rows(lo5 + s0, min(C5_CHUNK, n5 - s0), centres, SEED,
+                             out=X5[s0:s0 + C5_CHUNK])
+        logZ5 = torch.empty(n5, device=dev)
+
+        def step5(ar_events=None):
+            for s0 in range(0, n5, C5_CHUNK):
+                e0 = min(n5, s0 + C5_CHUNK)
+                L.estep(variant, X5[s0:e0], mu, cov, lpi,
+                        out=(logZ5[s0:e0], Nk, mu_acc, sig), accumulate=s0 > 0)
+            if world > 1:
+                if ar_events is not None:
+                    ar_events[0].record(stream)
+                dist.all_reduce(buf)
+                if ar_events is not None:
+                    ar_events[1].record(stream)
+
+        step5()
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        c5_ms, c5_ar = [], []
+        for _ in range(3):
+            e5 = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+            e5[0].record(stream)
+            step5((e5[2], e5[3]) if world > 1 else None)
+            e5[1].record(stream)
+            torch.cuda.synchronize(dev)
+            c5_ms.append(e5[0].elapsed_time(e5[1]))
+            c5_ar.append(e5[2].elapsed_time(e5[3]) if world > 1 else 0.0)
+        t5 = torch.tensor([statistics.median(c5_ms), statistics.median(c5_ar)], device=dev)
+        if world > 1:
+            dist.all_reduce(t5, op=dist.ReduceOp.MAX)
+        c5 = {"workload": WORKLOADS["c5"]["title"], "scaling": "strong",
+              "ms_per_step": float(t5[0]), "value": ROWS_C5 * K / (float(t5[0]) * 1e-3),
+              "unit": UNIT, "rows_per_rank": n5, "steps": 3, "warmup": 1,
+              "allreduce_ms": float(t5[1]) if world > 1 else None,
+              "how": "every rank streams its shard of the 100M C2-mixture rows (generated on "
+                     "device, 10M-row chunks, FGMM_FLAG_ACCUMULATE), then one NCCL all-reduce "
+                     "of the packed statistics; CUDA events, median of 3 steps, max over ranks"}
+        del X5, logZ5
 
     # ---- roofline of the dominant kernel
     peaks = load_peaks()
@@ -531,6 +596,8 @@ def main():
                                                              (peaks["bf16_tflops"] / 2 * 1e12),
                                                              t_exp) / (ms_step * 1e-3))},
         "clocks": clocks,
+        "allreduce_ms_per_step": ar_ms if world > 1 else None,
+        "c5": c5,
         "e2e": e2e,
         "gpu_launches": launches,
         "cpu_baseline": cpu,
