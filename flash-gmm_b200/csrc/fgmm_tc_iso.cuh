@@ -14,9 +14,9 @@
 // quadrant of 32 components (one epilogue warp; lane = component):
 //   MMA dist(j):  S[b] = W_lo X_hi + W_hi X_lo + W_hi X_hi   (24 MMAs, N = 128)
 //   A   ll = S 2^(a+s_k) + c0' - ish |x-c|^2 (log2 units) for the block's 32
-//       rows; per row the quadrant's max m (redux.sync.max) and the sum of
-//       p = 2^(ll - m) as a 23-bit fixed-point integer (redux.sync.add.u32,
-//       exact and independent of the order of the lanes);
+//       rows, read in the 16x256b fragment layout (4 components x 8 rows per
+//       thread); per row the quadrant's max m and the fp32 sum of
+//       p = 2^(ll - m) by in-thread max/add plus 3 shuffle rounds;
 //   B   (lane = row; each of the block's four warps) the four quadrants'
 //       pairs (shared memory) -> the CTA's (max, sum) per row, sent to the
 //       cluster's CTAs (st.async; warp q serves peers q and q + 4); every
@@ -33,9 +33,9 @@
 // vote.ballot), so the work follows the number of rows a quadrant takes part
 // in: all of them for overlapping components, about one in 32 when each row
 // belongs to one well separated component.  Up to four selected rows of a
-// block are re-read with single-column TMEM loads issued together; more,
-// with one 32-column load.  The results do not depend on the selection
-// beyond the stated cut-offs.
+// block are re-read with single-column TMEM loads issued together and the
+// block's words written in one pass; more, with one 32-column load.  The
+// results do not depend on the selection beyond the stated cut-offs.
 //
 // Both GEMMs carry 22-bit operands (fp16 hi/lo, exact power-of-two scaling):
 // logZ is held to 1e-5 and the statistics to 1e-4 also where the rows of a
@@ -80,8 +80,8 @@ struct IsoSmem {
   static constexpr int kStageMax = 2 * 2 * kIsoRows * 128;           // 64 KB
   static constexpr int kXs = 0;
   static constexpr int kXsq = kXs + kIsoStages * kStageMax;          // [NS][128] f32
-  // per tile parity, row block, quadrant and row: the quadrant's max (f32)
-  // and its fixed-point sum of 2^(ll - max) (u32, 23 fraction bits)
+  // per tile parity, row block, quadrant and row: the quadrant's max and its
+  // sum of 2^(ll - max) (f32)
   static constexpr int kQMax = kXsq + kIsoStages * kIsoRows * 4;     // [2][4 blk][4 q][32]
   static constexpr int kQSum = kQMax + 2 * 16 * 32 * 4;              // [2][4 blk][4 q][32]
   static constexpr int kFin = kQSum + 2 * 16 * 32 * 4;               // [8][128] f32
@@ -106,7 +106,7 @@ __global__ void __launch_bounds__(kIsoThreads, 1) tc_iso_kernel(const TcParams p
   uint8_t* xs = smem + IsoSmem::kXs;
   float* xsq = reinterpret_cast<float*>(smem + IsoSmem::kXsq);
   float* qmax = reinterpret_cast<float*>(smem + IsoSmem::kQMax);
-  uint32_t* qsum = reinterpret_cast<uint32_t*>(smem + IsoSmem::kQSum);
+  float* qsum = reinterpret_cast<float*>(smem + IsoSmem::kQSum);
   float* fin = reinterpret_cast<float*>(smem + IsoSmem::kFin);
   float2* xchg = reinterpret_cast<float2*>(smem + IsoSmem::kXchg);  // [slot][CTA][row]
   IsoCtl* ctl = reinterpret_cast<IsoCtl*>(smem + IsoSmem::kCtl);
@@ -291,6 +291,20 @@ __global__ void __launch_bounds__(kIsoThreads, 1) tc_iso_kernel(const TcParams p
     const float ish_row = uni ? p.consts[0].y : 0.f;
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
     float nk_acc = 0.f, rll_acc = 0.f;
+    // Phase A reads S in the 16x256b fragment layout: thread t holds the
+    // components (quadrant lanes) t/4 + 8u, u = 0..3, at the block's rows
+    // 8j + 2(t%4) + e, j = 0..3, e = 0..1; their constants:
+    float ac0[4], asck[4], aish[4];
+    if (warp < kIsoEpiWarps) {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float4 c4 = p.consts[(int)rank * kComps + q * 32 + (lane >> 2) + 8 * u];
+        ac0[u] = c4.x;
+        aish[u] = c4.y;
+        asck[u] = ldexpf(1.0f, xa + (int)c4.w);
+      }
+    }
+    const int rsub = 2 * (lane & 3);  // this thread's rows: 8j + rsub + e
     // Expanded-form accuracy: the distance comes out of an fp32 tensor-core
     // accumulation whose error grows with ish |x - c| |mu_k - c| (up to ~14
     // units of 2^-23 of it, measured), while logZ is held to 1e-5 of |logZ|.
@@ -313,43 +327,64 @@ __global__ void __launch_bounds__(kIsoThreads, 1) tc_iso_kernel(const TcParams p
       const uint32_t scol = tmem + lane_base + kIsoColS + 128u * (uint32_t)b + 32u * (uint32_t)cb;
       const float* xq = xsq + st * kIsoRows + 32 * cb;
       float* qm = qmax + (slot * 4 + cb) * 128;     // [4 q][32 rows] of this row block
-      uint32_t* qs = qsum + (slot * 4 + cb) * 128;
+      float* qs = qsum + (slot * 4 + cb) * 128;
       if (!iso_wait(&ctl->s_full[b], (j >> 1) & 1, ctl, p.err, 16)) break;
       if (!iso_wait(&ctl->xfull[st], (j / NS) & 1, ctl, p.err, 4096)) break;
       tc_fence_after();
-      // ---- A: per row, the quadrant's max m (redux.sync.max) and the sum of
-      // p = 2^(ll - m) over the quadrant's 32 components: each p in [0, 1] is
-      // rounded to a 23-bit fixed-point integer (p 2^23 + 2^23 leaves it in
-      // the low mantissa bits) and summed exactly by redux.sync.add.u32 (the
-      // 32 copies of 2^23's bits, 0x60000000 mod 2^32, come off when read).
-      // Lane 0 records both per row; the register holding a row's value is
-      // fixed, so no transposition is needed.
+      // ---- A: per row, the quadrant's max m and the sum of p = 2^(ll - m)
+      // over the quadrant's 32 components.  In the 16x256b layout each row's
+      // 32 values sit on the 8 threads sharing t % 4, four per thread: the
+      // max is 3 in-thread max + a 3-step xor butterfly, the sum 3 in-thread
+      // adds + a 3-round transpose-reduce, after which thread t holds the row
+      // 8 (t/8) + 2 (t%4) + (t/4)%2 and records its (max, sum).
       {
-        uint32_t sv[32];
-        tmem_ld32(scol, sv);
+        uint32_t v[32];
+        tmem_ld16x256_x4(scol, v);
+        tmem_ld16x256_x4(scol + (16u << 16), v + 16);
         tmem_wait_ld();
+        float mr[8], sr[8];
 #pragma unroll
-        for (int i = 0; i < 32; i += 4) {
-          float xv[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int jj = 0; jj < 4; ++jj) {
+          float xv[2] = {0.f, 0.f};
           if (!uni) {
-            const float4 s4 = *reinterpret_cast<const float4*>(xq + i);
-            xv[0] = s4.x; xv[1] = s4.y; xv[2] = s4.z; xv[3] = s4.w;
+            const float2 x2 = *reinterpret_cast<const float2*>(xq + 8 * jj + rsub);
+            xv[0] = x2.x;
+            xv[1] = x2.y;
           }
-          float mv[4];
-          uint32_t uv[4];
 #pragma unroll
-          for (int t = 0; t < 4; ++t) {
-            const float base = uni ? c0p : fmaf(-ish, xv[t], c0p);
-            const float ll = fmaf(__uint_as_float(sv[i + t]), sck, base);
-            mv[t] = redux_max(ll);
-            const float pe = ex2(ll - mv[t]);
-            uv[t] = redux_add_u32(__float_as_uint(fmaf(pe, 8388608.f, 8388608.f)));
-          }
-          if (lane == 0) {
-            *reinterpret_cast<float4*>(qm + q * 32 + i) = make_float4(mv[0], mv[1], mv[2], mv[3]);
-            *reinterpret_cast<uint4*>(qs + q * 32 + i) = make_uint4(uv[0], uv[1], uv[2], uv[3]);
+          for (int e = 0; e < 2; ++e) {
+            float ll[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const float base = uni ? ac0[u] : fmaf(-aish[u], xv[e], ac0[u]);
+              ll[u] = fmaf(__uint_as_float(v[16 * (u >> 1) + 4 * jj + 2 * (u & 1) + e]), asck[u],
+                           base);
+            }
+            float m = fmaxf(fmaxf(ll[0], ll[1]), fmaxf(ll[2], ll[3]));
+            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 8));
+            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 16));
+            mr[2 * jj + e] = m;
+            sr[2 * jj + e] = (ex2(ll[0] - m) + ex2(ll[1] - m)) + (ex2(ll[2] - m) + ex2(ll[3] - m));
           }
         }
+        // transpose-reduce of the 8 row sums over lane bits 4, 3, 2 (row-index
+        // bits 2, 1, 0); the max (equal on the 8 threads) is selected alongside
+#pragma unroll
+        for (int h = 4, msk = 16; h >= 1; h >>= 1, msk >>= 1) {
+          const bool up = (lane & msk) != 0;
+#pragma unroll
+          for (int i = 0; i < h; ++i) {
+            const float send = up ? sr[i] : sr[i + h];
+            const float keep = up ? sr[i + h] : sr[i];
+            sr[i] = keep + __shfl_xor_sync(0xffffffffu, send, msk);
+            mr[i] = up ? mr[i + h] : mr[i];
+          }
+        }
+        const int ri = (lane >> 2) & 7;  // row index 2j + e held now
+        const int row = 8 * (ri >> 1) + rsub + (ri & 1);
+        qm[q * 32 + row] = mr[0];
+        qs[q * 32 + row] = sr[0];
       }
       if (!sync_block(0, j, 256)) break;
       // ---- B (lane = row of the block; each of the block's four warps does
@@ -362,7 +397,7 @@ __global__ void __launch_bounds__(kIsoThreads, 1) tc_iso_kernel(const TcParams p
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
           mqq[u] = qm[u * 32 + lane];
-          sqq[u] = (float)(qs[u * 32 + lane] - 0x60000000u) * 1.1920928955078125e-7f;  // 2^-23
+          sqq[u] = qs[u * 32 + lane];
         }
         mq = q == 0 ? mqq[0] : q == 1 ? mqq[1] : q == 2 ? mqq[2] : mqq[3];
         const float M = fmaxf(fmaxf(mqq[0], mqq[1]), fmaxf(mqq[2], mqq[3]));
@@ -470,19 +505,18 @@ __global__ void __launch_bounds__(kIsoThreads, 1) tc_iso_kernel(const TcParams p
                 ((need >> (i + 1)) & 1u) ? resp(i + 1, __uint_as_float(v[2 * u + 1])) : 0.f;
             split2(r0, r1, h[u], l[u]);
           }
-          const uint32_t z = 0u;
-          const uint32_t zv[16] = {z, z, z, z, z, z, z, z, z, z, z, z, z, z, z, z};
-          tmem_st16(scol, zv);
-          tmem_st16(scol + 16, zv);
-          if (pairs) {
-            tmem_wait_st();  // the zeros land before the words that replace them
+          // the block's 16 hi and 16 lo words in one pass: the (at most two)
+          // computed column pairs, zeros elsewhere
+          const int c0 = i0[0] >= 0 ? (i0[0] >> 1) : -1;
+          const int c1 = i0[1] >= 0 ? (i0[1] >> 1) : -1;
+          uint32_t hv[16], lv[16];
 #pragma unroll
-            for (int u = 0; u < 2; ++u) {
-              if (i0[u] < 0) continue;
-              tmem_st1(scol + (uint32_t)(i0[u] >> 1), h[u]);
-              tmem_st1(scol + 16u + (uint32_t)(i0[u] >> 1), l[u]);
-            }
+          for (int c = 0; c < 16; ++c) {
+            hv[c] = c == c0 ? h[0] : (c == c1 ? h[1] : 0u);
+            lv[c] = c == c0 ? l[0] : (c == c1 ? l[1] : 0u);
           }
+          tmem_st16(scol, hv);
+          tmem_st16(scol + 16, lv);
         } else {
           uint32_t sv[32];
           tmem_ld32(scol, sv);
