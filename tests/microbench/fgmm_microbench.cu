@@ -289,7 +289,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(128, 1)
 // Issue-rate kernel: every thread runs `iters` rounds of 8 independent
 // operations of kind `op` (0 ex2.approx.ftz.f32, 1 ex2.approx.f16x2,
 // 2 fma.rn.f32, 3 two ex2.f32 and six FFMA, 4 redux.sync.add.u32,
-// 5 redux.sync.max.f32, 6 shfl.sync.bfly).  out[cta] = cycles.
+// 5 redux.sync.max.f32, 6 shfl.sync.bfly, 7 ex2.approx.ftz.f32 predicated
+// on for lane 0 of each warp only, 8 the same predicated off on every lane).
+// out[cta] = cycles.
 __global__ void __launch_bounds__(1024, 1) issue_rate_kernel(int iters, int op, long long* out,
                                                              float* sink) {
   float v[8];
@@ -323,6 +325,14 @@ __global__ void __launch_bounds__(1024, 1) issue_rate_kernel(int iters, int op, 
 #pragma unroll
       for (int i = 0; i < 8; ++i)
         asm volatile("redux.sync.max.f32 %0, %0, 0xffffffff;" : "+f"(v[i]));
+  } else if (op == 7 || op == 8) {
+    const uint32_t on = op == 7 ? ((threadIdx.x & 31) == 0 ? 1u : 0u) : 0u;
+    for (int it = 0; it < iters; ++it)
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.u32 p, %1, 0;\n\t@p ex2.approx.ftz.f32 %0, %0;\n\t}"
+                     : "+f"(v[i])
+                     : "r"(on));
   } else if (op == 6) {
     for (int it = 0; it < iters; ++it)
 #pragma unroll

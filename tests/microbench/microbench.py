@@ -95,7 +95,8 @@ def mma_rate_2cta(lib, N, pairs=1, iters=4096):
 
 OPS = {0: "ex2.approx.ftz.f32", 1: "ex2.approx.f16x2", 2: "fma.rn.f32",
        3: "2 ex2.f32 + 6 fma.f32", 4: "redux.sync.add.u32", 5: "redux.sync.max.f32",
-       6: "shfl.sync.bfly.b32"}
+       6: "shfl.sync.bfly.b32", 7: "ex2.approx.ftz.f32, 1 lane of 32 active",
+       8: "ex2.approx.ftz.f32, predicated off"}
 
 
 def issue_rate(lib, op, ctas=148, threads=1024, iters=2048):
@@ -159,7 +160,7 @@ def run_all(quick: bool = False):
         rows.append(mma_rate_2cta(lib, N))
     if not quick:
         rows.append(mma_rate_2cta(lib, 256, pairs=74))
-    for op in (0, 1, 2, 3, 4, 5, 6):
+    for op in (0, 1, 2, 3, 4, 5, 6, 7, 8):
         rows.append(issue_rate(lib, op, ctas=148 if not quick else 8))
     clusters = {}
     for smem in (100 * 1024, 200 * 1024):
