@@ -863,7 +863,8 @@ template <class G, class TX>
 __global__ void __launch_bounds__(256) tc_split_kernel(
     const TX* __restrict__ X, int64_t sxn, int64_t sxd, int vec_ok, int64_t N, int D, int Dp,
     int nch, int64_t rows_pad, const int* __restrict__ amax, const float* __restrict__ cvec,
-    uint8_t* __restrict__ xsplit, float* __restrict__ xsq, int* __restrict__ err) {
+    uint8_t* __restrict__ xsplit, float* __restrict__ xsq, int* __restrict__ err,
+    unsigned long long* __restrict__ corr = nullptr) {
   constexpr int ROWS = G::kRows, NV = G::kNV;
   constexpr bool DIAG = G::kDiag;
   constexpr int kChunk = ROWS * 128;
@@ -954,7 +955,10 @@ __global__ void __launch_bounds__(256) tc_split_kernel(
       if (!DIAG) {
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
-        if (lane == 0) xsq[row] = sq;
+        if (lane == 0) {
+          xsq[row] = sq;
+          if (corr != nullptr && row < N) corr[row] = 0ull;  // logZ refinement sums start at 0
+        }
       }
     }
   }
@@ -1102,13 +1106,16 @@ __global__ void __launch_bounds__(256) tc_refine_iso_kernel(
   }
 }
 
-// logZ += ln(1 + corr 2^-40) for rows with a correction.
+// logZ += ln(1 + corr 2^-40) for the rows of the listed pairs: the first
+// pair of a row to take its sum (atomicExch to 0) applies it, once.
 __global__ void __launch_bounds__(256) tc_apply_refine_kernel(
-    const unsigned long long* __restrict__ corr, int64_t N, float* __restrict__ logZ) {
-  for (int64_t n = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; n < N;
-       n += (int64_t)gridDim.x * blockDim.x) {
-    const long long v = (long long)corr[n];
-    if (v != 0) logZ[n] += (float)log1p((double)v / kCorrScale);
+    const int4* __restrict__ pairs, const int* __restrict__ count, int cap,
+    unsigned long long* __restrict__ corr, float* __restrict__ logZ) {
+  const int n = min(*count, cap);
+  for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < n; e += gridDim.x * blockDim.x) {
+    const int row = pairs[e].x;
+    const long long v = (long long)atomicExch(corr + row, 0ull);
+    if (v != 0) logZ[row] += (float)log1p((double)v / kCorrScale);
   }
 }
 
@@ -1642,9 +1649,7 @@ cudaError_t tc_estep(int variant, const EstepArgs& a) {
   // err[3]: pairs listed for the logZ refinement (tc_iso_kernel)
   e = cudaMemsetAsync(err, 0, 4 * sizeof(int), hi);
   if (e != cudaSuccess) return e;
-  if (refine_on && (e = cudaMemsetAsync(corr, 0, (size_t)a.N * sizeof(*corr), hi)) !=
-                       cudaSuccess)
-    return e;
+
   int launches = 0;
   launch_centre(a, pl.Dp, cvec, err + 1, hi);
   if (nchunks > 1) {  // the split passes need c and max|mu - c| only: they overlap the prep
@@ -1678,7 +1683,7 @@ cudaError_t tc_estep(int variant, const EstepArgs& a) {
         const TX* Xc = a.x<TX>() + row0 * a.sxn;
         tc_split_kernel<decltype(g), TX><<<sblocks, 256, 0, lo>>>(
             Xc, a.sxn, a.sxd, vec_ok, rows, a.D, pl.Dp, pl.nch, rows_pad, err + 1, cvec, xs_c,
-            xsq_c, err);
+            xsq_c, err, refine_on ? corr + row0 : nullptr);
         return 0;
       });
     });
@@ -1771,8 +1776,7 @@ cudaError_t tc_estep(int variant, const EstepArgs& a) {
                                                          consts, corr);
       return 0;
     });
-    tc_apply_refine_kernel<<<(int)std::min<int64_t>((a.N + 255) / 256, 8 * kSms), 256, 0, hi>>>(
-        corr, a.N, a.logZ);
+    tc_apply_refine_kernel<<<kSms, 256, 0, hi>>>(refine, err + 3, p.refine_cap, corr, a.logZ);
     launches += 2;
   }
   count_launches(launches);
