@@ -81,12 +81,6 @@ __device__ __forceinline__ void st_async_f2(uint32_t addr, float a, float b, uin
       "f"(a), "f"(b), "r"(bar)
       : "memory");
 }
-__device__ __forceinline__ void st_async_f1(uint32_t addr, float a, uint32_t bar) {
-  asm volatile(
-      "st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(addr),
-      "r"(__float_as_uint(a)), "r"(bar)
-      : "memory");
-}
 // Bulk copy global -> this CTA's shared memory, completing `bytes` on `bar`.
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes,
                                          uint64_t* bar) {
@@ -223,12 +217,6 @@ __device__ __forceinline__ uint32_t tmem_ld1(uint32_t taddr) {
 }
 __device__ __forceinline__ void tmem_st1(uint32_t taddr, uint32_t v) {
   asm volatile("tcgen05.st.sync.aligned.32x32b.x1.b32 [%0], {%1};" ::"r"(taddr), "r"(v) : "memory");
-}
-// Sum of a 32-bit integer over the warp (mod 2^32), returned to every lane.
-__device__ __forceinline__ uint32_t redux_add_u32(uint32_t v) {
-  uint32_t r;
-  asm("redux.sync.add.u32 %0, %1, 0xffffffff;" : "=r"(r) : "r"(v));
-  return r;
 }
 __device__ __forceinline__ void tmem_wait_st() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");

@@ -69,7 +69,7 @@ struct __align__(8) IsoCtl {
   uint64_t r_full[2];
   uint64_t t_done;
   uint64_t xchg_full[2][4];  // [tile parity][row block]
-  uint64_t e_bar[2][4];      // [sync point][row block]: one arrival per quadrant warp
+  uint64_t e_bar[4];         // [row block]: phase A done, one arrival per quadrant warp
   uint64_t e_end;
   uint32_t tmem_base;
   volatile int abort_flag;
@@ -130,8 +130,7 @@ __global__ void __launch_bounds__(kIsoThreads, 1) tc_iso_kernel(const TcParams p
     for (int cb = 0; cb < 4; ++cb) {
       mbar_init(&ctl->xchg_full[0][cb], 1);  // local arrive.expect_tx + peers' st.async bytes
       mbar_init(&ctl->xchg_full[1][cb], 1);
-      mbar_init(&ctl->e_bar[0][cb], 4);
-      mbar_init(&ctl->e_bar[1][cb], 4);
+      mbar_init(&ctl->e_bar[cb], 4);
     }
     mbar_init(&ctl->e_end, kIsoEpiWarps);
     ctl->abort_flag = 0;
@@ -314,10 +313,10 @@ __global__ void __launch_bounds__(kIsoThreads, 1) tc_iso_kernel(const TcParams p
     const float mck = (p.refine != nullptr && warp < kIsoEpiWarps) ? p.mc[kg] : 0.f;
     const float cmax = redux_max(ish * mck) * 3.814697265625e-06f;  // ish, mck >= 0
     const float cgate = cmax * cmax;
-    auto sync_block = [&](int e, int j, int code) -> bool {
+    auto sync_block = [&](int j, int code) -> bool {
       __syncwarp();
-      if (lane == 0) mbar_arrive(&ctl->e_bar[e][cb]);
-      return iso_wait(&ctl->e_bar[e][cb], j & 1, ctl, p.err, code);
+      if (lane == 0) mbar_arrive(&ctl->e_bar[cb]);
+      return iso_wait(&ctl->e_bar[cb], j & 1, ctl, p.err, code);
     };
     // peers' pair slots for this lane's row and the barrier words, per slot
     const int xrow = 32 * cb + lane;
@@ -386,7 +385,7 @@ __global__ void __launch_bounds__(kIsoThreads, 1) tc_iso_kernel(const TcParams p
         qm[q * 32 + row] = mr[0];
         qs[q * 32 + row] = sr[0];
       }
-      if (!sync_block(0, j, 256)) break;
+      if (!sync_block(j, 256)) break;
       // ---- B (lane = row of the block; each of the block's four warps does
       // this for all 32 rows, so no second block-wide sync is needed): the
       // CTA's (max, sum) from the four quadrants, sent to peers q and q + 4;
