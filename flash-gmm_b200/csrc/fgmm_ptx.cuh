@@ -137,6 +137,19 @@ __device__ __forceinline__ void mma_ts2(uint32_t d_tmem, uint32_t a_tmem, uint32
       "r"(a_tmem), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// mma_ss with both descriptors given by their low words and one shared high
+// word (both K-major, or both with the same swizzle, SBO and version bits).
+__device__ __forceinline__ void mma_ss2(uint32_t d_tmem, uint32_t a_lo, uint32_t b_lo,
+                                        uint32_t d_hi, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b64 ad, bd;\n\t"
+      "setp.ne.b32 p, %5, 0;\n\t"
+      "mov.b64 ad, {%1, %3};\n\t"
+      "mov.b64 bd, {%2, %3};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], ad, bd, %4, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_lo), "r"(b_lo), "r"(d_hi), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 // True on exactly one active lane of the warp (all 32 lanes must call it).
 __device__ __forceinline__ bool elect_one() {
   uint32_t pred;

@@ -457,17 +457,25 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fused_kernel(const TcParams p)
       const int ksd = p.nfeat / 16;
       const uint32_t lo_off = (uint32_t)G::lo_offset(p.nch);
       bool first_stats = true;
+      // Descriptors are formed once per stage as their low words and advanced
+      // by constant offsets (>> 4), in fully unrolled loops: the issuing lane
+      // shares its sub-partition with epilogue warps, and a per-MMA
+      // descriptor computation left the tensor pipe idle between MMAs.
+      const uint32_t xs0 = smem_u32(xs), wsm = smem_u32(whs);
       auto issue_stats = [&](int jj) -> void {
-        const uint8_t* st = xs + (jj % NS) * stage_bytes;
-        const uint32_t xhi = smem_u32(st), xlo = xhi + lo_off;
-        // terms lo*hi, hi*lo, then hi*hi (smallest magnitudes first)
+        const uint32_t xhi = xs0 + (uint32_t)((jj % NS) * stage_bytes);
+        const uint32_t dhi = desc_lo_mnmajor(xhi, G::kFStride);
+        const uint32_t dlo = desc_lo_mnmajor(xhi + lo_off, G::kFStride);
+        // terms lo*hi, hi*lo, then hi*hi (smallest magnitudes first); K-step s
+        // = rows 16s..16s+15, 2048 bytes apart
+#pragma unroll
         for (int t = 0; t < 3; ++t) {
-          const uint32_t acol = G::kColR + (t == 0 ? (uint32_t)(R / 2) : 0u);
-          const uint32_t b = t == 1 ? xlo : xhi;
-          for (int s = 0; s < R / 16; ++s) {
-            mma_ts(tmem + G::kColT, tmem + acol + 8 * s, desc_mnmajor(b + s * 2048, G::kFStride),
-                   id_stat, (first_stats && t == 0 && s == 0) ? 0u : 1u);
-          }
+          const uint32_t acol = tmem + G::kColR + (t == 0 ? (uint32_t)(R / 2) : 0u);
+          const uint32_t bd = t == 1 ? dlo : dhi;
+#pragma unroll
+          for (int s = 0; s < R / 16; ++s)
+            mma_ts2(tmem + G::kColT, acol + 8u * (uint32_t)s, bd + (uint32_t)(s * (2048 >> 4)),
+                    kDescHi, id_stat, (first_stats && t == 0 && s == 0) ? 0u : 1u);
         }
         first_stats = false;
         tc_commit(&ctl->r_empty);
@@ -478,27 +486,31 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fused_kernel(const TcParams p)
       for (int j = 0; j < ntiles && ok; ++j) {
         const int b = j % NS;
         if (!mbar_wait(&ctl->xfull[b], (j / NS) & 1, ctl, p.err, 1)) break;
-        const uint8_t* st = xs + b * stage_bytes;
-        const uint32_t xhi = smem_u32(st), xlo = xhi + lo_off;
+        const uint32_t xhi = xs0 + (uint32_t)(b * stage_bytes);
+        const uint32_t dhi = desc_lo_kmajor(xhi), dlo = desc_lo_kmajor(xhi + lo_off);
+        const uint32_t dw = desc_lo_kmajor(wsm);
         if constexpr (G::kStack) {
           if (j >= 1 && !mbar_wait(&ctl->s_empty, (j - 1) & 1, ctl, p.err, 2)) break;
           tc_fence_after();
           // per K-step: W_hi [F_hi; F_lo] (N = 2R: columns [hh | hl]), then
           // W_lo F_hi (N = R) into the hh columns
-          const uint32_t wsm = smem_u32(whs);
-          for (int s = 0; s < ksd; ++s) {
-            const uint32_t fa = xhi + (s >> 2) * G::kFStride + (s & 3) * 32;
-            const uint32_t wa = wsm + (s >> 2) * (kComps * 128) + (s & 3) * 32;
-            mma_ts(tmem + G::kColS, tmem + G::kColW + 8 * s, desc_kmajor(fa), id_dist2,
-                   s == 0 ? 0u : 1u);
-            mma_ss(tmem + G::kColS, desc_kmajor(wa), desc_kmajor(fa), id_dist, 1u);
+#pragma unroll
+          for (int s = 0; s < G::kMaxFeat / 16; ++s) {
+            if (s < ksd) {
+              const uint32_t fd = dhi + (uint32_t)(((s >> 2) * G::kFStride + (s & 3) * 32) >> 4);
+              const uint32_t wd = dw + (uint32_t)(((s >> 2) * (kComps * 128) + (s & 3) * 32) >> 4);
+              mma_ts2(tmem + G::kColS, tmem + G::kColW + 8u * (uint32_t)s, fd, kDescHi, id_dist2,
+                      s == 0 ? 0u : 1u);
+              mma_ss2(tmem + G::kColS, wd, fd, kDescHi, id_dist, 1u);
+            }
           }
           tc_commit(&ctl->s_full);
         } else {
           // terms W_lo x_hi, W_hi x_lo, W_hi x_hi (smallest magnitudes first),
           // per pass h over K-steps [8h, 8h + 8); W_lo from shared memory in
           // the wide kernel.  Pass (j, h) is s_full / s_empty phase j H + h.
-          const uint32_t wsm = smem_u32(whs);
+          constexpr int kKS = H == 1 ? G::kMaxFeat / 16 : 8;  // K-steps per pass, at most
+          static_assert(kKS <= 8, "distance pass length");
           for (int h = 0; h < H; ++h) {
             const int ph = j * H + h;
             if (ph >= 1 && !mbar_wait(&ctl->s_empty, (ph - 1) & 1, ctl, p.err, 2)) {
@@ -506,21 +518,26 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fused_kernel(const TcParams p)
               break;
             }
             tc_fence_after();
-            const int s0 = H == 1 ? 0 : 8 * h;
-            const int s1 = H == 1 ? ksd : (ksd < 8 * h + 8 ? ksd : 8 * h + 8);
+            const int s0 = 8 * h;
+            const int ns = ksd - s0 < kKS ? ksd - s0 : kKS;
+#pragma unroll
             for (int t = 0; t < 3; ++t) {
-              const uint32_t acol = G::kColW + (t == 0 ? wcols : 0u);
-              const uint32_t bb = t == 1 ? xlo : xhi;
-              for (int s = s0; s < s1; ++s) {
-                const uint32_t baddr = bb + (s >> 2) * G::kChunk + (s & 3) * 32;
-                const uint32_t acc = (t == 0 && s == s0) ? 0u : 1u;
-                if (G::kWloSmem && t == 0)
-                  mma_ss(tmem + G::kColS,
-                         desc_kmajor(wsm + (s >> 2) * (kComps * 128) + (s & 3) * 32),
-                         desc_kmajor(baddr), id_dist, acc);
-                else
-                  mma_ts(tmem + G::kColS, tmem + acol + 8 * s, desc_kmajor(baddr), id_dist,
-                         acc);
+              const uint32_t acol = tmem + G::kColW + (t == 0 ? wcols : 0u);
+              const uint32_t bd = t == 1 ? dlo : dhi;
+#pragma unroll
+              for (int i = 0; i < kKS; ++i) {
+                if (i < ns) {
+                  const int s = s0 + i;
+                  const uint32_t off = (uint32_t)(((s >> 2) * G::kChunk + (s & 3) * 32) >> 4);
+                  const uint32_t acc = (t == 0 && i == 0) ? 0u : 1u;
+                  if (G::kWloSmem && t == 0)
+                    mma_ss2(tmem + G::kColS,
+                            dw + (uint32_t)(((s >> 2) * (kComps * 128) + (s & 3) * 32) >> 4),
+                            bd + off, kDescHi, id_dist, acc);
+                  else
+                    mma_ts2(tmem + G::kColS, acol + 8u * (uint32_t)s, bd + off, kDescHi, id_dist,
+                            acc);
+                }
               }
             }
             tc_commit(&ctl->s_full);
