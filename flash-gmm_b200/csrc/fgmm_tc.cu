@@ -460,7 +460,10 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fused_kernel(const TcParams p)
       // Descriptors are formed once per stage as their low words and advanced
       // by constant offsets (>> 4), in fully unrolled loops: the issuing lane
       // shares its sub-partition with epilogue warps, and a per-MMA
-      // descriptor computation left the tensor pipe idle between MMAs.
+      // descriptor computation left the tensor pipe idle between MMAs.  A
+      // pass over all K-steps is issued straight-line; shorter ones (fewer
+      // features) by a plain loop: an unrolled loop with a guard per MMA
+      // issued slower than either.
       const uint32_t xs0 = smem_u32(xs), wsm = smem_u32(whs);
       auto issue_stats = [&](int jj) -> void {
         const uint32_t xhi = xs0 + (uint32_t)((jj % NS) * stage_bytes);
@@ -494,15 +497,18 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fused_kernel(const TcParams p)
           tc_fence_after();
           // per K-step: W_hi [F_hi; F_lo] (N = 2R: columns [hh | hl]), then
           // W_lo F_hi (N = R) into the hh columns
+          auto stack_mma = [&](int s) {
+            const uint32_t fd = dhi + (uint32_t)(((s >> 2) * G::kFStride + (s & 3) * 32) >> 4);
+            const uint32_t wd = dw + (uint32_t)(((s >> 2) * (kComps * 128) + (s & 3) * 32) >> 4);
+            mma_ts2(tmem + G::kColS, tmem + G::kColW + 8u * (uint32_t)s, fd, kDescHi, id_dist2,
+                    s == 0 ? 0u : 1u);
+            mma_ss2(tmem + G::kColS, wd, fd, kDescHi, id_dist, 1u);
+          };
+          if (ksd == G::kMaxFeat / 16) {  // all features: straight-line issue
 #pragma unroll
-          for (int s = 0; s < G::kMaxFeat / 16; ++s) {
-            if (s < ksd) {
-              const uint32_t fd = dhi + (uint32_t)(((s >> 2) * G::kFStride + (s & 3) * 32) >> 4);
-              const uint32_t wd = dw + (uint32_t)(((s >> 2) * (kComps * 128) + (s & 3) * 32) >> 4);
-              mma_ts2(tmem + G::kColS, tmem + G::kColW + 8u * (uint32_t)s, fd, kDescHi, id_dist2,
-                      s == 0 ? 0u : 1u);
-              mma_ss2(tmem + G::kColS, wd, fd, kDescHi, id_dist, 1u);
-            }
+            for (int s = 0; s < G::kMaxFeat / 16; ++s) stack_mma(s);
+          } else {
+            for (int s = 0; s < ksd; ++s) stack_mma(s);
           }
           tc_commit(&ctl->s_full);
         } else {
@@ -520,25 +526,25 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fused_kernel(const TcParams p)
             tc_fence_after();
             const int s0 = 8 * h;
             const int ns = ksd - s0 < kKS ? ksd - s0 : kKS;
-#pragma unroll
-            for (int t = 0; t < 3; ++t) {
-              const uint32_t acol = tmem + G::kColW + (t == 0 ? wcols : 0u);
+            auto dist_mma = [&](int t, int s, uint32_t acc) {
               const uint32_t bd = t == 1 ? dlo : dhi;
+              const uint32_t off = (uint32_t)(((s >> 2) * G::kChunk + (s & 3) * 32) >> 4);
+              if (G::kWloSmem && t == 0)
+                mma_ss2(tmem + G::kColS,
+                        dw + (uint32_t)(((s >> 2) * (kComps * 128) + (s & 3) * 32) >> 4),
+                        bd + off, kDescHi, id_dist, acc);
+              else
+                mma_ts2(tmem + G::kColS, tmem + G::kColW + (t == 0 ? wcols : 0u) + 8u * (uint32_t)s,
+                        bd + off, kDescHi, id_dist, acc);
+            };
+            if (ns == kKS) {  // a full pass: straight-line issue
 #pragma unroll
-              for (int i = 0; i < kKS; ++i) {
-                if (i < ns) {
-                  const int s = s0 + i;
-                  const uint32_t off = (uint32_t)(((s >> 2) * G::kChunk + (s & 3) * 32) >> 4);
-                  const uint32_t acc = (t == 0 && i == 0) ? 0u : 1u;
-                  if (G::kWloSmem && t == 0)
-                    mma_ss2(tmem + G::kColS,
-                            dw + (uint32_t)(((s >> 2) * (kComps * 128) + (s & 3) * 32) >> 4),
-                            bd + off, kDescHi, id_dist, acc);
-                  else
-                    mma_ts2(tmem + G::kColS, acol + 8u * (uint32_t)s, bd + off, kDescHi, id_dist,
-                            acc);
-                }
-              }
+              for (int t = 0; t < 3; ++t)
+#pragma unroll
+                for (int i = 0; i < kKS; ++i) dist_mma(t, s0 + i, (t == 0 && i == 0) ? 0u : 1u);
+            } else {
+              for (int t = 0; t < 3; ++t)
+                for (int i = 0; i < ns; ++i) dist_mma(t, s0 + i, (t == 0 && i == 0) ? 0u : 1u);
             }
             tc_commit(&ctl->s_full);
           }
