@@ -354,15 +354,35 @@ __global__ void __launch_bounds__(kP1Threads, 1) full_ll_kernel(const P1Params p
                 break;
               }
               tc_fence_after();
-              const uint32_t xhi = smem_u32(xs + tt * 2 * kXTile), xlo = xhi + kXTile;
+              const uint32_t xhi = smem_u32(xs + tt * 2 * kXTile);
+              const uint32_t dxh = desc_lo_kmajor(xhi), dxl = desc_lo_kmajor(xhi + kXTile);
+              const uint32_t dlh = desc_lo_kmajor(lhi), dll = desc_lo_kmajor(llo);
+              const uint32_t dacc = tmem + (uint32_t)(acc * 256);
               // terms x_lo*L_hi, x_hi*L_lo, x_hi*L_hi (smallest magnitudes first);
-              // K-steps below jb meet the zero upper triangle of L and are skipped
-              for (int term = 0; term < 3; ++term) {
-                const uint32_t a = term == 0 ? xlo : xhi;
-                const uint32_t b = term == 1 ? llo : lhi;
-                for (int ks = jb; ks < nreg; ++ks)
-                  mma_ss(tmem + acc * 256, desc_kmajor(a + 32 * ks), desc_kmajor(b + 32 * ks),
-                         idesc, (term == 0 && ks == jb) ? 0u : 1u);
+              // K-steps below jb meet the zero upper triangle of L and are skipped.
+              // Descriptor words advance 32 bytes (2 in >> 4 units) per K-step;
+              // each K-step count is issued straight-line.
+              auto p1_mma = [&](int term, int ks, uint32_t accf) {
+                mma_ss2(dacc, (term == 0 ? dxl : dxh) + 2u * (uint32_t)ks,
+                        (term == 1 ? dll : dlh) + 2u * (uint32_t)ks, kDescHi, idesc, accf);
+              };
+              auto tri = [&](auto nkc) {
+                constexpr int NK = decltype(nkc)::value;
+#pragma unroll
+                for (int term = 0; term < 3; ++term)
+#pragma unroll
+                  for (int i = 0; i < NK; ++i)
+                    p1_mma(term, jb + i, (term == 0 && i == 0) ? 0u : 1u);
+              };
+              switch (nreg - jb) {
+                case 4: tri(std::integral_constant<int, 4>{}); break;
+                case 3: tri(std::integral_constant<int, 3>{}); break;
+                case 2: tri(std::integral_constant<int, 2>{}); break;
+                case 1: tri(std::integral_constant<int, 1>{}); break;
+                default:
+                  for (int term = 0; term < 3; ++term)
+                    for (int ks = jb; ks < nreg; ++ks)
+                      p1_mma(term, ks, (term == 0 && ks == jb) ? 0u : 1u);
               }
               tc_commit(&ctl->afull[acc]);
             }
@@ -729,14 +749,20 @@ __global__ void __launch_bounds__(kP2Threads, 1) full_stats_kernel(const P2Param
             !mbar_wait_flag(&ctl->rin_full[b], (c >> 1) & 1, abort_flag, p.err, 4))
           break;
         tc_fence_after();
-        const uint32_t rhi = smem_u32(rst + b * 2 * kRBlock), rlo = rhi + kRBlock;
-        const uint32_t zhi = smem_u32(zst + b * kZStage), zlo = zhi + 4 * kZChunk;
-        for (int term = 0; term < 3; ++term) {  // r_lo*z_hi, r_hi*z_lo, r_hi*z_hi
-          const uint32_t ra = term == 0 ? rlo : rhi;
-          const uint32_t zb = term == 1 ? zlo : zhi;
+        const uint32_t rhi = smem_u32(rst + b * 2 * kRBlock);
+        const uint32_t zhi = smem_u32(zst + b * kZStage);
+        const uint32_t drh = desc_lo_kmajor(rhi), drl = desc_lo_kmajor(rhi + kRBlock);
+        const uint32_t dzh = desc_lo_mnmajor(zhi, kZChunk);
+        const uint32_t dzl = desc_lo_mnmajor(zhi + 4 * kZChunk, kZChunk);
+        // terms r_lo*z_hi, r_hi*z_lo, r_hi*z_hi, straight-line; K-step s: R^T
+        // 32 bytes along the row, z 16 rows = 2048 bytes
+#pragma unroll
+        for (int term = 0; term < 3; ++term) {
+#pragma unroll
           for (int s = 0; s < kP2Rows / 16; ++s)
-            mma_ss(tmem, desc_kmajor(ra + 32 * s), desc_mnmajor(zb + s * 2048, kZChunk), idesc,
-                   (c == 0 && term == 0 && s == 0) ? 0u : 1u);
+            mma_ss2(tmem, (term == 0 ? drl : drh) + 2u * (uint32_t)s,
+                    (term == 1 ? dzl : dzh) + (uint32_t)(s * (2048 >> 4)), kDescHi, idesc,
+                    (c == 0 && term == 0 && s == 0) ? 0u : 1u);
         }
         tc_commit(&ctl->zempty[b]);
         tc_commit(&ctl->rin_empty[b]);
