@@ -424,7 +424,7 @@ def main():
     step_ms = [t0.elapsed_time(t1) for t0, t1 in step_ev]
     kern_ms = [a.elapsed_time(b) for a, b in ev_pairs]
     ms_mean = sum(step_ms) / args.steps
-    ms_step = statistics.median(step_ms)  # the median of the K timed steps (SURVEY M1)
+    ms_step = statistics.median(step_ms)  # the median of the K timed steps
     kern_avg = statistics.median(kern_ms)
     ar_ms = statistics.median([x.elapsed_time(y) for x, y in ar_ev]) if ar_ev else 0.0
     if world > 1:
