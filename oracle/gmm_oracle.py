@@ -177,7 +177,9 @@ def estep_full(X, mu, prec_chol, log_pi, chunk: int = 16384):
         logZ[s:s + chunk] = lz
         Nk += r.sum(axis=0)
         mu_acc += r.T @ xs
-        sig += np.einsum("nk,ni,nj->kij", r, xs, xs, optimize=True)
+        # sum_n r_nk x_ni x_nj as one (K x n) @ (n x D^2) product
+        xx = (xs[:, :, None] * xs[:, None, :]).reshape(len(xs), D * D)
+        sig += (r.T @ xx).reshape(K, D, D)
     return logZ, Nk, mu_acc, sig
 
 
@@ -268,5 +270,7 @@ def estep_full_cpu_fp32(X, mu, prec_chol, log_pi, chunk: int = 16384):
         logZ[s:s + chunk] = lz
         Nk += r.sum(0)
         mu_acc += r.T @ xs
-        sig += torch.einsum("nk,ni,nj->kij", r, xs, xs)
+        # sum_n r_nk x_ni x_nj as one (K x n) @ (n x D^2) product (the
+        # three-operand einsum ran ~14x slower on the host BLAS)
+        sig += (r.T @ (xs[:, :, None] * xs[:, None, :]).reshape(len(xs), D * D)).view(K, D, D)
     return logZ, Nk, mu_acc, sig
