@@ -190,29 +190,39 @@ def estep_full(X, mu, prec_chol, log_pi, chunk: int = 16384):
 # ---------------------------------------------------------------------------
 
 def estep_iso_cpu_fp32(X, mu, log_sigma_sq, log_pi, chunk: int = 65536):
-    """fp32 torch-CPU restatement of flash_gmm.py:84-101 and 151-166."""
+    """fp32 torch-CPU restatement of flash_gmm.py:84-101 and 151-166.
+
+    ll = c_k + x . (mu_k e^{-lss_k}) - 0.5 |x|^2 e^{-lss_k} with
+    c_k = log pi_k - D/2 (log 2pi + lss_k) - 0.5 |mu_k|^2 e^{-lss_k} (the
+    expanded distance of flash_gmm.py:84-93, one matmul and one in-place
+    update per chunk), and sig_k = sum_n r_nk |x_n - mu_k|^2 from the raw
+    moments sum r |x|^2 - 2 mu_k . mu_acc_k + Nk |mu_k|^2, so no N x K
+    matrix other than ll/r is formed."""
     import torch
     N, D = X.shape
     K = mu.shape[0]
     mu = mu.float()
-    inv_s = torch.exp(-log_sigma_sq.float())
-    const = log_pi.float() - 0.5 * D * (LOG_2PI + log_sigma_sq.float())
+    lss = log_sigma_sq.float()
+    inv_s = torch.exp(-lss)
     mu_sq = (mu * mu).sum(1)
+    c = log_pi.float() - 0.5 * D * (LOG_2PI + lss) - 0.5 * mu_sq * inv_s
+    w = mu * inv_s[:, None]
     logZ = torch.empty(N)
     Nk = torch.zeros(K)
     mu_acc = torch.zeros(K, D)
-    sig = torch.zeros(K)
+    rxsq = torch.zeros(K)
     for s in range(0, N, chunk):
         xs = X[s:s + chunk].float()
         x_sq = (xs * xs).sum(1)
-        sq = x_sq[:, None] - 2.0 * (xs @ mu.T) + mu_sq[None, :]
-        ll = const[None, :] - 0.5 * sq * inv_s[None, :]
+        ll = torch.addmm(c[None, :], xs, w.T)
+        ll.addcmul_(x_sq[:, None], inv_s[None, :], value=-0.5)
         lz = torch.logsumexp(ll, dim=1)
-        r = torch.exp(ll - lz[:, None])
+        r = ll.sub_(lz[:, None]).exp_()          # in place: ll is not needed again
         logZ[s:s + chunk] = lz
         Nk += r.sum(0)
         mu_acc += r.T @ xs
-        sig += (r * sq).sum(0)
+        rxsq += r.T @ x_sq
+    sig = rxsq - 2.0 * (mu_acc * mu).sum(1) + Nk * mu_sq
     return logZ, Nk, mu_acc, sig
 
 
@@ -235,9 +245,10 @@ def estep_diag_cpu_fp32(X, mu, log_sigma_sq, log_pi, chunk: int = 65536):
     for s in range(0, N, chunk):
         xs = X[s:s + chunk].float()
         x2 = xs * xs
-        ll = const[None, :] - 0.5 * (x2 @ inv.T) + xs @ w.T
+        ll = torch.addmm(const[None, :], xs, w.T)
+        ll.addmm_(x2, inv.T, alpha=-0.5)
         lz = torch.logsumexp(ll, dim=1)
-        r = torch.exp(ll - lz[:, None])
+        r = ll.sub_(lz[:, None]).exp_()          # in place: ll is not needed again
         logZ[s:s + chunk] = lz
         Nk += r.sum(0)
         mu_acc += r.T @ xs
@@ -266,7 +277,7 @@ def estep_full_cpu_fp32(X, mu, prec_chol, log_pi, chunk: int = 16384):
         v = torch.einsum("nd,kde->nke", xs, L) - b[None]   # (n, K, D)
         ll = c[None, :] - 0.5 * (v * v).sum(2)
         lz = torch.logsumexp(ll, dim=1)
-        r = torch.exp(ll - lz[:, None])
+        r = ll.sub_(lz[:, None]).exp_()
         logZ[s:s + chunk] = lz
         Nk += r.sum(0)
         mu_acc += r.T @ xs
