@@ -568,7 +568,7 @@ def main():
         Xc, muc, covc, lpic = X[:ncpu].cpu(), mu.cpu(), cov.cpu(), lpi.cpu()
         phys, logical = host_cores()
         rate, nrows, secs = cpu_reference_rate(kind, Xc, muc, covc, lpic, budget_s=12.0,
-                                               chunk=16384 if kind != "full" else 4096,
+                                               chunk=65536 if kind != "full" else 4096,
                                                threads=phys)
         cpu = {"value": rate, "unit": UNIT, "cores": phys, "cores_physical": phys,
                "cores_logical": logical, "kind": "port",
