@@ -185,14 +185,16 @@ struct TcParams {
   float* part;               // [clusters][C*128][plen]
   int plen;
   int* err;
-  // isotropic single-pass kernel: (row, component) pairs whose expanded
+  // isotropic kernels (modes 0 and 2): (row, component) pairs whose expanded
   // distance may carry more error than logZ's tolerance allows are appended
-  // here (null: none) for tc_refine_iso_kernel; mc[k] = |mu_k - c|
+  // here (null: none) for tc_refine_iso_kernel; mc[k] = |mu_k - c| for this
+  // launch's components
   const float* mc = nullptr;
-  int4* refine = nullptr;     // {row of the call, component, r bits, ll (log2) bits}
+  int4* refine = nullptr;     // {row of the call, component of the call, r bits, ll (log2) bits}
   int* refine_count = nullptr;
   int refine_cap = 0;
   int row_base = 0;           // first row of this launch within the call
+  int comp_base = 0;          // first component of this launch within the call
 };
 
 struct __align__(8) SmemCtl {
@@ -602,6 +604,18 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fused_kernel(const TcParams p)
     const float sck = ldexpf(1.0f, (G::kDiag ? 0 : xa) + (int)kc.w);  // S = S' 2^(a + s_k)
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
     float nk_acc = 0.f, rll_acc = 0.f;
+    // Isotropic logZ refinement gate: the expanded distance's error grows
+    // with ish |x - c| |mu_k - c|; pairs with r >= 2^-8 where 64 x 2^-23 of
+    // that exceeds logZ's tolerance are listed for tc_refine_iso_kernel (64
+    // units: these kernels sum up to 16 K-steps, in two chains on the wide
+    // one).  gate2() = (64 x 2^-23 ish |mu_k - c|)^2, formed where it is used
+    // from |mu_k - c| loaded once (a load per tile would sit on the
+    // epilogue's latency chain).
+    const float mck = (!G::kDiag && p.refine != nullptr && warp < kEpiWarps) ? p.mc[kg] : 0.f;
+    auto gate2 = [&]() -> float {
+      const float rbk = ish * mck * 7.62939453125e-06f;
+      return rbk * rbk;
+    };
     const int tid_e = threadIdx.x;                 // 0..511
     const int g = lane >> 3;                       // lane group for row work
     const bool row_owner = 8 * warp < R;           // warps that own rows in B / C
@@ -783,6 +797,42 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fused_kernel(const TcParams p)
       // ---- D: r = 2^(ll - logZ2), per-component sums, R^T into TMEM (16 rows at a time)
       const float* sc = scale_s + RB * cb;            // log2 normaliser per row
       float nk_t = 0.f, rll_t = 0.f;
+      if constexpr (!G::kDiag) {
+        if (p.refine != nullptr) {
+          // Rows whose pairs may need the logZ refinement: |x - c|^2 times the
+          // warp's largest gate exceeds the row's tolerance (a warp-uniform
+          // mask; on most data empty).  For those rows each component forms
+          // r = 2^(ll - logZ2) (ll by a select chain, which keeps ll[] in
+          // registers) and lists the pair if r >= 2^-8 and its own gate
+          // passes.  Done before the R^T words are released, while the
+          // stage's |x|^2 and normaliser words are valid.
+          const float rb2 = gate2();
+          const float rbk2max = redux_max(rb2);
+          bool pass = false;
+          if (lane < RB) {
+            const int ro = RB * cb + lane;
+            const float lzv = MODE == 2 ? lzs[b * R + ro] : sc[lane];
+            const float tt = 1e-5f * fmaxf(1.44269504f, fabsf(lzv));
+            pass = row0 + ro < p.N && xsq[b * R + ro] * rbk2max > tt * tt;
+          }
+          for (uint32_t m = __ballot_sync(0xffffffffu, pass); m != 0u; m &= m - 1u) {
+            const int i = __ffs(m) - 1;
+            float lli = ll[0];
+#pragma unroll
+            for (int jj = 1; jj < RB; ++jj) lli = jj == i ? ll[jj] : lli;
+            const int ro = RB * cb + i;  // row within the tile
+            const float lzv = MODE == 2 ? lzs[b * R + ro] : sc[i];
+            const float tt = 1e-5f * fmaxf(1.44269504f, fabsf(lzv));
+            const float r = ex2(lli - lzv);
+            if (r >= 0.00390625f && xsq[b * R + ro] * rb2 > tt * tt) {
+              const int at = atomicAdd(p.refine_count, 1);
+              if (at < p.refine_cap)
+                p.refine[at] = make_int4(p.row_base + (int)(row0 + ro), p.comp_base + kg,
+                                         __float_as_int(r), __float_as_int(lli));
+            }
+          }
+        }
+      }
       if (t >= 1 && !mbar_wait(&ctl->r_empty, (t - 1) & 1, ctl, p.err, 64)) break;
       tc_fence_after();
 #pragma unroll
@@ -1092,8 +1142,9 @@ __global__ void tc_lse_combine_kernel(const float* __restrict__ lse_part, int nb
   }
 }
 
-// Exact refinement of logZ for the (row, component) pairs listed by
-// tc_iso_kernel (isotropic, log2 units): one warp per pair forms
+// Exact refinement of logZ for the (row, component) pairs listed by the
+// isotropic kernels (tc_iso_kernel, and tc_fused_kernel's isotropic
+// configurations in modes 0 and 2; log2 units): one warp per pair forms
 // |x - mu_k|^2 from the inputs with exact differences (lanes over features,
 // a fixed shuffle order), ll = c0_k - ish_k |x - mu_k|^2, and adds
 // r (2^(ll - ll_used) - 1) -- the relative change of the row's sum of
@@ -1360,6 +1411,10 @@ cudaError_t launch_fused(const TcPlan& pl, const TcParams& p, cudaStream_t strea
   return cudaLaunchKernelEx(&cfg, kern, p);
 }
 
+// Room for pairs to refine: two per row on average (a row has at most 256
+// pairs with r >= 2^-8; pairs beyond the room keep the tensor-core value).
+inline int64_t refine_cap(int64_t N) { return std::min<int64_t>(2 * N + 4096, INT32_MAX); }
+
 // K > 1024 (iso / diag): the components run in blocks of 1024 (one 8-CTA
 // cluster each).  Phase 1 launches the fused kernel in LSE-only mode per
 // block, a small kernel combines the blocks' log-sum-exps into logZ, and
@@ -1373,12 +1428,18 @@ struct MbWs {
   float* cvec = nullptr;
   __half* Whi[kMaxBlocks];
   __half* Wlo[kMaxBlocks];
-  float4* consts[kMaxBlocks];
+  float4* consts[kMaxBlocks];  // block b at consts_all + b * kBlockComps
+  float4* consts_all = nullptr;
   float* part[kMaxBlocks];
   uint8_t* xsplit = nullptr;
   float* xsq = nullptr;
   float* lse_part = nullptr;
   float* lz2 = nullptr;
+  // isotropic logZ refinement: |mu_k - c| (by the call's component number),
+  // per-row correction sums and the listed pairs
+  float* mc = nullptr;
+  unsigned long long* corr = nullptr;
+  int4* refine = nullptr;
   int64_t npad = 0;
   size_t bytes = 0;
 };
@@ -1395,16 +1456,24 @@ MbWs carve_mb(void* base, int variant, int64_t N, int K, int D, bool query_devic
   WsCarve w(base);
   m.err = w.take<int>(64);
   m.cvec = w.take<float>(p0.Dp);
+  // the blocks' component constants in one array (Kpad <= kBlockComps per
+  // block), so the logZ refinement indexes them by the call's component
+  m.consts_all = w.take<float4>((size_t)m.nb * kBlockComps);
   for (int b = 0; b < m.nb; ++b) {
     m.Whi[b] = w.take<__half>((size_t)m.pl[b].Kpad * p0.nfeat);
     m.Wlo[b] = w.take<__half>((size_t)m.pl[b].Kpad * p0.nfeat);
-    m.consts[b] = w.take<float4>(m.pl[b].Kpad);
+    m.consts[b] = m.consts_all + (size_t)b * kBlockComps;
     m.part[b] = w.take<float>((size_t)(kSms / m.pl[b].C) * m.pl[b].Kpad * p0.plen);
   }
   m.xsplit = w.take<uint8_t>((size_t)p0.num_tiles * p0.stage_bytes);
   if (!p0.diag) m.xsq = w.take<float>((size_t)p0.num_tiles * p0.rows);
   m.lse_part = w.take<float>((size_t)m.nb * m.npad);
   m.lz2 = w.take<float>((size_t)m.npad);
+  if (!p0.diag) {
+    m.mc = w.take<float>((size_t)m.nb * kBlockComps);
+    m.corr = w.take<unsigned long long>((size_t)N);
+    m.refine = w.take<int4>((size_t)refine_cap(N));
+  }
   m.bytes = w.used + 256;
   return m;
 }
@@ -1413,7 +1482,9 @@ cudaError_t tc_estep_blocks(int variant, const EstepArgs& a) {
   const MbWs m = carve_mb(a.ws, variant, a.N, a.K, a.D, true);
   const TcPlan& p0 = m.pl[0];
   cudaStream_t st = a.stream;
-  cudaError_t e = cudaMemsetAsync(m.err, 0, 2 * sizeof(int), st);
+  // err[3]: pairs listed for the logZ refinement (isotropic)
+  const bool refine_on = !p0.diag && a.N <= INT32_MAX;  // pairs store 32-bit row numbers
+  cudaError_t e = cudaMemsetAsync(m.err, 0, 4 * sizeof(int), st);
   if (e != cudaSuccess) return e;
   int launches = 0;
   // one centre and X scale for all blocks
@@ -1430,7 +1501,7 @@ cudaError_t tc_estep_blocks(int variant, const EstepArgs& a) {
     else
       tc_prep_kernel<<<m.pl[b].Kpad, prep_threads(p0.Dp), 0, st>>>(
           mub, a.smk, a.smd, a.cov + k0, a.lpi + k0, m.cvec, m.Kb[b], a.D, p0.Dp, m.Whi[b],
-          m.Wlo[b], m.consts[b], nullptr);
+          m.Wlo[b], m.consts[b], nullptr, m.mc != nullptr ? m.mc + k0 : nullptr);
     ++launches;
   }
   const int vec_ok = a.x_vec_ok();
@@ -1441,7 +1512,7 @@ cudaError_t tc_estep_blocks(int variant, const EstepArgs& a) {
       using TX = std::remove_const_t<std::remove_pointer_t<decltype(tx)>>;
       tc_split_kernel<decltype(g), TX><<<sblocks, 256, 0, st>>>(
           a.x<TX>(), a.sxn, a.sxd, vec_ok, a.N, a.D, p0.Dp, p0.nch, m.npad, m.err + 1, m.cvec,
-          m.xsplit, m.xsq, m.err);
+          m.xsplit, m.xsq, m.err, refine_on ? m.corr : nullptr);
       return 0;
     });
   });
@@ -1459,6 +1530,11 @@ cudaError_t tc_estep_blocks(int variant, const EstepArgs& a) {
   p.xscale = m.err + 1;
   p.plen = p0.plen;
   p.err = m.err;
+  if (refine_on) {  // pairs are listed by the statistics phase (mode 2)
+    p.refine = m.refine;
+    p.refine_count = m.err + 3;
+    p.refine_cap = (int)refine_cap(a.N);
+  }
   profile_mark(false, st);
   for (int phase = 1; phase <= 2; ++phase) {
     for (int b = 0; b < m.nb; ++b) {
@@ -1467,6 +1543,8 @@ cudaError_t tc_estep_blocks(int variant, const EstepArgs& a) {
       p.Whi = m.Whi[b];
       p.Wlo = m.Wlo[b];
       p.consts = m.consts[b];
+      p.comp_base = b * kBlockComps;
+      if (refine_on) p.mc = m.mc + (size_t)b * kBlockComps;
       p.part = m.part[b];
       p.logZ = phase == 1 ? m.lse_part + (size_t)b * m.npad : m.lz2;  // out / in, log2 units
       const TcPlan& pb = m.pl[b];
@@ -1497,6 +1575,18 @@ cudaError_t tc_estep_blocks(int variant, const EstepArgs& a) {
                                                  a.mu_acc + k0 * a.D, a.sig + k0, accumulate);
     }
     ++launches;
+  }
+  if (refine_on) {
+    with_xtype(a.xtype, [&](auto tx) {
+      using TX = std::remove_const_t<std::remove_pointer_t<decltype(tx)>>;
+      tc_refine_iso_kernel<TX><<<2 * kSms, 256, 0, st>>>(m.refine, m.err + 3, p.refine_cap,
+                                                         a.x<TX>(), a.sxn, a.sxd, a.mu, a.smk,
+                                                         a.smd, a.D, m.consts_all, m.corr);
+      return 0;
+    });
+    tc_apply_refine_kernel<<<kSms, 256, 0, st>>>(m.refine, m.err + 3, p.refine_cap, m.corr,
+                                                 a.logZ);
+    launches += 2;
   }
   count_launches(launches);
   return cudaGetLastError();
@@ -1589,10 +1679,6 @@ bool tc_supported(int variant, const EstepArgs& a, std::string* why) {
   return true;
 }
 
-// Room for pairs to refine: two per row on average (a row has at most 256
-// pairs with r >= 2^-8; pairs beyond the room keep the tensor-core value).
-inline int64_t refine_cap(int64_t N) { return std::min<int64_t>(2 * N + 4096, INT32_MAX); }
-
 size_t tc_workspace_bytes(int variant, int64_t N, int K, int D) {
   if (variant == kFull) return full_tc_workspace_bytes(N, K, D);
   EstepArgs probe{};
@@ -1615,7 +1701,7 @@ size_t tc_workspace_bytes(int variant, int64_t N, int K, int D) {
   w.take<float>((size_t)plan_chunks(pl) * (kSms / pl.C) * pl.Kpad * pl.plen);
   w.take<uint8_t>((size_t)pl.num_tiles * pl.stage_bytes);             // split features
   if (!pl.diag) w.take<float>((size_t)pl.num_tiles * pl.rows);         // |x|^2
-  if (pl.iso) {                                                        // logZ refinement
+  if (!pl.diag) {                                                      // logZ refinement
     w.take<float>(pl.Kpad);
     w.take<unsigned long long>((size_t)N);
     w.take<int4>((size_t)refine_cap(N));
@@ -1646,8 +1732,8 @@ cudaError_t tc_estep(int variant, const EstepArgs& a) {
   float* mc = nullptr;
   unsigned long long* corr = nullptr;
   int4* refine = nullptr;
-  const bool refine_on = pl.iso && a.N <= INT32_MAX;  // pairs store 32-bit row numbers
-  if (pl.iso) {
+  const bool refine_on = !pl.diag && a.N <= INT32_MAX;  // pairs store 32-bit row numbers
+  if (!pl.diag) {
     mc = w.take<float>(pl.Kpad);
     corr = w.take<unsigned long long>((size_t)a.N);
     refine = w.take<int4>((size_t)refine_cap(a.N));
@@ -1669,7 +1755,7 @@ cudaError_t tc_estep(int variant, const EstepArgs& a) {
   // err[0]: device error word, err[1]: max|mu - c| (float bits, for the X
   // scale), written by the centre kernel
   // err[2]: the components' variances differ (isotropic prep)
-  // err[3]: pairs listed for the logZ refinement (tc_iso_kernel)
+  // err[3]: pairs listed for the logZ refinement (isotropic kernels)
   e = cudaMemsetAsync(err, 0, 4 * sizeof(int), hi);
   if (e != cudaSuccess) return e;
 

@@ -53,11 +53,20 @@ def _tight(N, K, D, kind, seed, equal_var=False):
     ("iso", 40000, 256, 64, False),
     ("diag", 65536, 1024, 96, False),   # C3 shape
     ("diag", 40000, 512, 64, False),
-], ids=["iso-c2", "iso-c2-equal-var", "iso-k256", "diag-c3", "diag-k512"])
+    ("iso", 30000, 1024, 256, False),   # wide kernel (64-row tiles, two distance chains)
+    ("iso", 30000, 2048, 128, False),   # one pass on 16-CTA clusters
+    ("iso", 20000, 4096, 64, False),    # blocks of 1024 components, two phases
+    ("diag", 30000, 1024, 128, False),  # wide diagonal
+    ("diag", 20000, 4096, 64, False),   # blocked diagonal
+], ids=["iso-c2", "iso-c2-equal-var", "iso-k256", "diag-c3", "diag-k512", "iso-d256",
+        "iso-k2048", "iso-k4096", "diag-d128", "diag-k4096"])
 def test_tight_clusters_default_path_vs_oracle(kind, N, K, D, equal_var):
     X, mu, lss, lpi = _tight(N, K, D, kind, seed=11 + K + D, equal_var=equal_var)
-    fn = flash_gmm.flash_gmm_estep if kind == "iso" else flash_gmm_diag_h100.flash_gmm_estep_diag
-    out = _np(fn(X.to(DEV), mu.to(DEV), lss.to(DEV), lpi.to(DEV)))
+    args = (X.to(DEV), mu.to(DEV), lss.to(DEV), lpi.to(DEV))
+    if kind == "iso":
+        out = _np(flash_gmm.flash_gmm_estep(*args, BLOCK_D=max(128, D)))
+    else:
+        out = _np(flash_gmm_diag_h100.flash_gmm_estep_diag(*args))
     ref = (O.estep_iso if kind == "iso" else O.estep_diag)(
         X.numpy(), mu.numpy(), lss.numpy(), lpi.numpy())
     assert_parity(out, ref, what=f"tight clusters {kind} N={N} K={K} D={D}")
