@@ -1,10 +1,11 @@
 """fgmm_estep_iso_noalloc: the isotropic E-step with library-owned scratch.
 
 Called through the C ABI with ctypes (the argtypes are set here, as a
-binding of the header would).  Its results must match fgmm_estep_iso (with
-a caller workspace) within the parity tolerances of tests/parity.py on two
-calls in a row, whether this file runs alone in a fresh process or after the
-rest of the suite.  The file name sorts last on purpose.
+binding of the header would).  Its results must match the fp64 oracle and
+fgmm_estep_iso (with a caller workspace) within the parity tolerances of
+tests/parity.py on two calls in a row, whether this file runs alone in a
+fresh process or after the rest of the suite.  The file name sorts last on
+purpose.
 """
 
 import ctypes
@@ -15,6 +16,7 @@ import torch
 
 import _fgmm_lib as L
 import gmm_data
+from oracle import gmm_oracle as O
 from parity import assert_parity
 
 _P, _I64, _I32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32
@@ -97,11 +99,15 @@ def test_noalloc_matches_workspace_entry_on_two_calls(N, K, D, transposed, flags
     X, mu, lss, lpi = _inputs(N, K, D, seed=77 + K, transposed=transposed)
     ref = _host(L.estep(L.FGMM_VARIANT_ISO, X, mu, lss, lpi,
                         force_general=bool(flags & L.FGMM_FLAG_FORCE_GENERAL)))
+    oracle = O.estep_iso(X.cpu().numpy(), mu.cpu().numpy(), lss.cpu().numpy(),
+                         lpi.cpu().numpy())
     for call in range(2):
         out = _fresh(N, K, D)
         rc = _call(f, X, mu, lss, lpi, out, flags)
         assert rc == 0, lib.fgmm_last_error().decode()
-        assert_parity(_host(out), ref, what=f"noalloc call {call + 1} vs fgmm_estep_iso")
+        got = _host(out)
+        assert_parity(got, oracle, what=f"noalloc call {call + 1} vs the oracle")
+        assert_parity(got, ref, what=f"noalloc call {call + 1} vs fgmm_estep_iso")
 
 
 @pytest.mark.gpu
