@@ -1,9 +1,11 @@
 """Build check (CPU, needs nvcc): the fused E-step kernels that carry the
 benchmark shapes keep their epilogue in registers.  A register spill in the
 128-row isotropic kernel cost ~4% of the C2 E-step, so the isotropic
-K <= 1024 kernel (tc_iso_kernel) and the single-pass (MODE 0) instantiations
-of the other 8-CTA-cluster configurations (diagonal, wide) must report no
-spill stores or loads in ptxas's resource usage."""
+K <= 1024 kernel (tc_iso_kernel), the single-pass (MODE 0) instantiations
+of the other 8-CTA-cluster configurations (diagonal, wide), and the two
+phases (MODE 1 and 2) of every configuration on the blocked path for more
+than 2048 components must report no spill stores or loads in ptxas's
+resource usage."""
 
 import os
 import re
@@ -56,3 +58,14 @@ def test_single_pass_fused_kernels_do_not_spill():
             checked["tc_iso_kernel"] = spills
     assert len(checked) == 4, sorted(found)
     assert all(v == (0, 0) for v in checked.values()), checked
+    # the blocked path: MODE 1 (log-sum-exp) and MODE 2 (statistics with the
+    # known normaliser, which also lists pairs for the logZ refinement)
+    blocked = re.compile(r"tc_fused_kernelINS0_3CfgILi(\d+)ELb([01])ELi(\d+)ELi\d+ELb[01]ELb[01]"
+                         r"ELi8EEELi([12])EEEv")
+    phases = {}
+    for name, spills in found.items():
+        m = blocked.search(name)
+        if m:
+            phases[f"rows={m.group(1)} diag={m.group(2)} feat={m.group(3)} mode={m.group(4)}"] = spills
+    assert len(phases) == 8, sorted(found)
+    assert all(v == (0, 0) for v in phases.values()), phases
